@@ -1,0 +1,177 @@
+/*
+ * kvb_cuda.h -- C ABI of the B200 paged decode-attention library (libkvbcuda.so).
+ *
+ * This is the boundary a host binds to. Every entry point is extern "C", takes plain pointers,
+ * sizes and plain structs, returns a status code, and never throws. The text of the last error
+ * of the calling thread is available from kvb_last_error().
+ *
+ * Two levels:
+ *   1. The reference-facing level (kvb_available ... kvb_flush_caches) implements, one for one,
+ *      the functions of kv-cache-bench's C++ host API src/metal_attn.hpp (cited per function).
+ *      kv_cache_bench_b200/csrc/metal_attn_cuda.cpp turns these into the C++ API itself (a
+ *      drop-in for src/metal_attn.mm). Buffers are CUDA managed memory, which the host fills
+ *      in place as it fills the reference's shared-storage MTLBuffers; lengths are checked on the
+ *      host before any device work, and calls are synchronous unless pipelined mode is on.
+ *   2. The stream level (kvb_paged_workspace_bytes, kvb_paged_decode_async) takes device
+ *      pointers and a CUDA stream, reads nothing on the host, allocates nothing and never
+ *      synchronizes. It is what a serving framework or a CUDA graph calls.
+ *
+ * Layouts (src/reference.hpp:38-58, src/metal_attn.hpp:53-69):
+ *   q, out       float [B][H][D]
+ *   k, v pools   [num_blocks][Hkv][page_size][D] of fp32, fp16 or int8
+ *   block_table  int32 [B][max_blocks], -1 for unused entries
+ *   seq_lens     int32 [B]
+ *   k/v scales   float [num_blocks][Hkv] (int8 pools only), value = int8 * scale
+ * Query head h reads KV head h / (H / Hkv). The softmax scale is 1/sqrt(D).
+ */
+#ifndef KVB_CUDA_H
+#define KVB_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. KVB_ERR_INVALID corresponds to the reference's std::invalid_argument (raised
+ * before any device work, outputs untouched), KVB_ERR_DEVICE to its std::runtime_error. */
+enum {
+    KVB_OK = 0,
+    KVB_ERR_INVALID = 1,   /* bad argument; nothing was launched */
+    KVB_ERR_DEVICE = 2,    /* CUDA error (launch, allocation, synchronization) */
+    KVB_ERR_NO_DEVICE = 3, /* no CUDA device */
+    KVB_ERR_STATE = 4      /* call out of order (e.g. end_pipelined without begin) */
+};
+
+/* Storage type of the K/V pools: src/metal_attn.hpp:37 (KvType). */
+enum { KVB_F32 = 0, KVB_F16 = 1, KVB_I8 = 2 };
+
+/* Kernel selection for kvb_paged_args.kernel. AUTO picks the TMA + tensor-core kernel when the
+ * shape allows it (fp16/int8, page size a multiple of 8 dividing or divided by 64, at most 8
+ * query heads per KV head group) and the CUDA-core kernel otherwise. */
+enum { KVB_KERNEL_AUTO = 0, KVB_KERNEL_SIMT = 1, KVB_KERNEL_MMA = 2 };
+
+/* src/reference.hpp:17-23 (Shape). */
+typedef struct kvb_shape {
+    int batch;        /* B */
+    int num_heads;    /* H, query heads */
+    int num_kv_heads; /* Hkv; H % Hkv == 0 */
+    int head_dim;     /* D, 64 or 128 */
+} kvb_shape;
+
+/* src/metal_attn.hpp:53-69 (PagedArgs), field for field, plus the pool size and a kernel choice.
+ * num_blocks is the number of physical blocks in the K and V pools; block ids of live blocks are
+ * checked against it (the reference does not check them at all). */
+typedef struct kvb_paged_args {
+    kvb_shape shape;
+    int kv_type;          /* KVB_F32 / KVB_F16 / KVB_I8 */
+    int page_size;        /* tokens per block, > 0 */
+    int max_blocks;       /* row stride of block_table */
+    int max_len;          /* longest sequence; sizes the split-K workspace. 0: all empty, out = 0 */
+    int part_tokens;      /* split-K partition size; 0 = chosen by the library for B200 */
+    const float* q;
+    const void* k;
+    const void* v;
+    const int32_t* block_table;
+    const int32_t* seq_lens;
+    float* out;
+    int share_kv;         /* 1: one CTA serves every query head of a KV head (GQA); 0: one per query head */
+    const float* k_scale; /* required for KVB_I8 */
+    const float* v_scale;
+    int64_t num_blocks;   /* physical blocks in the pools (> 0 when any sequence is non-empty) */
+    int kernel;           /* KVB_KERNEL_* */
+} kvb_paged_args;
+
+/* src/metal_attn.hpp:71-80 (NaiveArgs): contiguous cache [B][Hkv][max_len][D], fp32 or fp16. */
+typedef struct kvb_naive_args {
+    kvb_shape shape;
+    int kv_type;
+    int max_len;
+    const float* q;
+    const void* k;
+    const void* v;
+    const int32_t* seq_lens;
+    float* out;
+} kvb_naive_args;
+
+/* ---- reference-facing level ----------------------------------------------------------------- */
+
+/* src/metal_attn.hpp:13 metal_available(): 1 if a CUDA device is usable, else 0. */
+int kvb_available(void);
+
+/* src/metal_attn.hpp:14 device_name(): writes the device name (NUL-terminated, truncated to
+ * `len`). */
+int kvb_device_name(char* buf, size_t len);
+
+/* src/metal_attn.hpp:18-33 Buffer(bytes) / ~Buffer(): host-visible, device-usable memory of at
+ * least max(bytes, 16) bytes (CUDA managed memory; the same pointer serves data() and handle()). */
+int kvb_buffer_alloc(size_t bytes, void** ptr);
+int kvb_buffer_free(void* ptr);
+
+/* src/metal_attn.hpp:86 run_paged() and :91 run_paged_steps(): `steps` decode steps, one after
+ * another on the library's stream. Pointers may be managed, pinned-host-mapped or device memory;
+ * seq_lens and block_table are read on the host (copied first when they are device memory) to
+ * refuse a length below 0, above max_len or above max_blocks * page_size, and a live block id
+ * outside [0, num_blocks), with KVB_ERR_INVALID before any device work. *gpu_ms receives the
+ * device time of the steps (CUDA events), or 0 in pipelined mode. */
+int kvb_run_paged(const kvb_paged_args* args, int steps, double* gpu_ms);
+
+/* src/metal_attn.hpp:87 run_naive(): the three-pass baseline (scores, softmax, PV) on the
+ * contiguous cache; fp32 and fp16 only. */
+int kvb_run_naive(const kvb_naive_args* args, double* gpu_ms);
+
+/* src/metal_attn.hpp:98-99 begin_pipelined() / end_pipelined(): between them, kvb_run_* and
+ * kvb_flush_caches enqueue without waiting and run strictly in order; end waits and writes the
+ * device milliseconds of every kvb_run_* call, in order, to ms[0 .. min(*count, cap)), setting
+ * *count to the number of runs. */
+int kvb_begin_pipelined(void);
+int kvb_end_pipelined(double* ms, size_t cap, size_t* count);
+
+/* Number of kvb_run_* calls queued since kvb_begin_pipelined (to size the array for
+ * kvb_end_pipelined). */
+int kvb_pipelined_runs(size_t* count);
+
+/* src/metal_attn.hpp:102 run_read_bandwidth(): streams `bytes` of `src` once with 16-byte loads;
+ * *gpu_ms receives the device time. */
+int kvb_read_bandwidth(const void* src, size_t bytes, double* gpu_ms);
+
+/* src/metal_attn.hpp:106 flush_gpu_caches(): overwrites a scratch buffer of max(256 MiB, 4 x L2)
+ * so the next run starts with a cold L2. */
+int kvb_flush_caches(void);
+
+/* src/metal_attn.hpp:47-51 auto_part_tokens(): the reference's own split-K rule, kept for
+ * callers that print it (largest power of two in [64, 512] giving >= 512 work groups). */
+int kvb_auto_part_tokens(kvb_shape shape, int max_len);
+
+/* Text of the calling thread's last error ("" if none). */
+const char* kvb_last_error(void);
+
+/* ---- stream level (no host reads, no allocation, no synchronization) ------------------------ */
+
+/* The split-K partition size a call with these arguments uses (args->part_tokens, or the B200
+ * rule when it is 0), or a negative status on a bad argument. Depends on shape, max_len, share_kv
+ * and the current device's SM count only. */
+int kvb_paged_part_tokens(const kvb_paged_args* args);
+
+/* Device workspace a kvb_paged_decode_async call with these arguments needs. The workspace must
+ * be zero-filled once before its first use (cudaMemset); every call leaves it ready for the next. */
+int kvb_paged_workspace_bytes(const kvb_paged_args* args, size_t* bytes);
+
+/* src/metal_attn.hpp:86 run_paged() as one stream-ordered launch: all pointers are device
+ * pointers, `stream` is a cudaStream_t (NULL = legacy default stream). Nothing is read on the
+ * host, so lengths cannot be refused up front: a length outside [0, min(max_len,
+ * max_blocks * page_size)] or a live block id outside [0, num_blocks) makes the kernel write NaN
+ * to that sequence's outputs and set a flag that kvb_paged_error_flag() reads; no access leaves
+ * the buffers. Calls that share one workspace must not overlap on the device. */
+int kvb_paged_decode_async(const kvb_paged_args* args, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Reads and clears the error flag of a workspace (synchronizes `stream`). *flag = 0: no bad
+ * length or block id since the last read. */
+int kvb_paged_error_flag(void* workspace, void* stream, int* flag);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVB_CUDA_H */

@@ -1,0 +1,640 @@
+// Host side of the C ABI declared in include/kvb_cuda.h: argument checks, managed buffers, the
+// split-K workspace, tensor-map encoding, kernel choice, timing and pipelined mode.
+//
+// Mirrors the runtime of the reference's Metal host layer (src/metal_attn.mm): argument and length
+// checks before any device work (:199-201, :107-117 check_lens), a grow-only workspace (:98-105),
+// one queue (here one CUDA stream), device time per call (:119-130 finish), pipelined mode
+// (:37-53, :278-293), the read-bandwidth probe (:249-264) and the cache flush (:266-276).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "../../include/kvb_cuda.h"
+#include "kvb_internal.h"
+
+namespace {
+
+thread_local std::string t_err;
+
+int fail(int code, const std::string& msg) {
+    t_err = msg;
+    return code;
+}
+
+#define KVB_CUDA(call)                                                                               \
+    do {                                                                                             \
+        const cudaError_t e_ = (call);                                                               \
+        if (e_ != cudaSuccess) return fail(KVB_ERR_DEVICE, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+size_t elem_size(int t) { return t == KVB_F32 ? 4 : t == KVB_F16 ? 2 : 1; }
+
+// ---- per-device facts ------------------------------------------------------------------------
+
+struct DeviceFacts {
+    int num_sms = 0, l2_bytes = 0;
+};
+
+int device_facts(DeviceFacts* out) {
+    static std::mutex mu;
+    static std::vector<DeviceFacts> cache;
+    int dev = 0;
+    KVB_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
+    if ((int)cache.size() <= dev) cache.resize(dev + 1);
+    DeviceFacts& f = cache[dev];
+    if (!f.num_sms) {
+        KVB_CUDA(cudaDeviceGetAttribute(&f.num_sms, cudaDevAttrMultiProcessorCount, dev));
+        KVB_CUDA(cudaDeviceGetAttribute(&f.l2_bytes, cudaDevAttrL2CacheSize, dev));
+    }
+    *out = f;
+    return KVB_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// ---- geometry of a paged call ------------------------------------------------------------------
+
+struct Geometry {
+    int G, qg, gpk, nhg, part, max_parts;
+};
+
+Geometry geometry(const kvb_paged_args* a, int num_sms) {
+    Geometry g;
+    const kvb_shape& s = a->shape;
+    g.G = s.num_heads / s.num_kv_heads;
+    g.qg = a->share_kv ? std::min(g.G, 8) : 1;
+    g.gpk = (g.G + g.qg - 1) / g.qg;
+    g.nhg = s.num_kv_heads * g.gpk;
+    if (a->part_tokens > 0) {
+        g.part = a->part_tokens;
+    } else {
+        // B200 rule: enough partitions per (sequence, head group) that the units of the longest
+        // sequence fill every CTA slot once (two CTAs per SM), and no partition longer than 2048
+        // tokens (bounded per-unit work for load balance); rounded up to whole 64-token chunks.
+        const long long S = std::max<long long>(1, (long long)s.batch * g.nhg);
+        const long long slots = 2LL * std::max(1, num_sms);
+        const long long n = std::max<long long>({1, (slots + S - 1) / S, ((long long)a->max_len + 2047) / 2048});
+        const long long per = ((long long)a->max_len + n - 1) / n;
+        g.part = (int)std::max<long long>(KVB_CHUNK, (per + KVB_CHUNK - 1) / KVB_CHUNK * KVB_CHUNK);
+    }
+    g.max_parts = std::max(1, (int)(((long long)a->max_len + g.part - 1) / g.part));
+    return g;
+}
+
+// Checks everything that can be checked without reading device data. Messages follow the
+// reference's std::invalid_argument texts where it has one.
+int check_static(const kvb_paged_args* a) {
+    if (!a) return fail(KVB_ERR_INVALID, "null arguments");
+    const kvb_shape& s = a->shape;
+    if (a->part_tokens < 0 || a->max_len < 0 || a->page_size <= 0)
+        return fail(KVB_ERR_INVALID, "part_tokens < 0, max_len < 0 or page_size <= 0");
+    if (a->kv_type < KVB_F32 || a->kv_type > KVB_I8) return fail(KVB_ERR_INVALID, "unknown kv_type");
+    if (a->kv_type == KVB_I8 && (!a->k_scale || !a->v_scale)) return fail(KVB_ERR_INVALID, "i8 cache without scales");
+    if (s.batch < 0 || s.num_heads <= 0 || s.num_kv_heads <= 0) return fail(KVB_ERR_INVALID, "bad shape");
+    if (s.head_dim != 64 && s.head_dim != 128) return fail(KVB_ERR_INVALID, "head_dim must be 64 or 128");
+    if (s.num_heads % s.num_kv_heads != 0) return fail(KVB_ERR_INVALID, "H % Hkv != 0");
+    if (a->max_blocks < 0) return fail(KVB_ERR_INVALID, "max_blocks < 0");
+    if (a->kernel < KVB_KERNEL_AUTO || a->kernel > KVB_KERNEL_MMA) return fail(KVB_ERR_INVALID, "unknown kernel");
+    if (s.batch > 0 && (!a->q || !a->out || !a->seq_lens)) return fail(KVB_ERR_INVALID, "null q, out or seq_lens");
+    if (s.batch > 0 && a->max_len > 0) {
+        if (!a->k || !a->v || !a->block_table) return fail(KVB_ERR_INVALID, "null k, v or block_table");
+        if (a->num_blocks <= 0) return fail(KVB_ERR_INVALID, "num_blocks must be > 0 for a non-empty cache");
+    }
+    if ((long long)s.batch * s.num_heads * s.head_dim > (1LL << 31))
+        return fail(KVB_ERR_INVALID, "q/out larger than 2^31 elements");
+    return KVB_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Encodes the tile map of one pool: rows of D elements, num_blocks * Hkv * page rows, boxes of
+// (128 bytes) x min(page, 64) rows, 128-byte swizzle.
+int encode_pool_map(CUtensorMap* map, const void* pool, const kvb_paged_args* a) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+    if (!enc) return fail(KVB_ERR_DEVICE, "cuTensorMapEncodeTiled is unavailable");
+    const size_t es = elem_size(a->kv_type);
+    const cuuint64_t rows = (cuuint64_t)a->num_blocks * a->shape.num_kv_heads * a->page_size;
+    const cuuint64_t dims[2] = {(cuuint64_t)a->shape.head_dim, rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)a->shape.head_dim * es};
+    const cuuint32_t box[2] = {(cuuint32_t)(128 / es), (cuuint32_t)std::min(a->page_size, KVB_CHUNK)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, a->kv_type == KVB_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                           2, const_cast<void*>(pool), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(KVB_ERR_DEVICE, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    return KVB_OK;
+}
+
+// One decode step on `stream` with workspace `ws` (zeroed once, sized by kvb_paged_workspace_bytes).
+int launch_paged(const kvb_paged_args* a, void* ws, cudaStream_t stream) {
+    DeviceFacts f;
+    if (int rc = device_facts(&f)) return rc;
+    const Geometry g = geometry(a, f.num_sms);
+    const kvb_shape& s = a->shape;
+    if (s.batch == 0) return KVB_OK;
+    const WorkspaceLayout w = kvb_workspace_layout(s.batch, s.num_heads, g.nhg, g.max_parts, s.head_dim);
+    char* wsb = static_cast<char*>(ws);
+
+    DecodeParams p;
+    p.q = a->q;
+    p.k = a->k;
+    p.v = a->v;
+    p.block_table = a->block_table;
+    p.seq_lens = a->seq_lens;
+    p.k_scale = a->k_scale;
+    p.v_scale = a->v_scale;
+    p.out = a->out;
+    p.part_o = reinterpret_cast<float*>(wsb + w.o_off);
+    p.part_ml = reinterpret_cast<float2*>(wsb + w.ml_off);
+    p.counters = reinterpret_cast<unsigned*>(wsb + w.counters_off);
+    p.error_flag = reinterpret_cast<unsigned*>(wsb + w.flag_off);
+    p.B = s.batch;
+    p.H = s.num_heads;
+    p.Hkv = s.num_kv_heads;
+    p.G = g.G;
+    p.qg = g.qg;
+    p.gpk = g.gpk;
+    p.nhg = g.nhg;
+    p.page = a->page_size;
+    p.max_blocks = a->max_blocks;
+    p.max_len = a->max_len;
+    p.part_tokens = g.part;
+    p.max_parts = g.max_parts;
+    p.num_blocks = a->num_blocks;
+    p.q_scale = 1.4426950408889634f / std::sqrt(float(s.head_dim));
+
+    const long long rows = (long long)a->num_blocks * s.num_kv_heads * a->page_size;
+    const bool mma_ok = a->max_len > 0 && kvb_mma_supported(a->kv_type, s.head_dim, a->page_size, g.qg) &&
+                        rows < (1LL << 31) && aligned16(a->k) && aligned16(a->v);
+    if (a->kernel == KVB_KERNEL_MMA && !mma_ok)
+        return fail(KVB_ERR_INVALID, "the tensor-core kernel does not support this shape, page size or dtype");
+    LaunchInfo li{f.num_sms, stream};
+    cudaError_t e;
+    if (mma_ok && a->kernel != KVB_KERNEL_SIMT) {
+        CUtensorMap tk, tv;
+        if (int rc = encode_pool_map(&tk, a->k, a)) return rc;
+        if (int rc = encode_pool_map(&tv, a->v, a)) return rc;
+        e = kvb_launch_decode_mma(p, a->kv_type, s.head_dim, &tk, &tv, li);
+    } else {
+        e = kvb_launch_decode_simt(p, a->kv_type, s.head_dim, li);
+    }
+    if (e != cudaSuccess) return fail(KVB_ERR_DEVICE, std::string("decode launch: ") + cudaGetErrorString(e));
+    return KVB_OK;
+}
+
+// ---- reference-facing state ----------------------------------------------------------------------
+
+struct State {
+    std::mutex mu;
+    bool ready = false;
+    int dev = 0;
+    cudaStream_t stream = nullptr;
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    void* scores = nullptr;
+    size_t scores_bytes = 0;
+    void* flush = nullptr;
+    size_t flush_bytes = 0;
+    float* sink = nullptr;
+    uint32_t flush_value = 0;
+    bool pipelined = false;
+    bool pipeline_checks = false;  // a run in the current pipeline needs its error flag checked
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> timed;
+};
+
+State& st() {
+    static State s;
+    return s;
+}
+
+int ensure_ready(State& S) {
+    if (S.ready) return KVB_OK;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(KVB_ERR_NO_DEVICE, "no CUDA device");
+    }
+    KVB_CUDA(cudaGetDevice(&S.dev));
+    KVB_CUDA(cudaStreamCreateWithFlags(&S.stream, cudaStreamNonBlocking));
+    KVB_CUDA(cudaMalloc(&S.sink, 256 * sizeof(float)));
+    S.ready = true;
+    return KVB_OK;
+}
+
+// Grows a device scratch buffer (contents not kept); zero-filled when `zero`.
+int grow(State& S, void** buf, size_t* have, size_t need, bool zero) {
+    need = std::max<size_t>(need, 256);
+    if (*buf && *have >= need) return KVB_OK;
+    if (*buf) {
+        KVB_CUDA(cudaStreamSynchronize(S.stream));
+        KVB_CUDA(cudaFree(*buf));
+        *buf = nullptr;
+        *have = 0;
+    }
+    KVB_CUDA(cudaMalloc(buf, need));
+    *have = need;
+    if (zero) KVB_CUDA(cudaMemsetAsync(*buf, 0, need, S.stream));
+    return KVB_OK;
+}
+
+enum class Mem { host_only, host_and_device, device_only };
+
+Mem classify(const void* p) {
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return Mem::host_only;
+    }
+    switch (at.type) {
+    case cudaMemoryTypeManaged: return Mem::host_and_device;
+    case cudaMemoryTypeHost: return at.devicePointer ? Mem::host_and_device : Mem::host_only;
+    case cudaMemoryTypeDevice: return Mem::device_only;
+    default: return Mem::host_only;
+    }
+}
+
+// Reads n ints of a buffer the host may or may not be able to address.
+int read_ints(const int32_t* p, size_t n, std::vector<int32_t>* out) {
+    out->resize(n);
+    if (!n) return KVB_OK;
+    if (classify(p) == Mem::device_only) {
+        KVB_CUDA(cudaMemcpy(out->data(), p, n * sizeof(int32_t), cudaMemcpyDeviceToHost));
+    } else {
+        std::memcpy(out->data(), p, n * sizeof(int32_t));
+    }
+    return KVB_OK;
+}
+
+int require_device_accessible(const void* p, const char* what) {
+    if (p && classify(p) == Mem::host_only)
+        return fail(KVB_ERR_INVALID, std::string(what) + " is not device-accessible (use kvb_buffer_alloc)");
+    return KVB_OK;
+}
+
+int prefetch(State& S, const void* p, size_t bytes) {
+    if (!p || !bytes) return KVB_OK;
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess || at.type != cudaMemoryTypeManaged) {
+        cudaGetLastError();
+        return KVB_OK;
+    }
+    KVB_CUDA(cudaMemPrefetchAsync(p, bytes, S.dev, S.stream));
+    return KVB_OK;
+}
+
+int begin_timed(State& S, cudaEvent_t* e0, cudaEvent_t* e1) {
+    KVB_CUDA(cudaEventCreate(e0));
+    KVB_CUDA(cudaEventCreate(e1));
+    KVB_CUDA(cudaEventRecord(*e0, S.stream));
+    return KVB_OK;
+}
+
+int check_flag(State& S) {
+    if (!S.ws) return KVB_OK;
+    unsigned flag = 0;
+    KVB_CUDA(cudaMemcpyAsync(&flag, S.ws, sizeof flag, cudaMemcpyDeviceToHost, S.stream));
+    KVB_CUDA(cudaStreamSynchronize(S.stream));
+    if (!flag) return KVB_OK;
+    KVB_CUDA(cudaMemsetAsync(S.ws, 0, sizeof flag, S.stream));
+    KVB_CUDA(cudaStreamSynchronize(S.stream));
+    return fail(KVB_ERR_DEVICE, "decode kernel reported error flags " + std::to_string(flag));
+}
+
+// Non-pipelined: waits and returns the device time. Pipelined: queues the pair and returns 0.
+int end_timed(State& S, cudaEvent_t e0, cudaEvent_t e1, double* ms, bool check) {
+    KVB_CUDA(cudaEventRecord(e1, S.stream));
+    if (S.pipelined) {
+        S.timed.emplace_back(e0, e1);
+        S.pipeline_checks |= check;
+        if (ms) *ms = 0;
+        return KVB_OK;
+    }
+    const cudaError_t sync = cudaEventSynchronize(e1);
+    float t = 0;
+    if (sync == cudaSuccess) cudaEventElapsedTime(&t, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (sync != cudaSuccess) return fail(KVB_ERR_DEVICE, std::string("device failure: ") + cudaGetErrorString(sync));
+    if (check)
+        if (int rc = check_flag(S)) return rc;
+    if (ms) *ms = t;
+    return KVB_OK;
+}
+
+}  // namespace
+
+// ==================================================================================================
+extern "C" {
+
+int kvb_available(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n > 0 ? 1 : 0;
+}
+
+int kvb_device_name(char* buf, size_t len) {
+    if (!buf || !len) return fail(KVB_ERR_INVALID, "null buffer");
+    buf[0] = 0;
+    if (!kvb_available()) return fail(KVB_ERR_NO_DEVICE, "no CUDA device");
+    int dev = 0;
+    KVB_CUDA(cudaGetDevice(&dev));
+    cudaDeviceProp prop;
+    KVB_CUDA(cudaGetDeviceProperties(&prop, dev));
+    std::strncpy(buf, prop.name, len - 1);
+    buf[len - 1] = 0;
+    return KVB_OK;
+}
+
+int kvb_buffer_alloc(size_t bytes, void** ptr) {
+    if (!ptr) return fail(KVB_ERR_INVALID, "null ptr");
+    *ptr = nullptr;
+    State& S = st();
+    std::lock_guard<std::mutex> lock(S.mu);
+    if (int rc = ensure_ready(S)) return rc;
+    const cudaError_t e = cudaMallocManaged(ptr, std::max<size_t>(bytes, 16), cudaMemAttachGlobal);
+    if (e != cudaSuccess) {
+        *ptr = nullptr;
+        return fail(KVB_ERR_DEVICE, "managed allocation failed (" + std::to_string(bytes) + " bytes): " +
+                                        cudaGetErrorString(e));
+    }
+    return KVB_OK;
+}
+
+int kvb_buffer_free(void* ptr) {
+    if (!ptr) return KVB_OK;
+    KVB_CUDA(cudaFree(ptr));
+    return KVB_OK;
+}
+
+int kvb_auto_part_tokens(kvb_shape s, int max_len) {
+    int part = 512;
+    while (part > 64 && (long long)s.batch * s.num_kv_heads * ((max_len + part - 1) / part) < 512) part /= 2;
+    return part;
+}
+
+int kvb_paged_part_tokens(const kvb_paged_args* a) {
+    if (int rc = check_static(a)) return -rc;
+    DeviceFacts f;
+    if (int rc = device_facts(&f)) return -rc;
+    return geometry(a, f.num_sms).part;
+}
+
+int kvb_paged_workspace_bytes(const kvb_paged_args* a, size_t* bytes) {
+    if (!bytes) return fail(KVB_ERR_INVALID, "null bytes");
+    if (int rc = check_static(a)) return rc;
+    DeviceFacts f;
+    if (int rc = device_facts(&f)) return rc;
+    const Geometry g = geometry(a, f.num_sms);
+    *bytes = kvb_workspace_layout(a->shape.batch, a->shape.num_heads, g.nhg, g.max_parts, a->shape.head_dim).total;
+    return KVB_OK;
+}
+
+int kvb_paged_decode_async(const kvb_paged_args* a, void* workspace, size_t workspace_bytes, void* stream) {
+    if (int rc = check_static(a)) return rc;
+    size_t need = 0;
+    if (int rc = kvb_paged_workspace_bytes(a, &need)) return rc;
+    if (!workspace || workspace_bytes < need)
+        return fail(KVB_ERR_INVALID, "workspace too small: need " + std::to_string(need) + " bytes");
+    return launch_paged(a, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int kvb_paged_error_flag(void* workspace, void* stream, int* flag) {
+    if (!workspace || !flag) return fail(KVB_ERR_INVALID, "null workspace or flag");
+    unsigned h = 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    KVB_CUDA(cudaMemcpyAsync(&h, workspace, sizeof h, cudaMemcpyDeviceToHost, s));
+    KVB_CUDA(cudaStreamSynchronize(s));
+    if (h) {
+        KVB_CUDA(cudaMemsetAsync(workspace, 0, sizeof h, s));
+        KVB_CUDA(cudaStreamSynchronize(s));
+    }
+    *flag = (int)h;
+    return KVB_OK;
+}
+
+int kvb_run_paged(const kvb_paged_args* a, int steps, double* gpu_ms) {
+    if (gpu_ms) *gpu_ms = 0;
+    if (int rc = check_static(a)) return rc;
+    if (steps < 0) return fail(KVB_ERR_INVALID, "steps < 0");
+    State& S = st();
+    std::lock_guard<std::mutex> lock(S.mu);
+    if (int rc = ensure_ready(S)) return rc;
+    const kvb_shape& s = a->shape;
+    const int B = s.batch;
+
+    // Lengths and live block ids are checked on the host before anything is launched
+    // (src/metal_attn.mm:107-117; the block ids are a check the reference does not make).
+    std::vector<int32_t> lens, table;
+    if (int rc = read_ints(a->seq_lens, (size_t)B, &lens)) return rc;
+    const long long capacity = (long long)a->max_blocks * a->page_size;
+    for (int b = 0; b < B; ++b) {
+        const int len = lens[b];
+        if (len < 0 || len > a->max_len || (long long)len > capacity)
+            return fail(KVB_ERR_INVALID, "sequence " + std::to_string(b) + " has length " + std::to_string(len) +
+                                             ", max_len " + std::to_string(a->max_len) + ", capacity " +
+                                             std::to_string(capacity));
+    }
+    if (a->max_len > 0) {
+        if (int rc = read_ints(a->block_table, (size_t)B * a->max_blocks, &table)) return rc;
+        for (int b = 0; b < B; ++b) {
+            const int live = (lens[b] + a->page_size - 1) / a->page_size;
+            for (int i = 0; i < live; ++i) {
+                const int32_t blk = table[(size_t)b * a->max_blocks + i];
+                if (blk < 0 || blk >= a->num_blocks)
+                    return fail(KVB_ERR_INVALID, "sequence " + std::to_string(b) + " block " + std::to_string(i) +
+                                                     " has id " + std::to_string(blk) + ", pool of " +
+                                                     std::to_string(a->num_blocks) + " blocks");
+            }
+        }
+    }
+    for (auto [p, what] : {std::pair<const void*, const char*>{a->q, "q"}, {a->out, "out"}, {a->k, "k"},
+                           {a->v, "v"}, {a->block_table, "block_table"}, {a->seq_lens, "seq_lens"},
+                           {a->k_scale, "k_scale"}, {a->v_scale, "v_scale"}})
+        if (int rc = require_device_accessible(p, what)) return rc;
+
+    size_t need = 0;
+    if (int rc = kvb_paged_workspace_bytes(a, &need)) return rc;
+    if (int rc = grow(S, &S.ws, &S.ws_bytes, need, true)) return rc;
+
+    // Managed buffers are moved to the device before the timed region (the reference's GPU time
+    // excludes encoding too).
+    const size_t nq = (size_t)B * s.num_heads * s.head_dim * sizeof(float);
+    const size_t pool = (size_t)a->num_blocks * s.num_kv_heads * a->page_size * s.head_dim * elem_size(a->kv_type);
+    const size_t scales = (size_t)a->num_blocks * s.num_kv_heads * sizeof(float);
+    const int live = a->max_len > 0;
+    if (int rc = prefetch(S, a->q, nq)) return rc;
+    if (int rc = prefetch(S, a->out, nq)) return rc;
+    if (int rc = prefetch(S, a->seq_lens, (size_t)B * sizeof(int32_t))) return rc;
+    if (live) {
+        if (int rc = prefetch(S, a->block_table, (size_t)B * a->max_blocks * sizeof(int32_t))) return rc;
+        if (int rc = prefetch(S, a->k, pool)) return rc;
+        if (int rc = prefetch(S, a->v, pool)) return rc;
+        if (a->kv_type == KVB_I8) {
+            if (int rc = prefetch(S, a->k_scale, scales)) return rc;
+            if (int rc = prefetch(S, a->v_scale, scales)) return rc;
+        }
+    }
+    cudaEvent_t e0, e1;
+    if (int rc = begin_timed(S, &e0, &e1)) return rc;
+    for (int i = 0; i < steps; ++i) {
+        if (int rc = launch_paged(a, S.ws, S.stream)) {
+            cudaEventDestroy(e0);
+            cudaEventDestroy(e1);
+            return rc;
+        }
+    }
+    return end_timed(S, e0, e1, gpu_ms, true);
+}
+
+int kvb_run_naive(const kvb_naive_args* a, double* gpu_ms) {
+    if (gpu_ms) *gpu_ms = 0;
+    if (!a) return fail(KVB_ERR_INVALID, "null arguments");
+    const kvb_shape& s = a->shape;
+    if (a->kv_type == KVB_I8) return fail(KVB_ERR_INVALID, "naive kernels take f32 or f16 caches");
+    if (a->kv_type != KVB_F32 && a->kv_type != KVB_F16) return fail(KVB_ERR_INVALID, "unknown kv_type");
+    if (a->max_len < 0) return fail(KVB_ERR_INVALID, "max_len < 0");
+    if (s.batch < 0 || s.num_heads <= 0 || s.num_kv_heads <= 0) return fail(KVB_ERR_INVALID, "bad shape");
+    if (s.head_dim != 64 && s.head_dim != 128) return fail(KVB_ERR_INVALID, "head_dim must be 64 or 128");
+    if (s.num_heads % s.num_kv_heads != 0) return fail(KVB_ERR_INVALID, "H % Hkv != 0");
+    if (s.batch > 0 && (!a->q || !a->out || !a->seq_lens || (a->max_len > 0 && (!a->k || !a->v))))
+        return fail(KVB_ERR_INVALID, "null pointer argument");
+    State& S = st();
+    std::lock_guard<std::mutex> lock(S.mu);
+    if (int rc = ensure_ready(S)) return rc;
+    std::vector<int32_t> lens;
+    if (int rc = read_ints(a->seq_lens, (size_t)s.batch, &lens)) return rc;
+    for (int b = 0; b < s.batch; ++b)
+        if (lens[b] < 0 || lens[b] > a->max_len)
+            return fail(KVB_ERR_INVALID, "sequence " + std::to_string(b) + " has length " + std::to_string(lens[b]) +
+                                             ", max_len " + std::to_string(a->max_len) + ", capacity " +
+                                             std::to_string(a->max_len));
+    for (auto [p, what] : {std::pair<const void*, const char*>{a->q, "q"}, {a->out, "out"}, {a->k, "k"},
+                           {a->v, "v"}, {a->seq_lens, "seq_lens"}})
+        if (int rc = require_device_accessible(p, what)) return rc;
+    const size_t nscores = (size_t)s.batch * s.num_heads * std::max(a->max_len, 1) * sizeof(float);
+    if (int rc = grow(S, &S.scores, &S.scores_bytes, nscores, false)) return rc;
+    const size_t nq = (size_t)s.batch * s.num_heads * s.head_dim * sizeof(float);
+    const size_t nkv = (size_t)s.batch * s.num_kv_heads * a->max_len * s.head_dim * elem_size(a->kv_type);
+    for (auto [p, n] : {std::pair<const void*, size_t>{a->q, nq}, {a->out, nq}, {a->k, nkv}, {a->v, nkv},
+                        {a->seq_lens, (size_t)s.batch * sizeof(int32_t)}})
+        if (int rc = prefetch(S, p, n)) return rc;
+    cudaEvent_t e0, e1;
+    if (int rc = begin_timed(S, &e0, &e1)) return rc;
+    const cudaError_t e = kvb_launch_naive(a->q, a->k, a->v, a->seq_lens, a->out, static_cast<float*>(S.scores),
+                                           s.batch, s.num_heads, s.num_kv_heads, s.head_dim, a->max_len, a->kv_type,
+                                           S.stream);
+    if (e != cudaSuccess) {
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        return fail(KVB_ERR_DEVICE, std::string("naive launch: ") + cudaGetErrorString(e));
+    }
+    return end_timed(S, e0, e1, gpu_ms, false);
+}
+
+int kvb_begin_pipelined(void) {
+    State& S = st();
+    std::lock_guard<std::mutex> lock(S.mu);
+    if (int rc = ensure_ready(S)) return rc;
+    for (auto& pr : S.timed) {
+        cudaEventDestroy(pr.first);
+        cudaEventDestroy(pr.second);
+    }
+    S.timed.clear();
+    S.pipelined = true;
+    S.pipeline_checks = false;
+    return KVB_OK;
+}
+
+int kvb_pipelined_runs(size_t* count) {
+    if (!count) return fail(KVB_ERR_INVALID, "null count");
+    State& S = st();
+    std::lock_guard<std::mutex> lock(S.mu);
+    if (!S.pipelined) return fail(KVB_ERR_STATE, "not in pipelined mode");
+    *count = S.timed.size();
+    return KVB_OK;
+}
+
+int kvb_end_pipelined(double* ms, size_t cap, size_t* count) {
+    State& S = st();
+    std::lock_guard<std::mutex> lock(S.mu);
+    if (!S.pipelined) return fail(KVB_ERR_STATE, "end_pipelined without begin_pipelined");
+    S.pipelined = false;
+    if (count) *count = S.timed.size();
+    int rc = KVB_OK;
+    for (size_t i = 0; i < S.timed.size(); ++i) {
+        const cudaError_t sync = cudaEventSynchronize(S.timed[i].second);
+        float t = 0;
+        if (sync == cudaSuccess) cudaEventElapsedTime(&t, S.timed[i].first, S.timed[i].second);
+        else if (rc == KVB_OK) rc = fail(KVB_ERR_DEVICE, std::string("device failure: ") + cudaGetErrorString(sync));
+        if (ms && i < cap) ms[i] = t;
+        cudaEventDestroy(S.timed[i].first);
+        cudaEventDestroy(S.timed[i].second);
+    }
+    S.timed.clear();
+    if (rc == KVB_OK && S.pipeline_checks) rc = check_flag(S);
+    S.pipeline_checks = false;
+    return rc;
+}
+
+int kvb_read_bandwidth(const void* src, size_t bytes, double* gpu_ms) {
+    if (gpu_ms) *gpu_ms = 0;
+    if (!src && bytes) return fail(KVB_ERR_INVALID, "null src");
+    State& S = st();
+    std::lock_guard<std::mutex> lock(S.mu);
+    if (int rc = ensure_ready(S)) return rc;
+    if (int rc = require_device_accessible(src, "src")) return rc;
+    if (int rc = prefetch(S, src, bytes)) return rc;
+    DeviceFacts f;
+    if (int rc = device_facts(&f)) return rc;
+    cudaEvent_t e0, e1;
+    if (int rc = begin_timed(S, &e0, &e1)) return rc;
+    const cudaError_t e = kvb_launch_read_bw(src, bytes, S.sink, f.num_sms, S.stream);
+    if (e != cudaSuccess) {
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        return fail(KVB_ERR_DEVICE, std::string("read_bw launch: ") + cudaGetErrorString(e));
+    }
+    return end_timed(S, e0, e1, gpu_ms, false);
+}
+
+int kvb_flush_caches(void) {
+    State& S = st();
+    std::lock_guard<std::mutex> lock(S.mu);
+    if (int rc = ensure_ready(S)) return rc;
+    DeviceFacts f;
+    if (int rc = device_facts(&f)) return rc;
+    const size_t want = std::max<size_t>(256u << 20, 4 * (size_t)f.l2_bytes);
+    if (int rc = grow(S, &S.flush, &S.flush_bytes, want, false)) return rc;
+    const cudaError_t e = kvb_launch_fill(S.flush, S.flush_bytes, ++S.flush_value, f.num_sms, S.stream);
+    if (e != cudaSuccess) return fail(KVB_ERR_DEVICE, std::string("flush launch: ") + cudaGetErrorString(e));
+    if (!S.pipelined) KVB_CUDA(cudaStreamSynchronize(S.stream));
+    return KVB_OK;
+}
+
+const char* kvb_last_error(void) { return t_err.c_str(); }
+
+}  // extern "C"

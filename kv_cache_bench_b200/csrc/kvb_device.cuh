@@ -1,0 +1,398 @@
+// Device-side building blocks shared by the paged decode kernels: inline-PTX wrappers for sm_100a
+// (mbarrier, TMA tile loads, ldmatrix, mma.sync), bounded waits that report instead of hanging,
+// the split-K work-unit enumeration, and the per-unit epilogue with the fused cross-partition merge.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "kvb_internal.h"
+
+namespace kvb_dev {
+
+// A score that is "minus infinity" but finite: exp2(NEG_BIG - m) is exactly 0 for any real m and
+// max/min arithmetic on it never produces NaN (the same convention as the reference kernel,
+// src/kernels.metal:18-20).
+constexpr float NEG_BIG = -1e30f;
+
+// ---- error reporting -------------------------------------------------------------------------
+
+// Sets bits of the workspace error word (KVB_DEVERR_* in kvb_internal.h).
+__device__ __forceinline__ void raise_error(unsigned* flag, unsigned bits) { atomicOr(flag, bits); }
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---- shared memory / mbarrier ------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbarrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase with parity `parity` of `bar` to complete, for at most KVB_WAIT_LIMIT_NS of
+// wall time (or until `*abort` is set by another warp). Returns false when it gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 0) {
+            if (*abort) return false;
+            if (globaltimer_ns() - t0 > KVB_WAIT_LIMIT_NS) return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Named barrier among `nthreads` threads (ids 1..15; 0 is __syncthreads).
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Named barrier that also returns whether `pred` was non-zero in any participating thread.
+__device__ __forceinline__ int named_barrier_or(uint32_t id, uint32_t nthreads, int pred) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.s32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.s32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(pred), "r"(id), "r"(nthreads)
+        : "memory");
+    return r;
+}
+
+// ---- TMA ----------------------------------------------------------------------------------------
+
+// 2-D tiled bulk tensor load global -> shared, completing on `bar` (transaction bytes). The
+// innermost coordinate x is always 0 or a multiple of 128 bytes in this code.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// L2 policy for streamed K/V pages: evict first, so block tables, scales and partials stay.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// ---- shared-memory loads and tensor-core helpers -----------------------------------------------
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ void lds64(uint32_t addr, uint32_t& a, uint32_t& b) {
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "r"(addr));
+}
+
+__device__ __forceinline__ void sts128_zero(uint32_t addr) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                              uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// D = A(16x16 f16, row) * B(16x8 f16, col) + D, fp32 accumulate.
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// Splits (x0, x1) into fp16 pairs hi + lo with hi = fp16(x), lo = fp16(x - hi): the pair carries
+// about 22 significant bits, enough for fp32-level dot products on exact fp16/int8 operands.
+__device__ __forceinline__ void split_hi_lo(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    hi = h2_as_u32(h);
+    lo = h2_as_u32(__floats2half2_rn(x0 - hf.x, x1 - hf.y));
+}
+
+// int8 -> fp16 pairs. An fp16 with bit pattern 0x64XX is 1024 + XX for XX < 1024, so a signed byte
+// b becomes 0x64 | (b ^ 0x80) = 1152 + b and one subtraction of 1152 gives b exactly.
+//
+// Bytes (lo_byte, hi_byte) of `w_biased` (already XORed with 0x80808080) to half2(b_lo, b_hi):
+__device__ __forceinline__ uint32_t i8pair_to_h2(uint32_t w_biased, uint32_t sel) {
+    const uint32_t x = __byte_perm(w_biased, 0x64646464u, sel);
+    return h2_as_u32(__hsub2(u32_as_h2(x), __half2half2(__ushort_as_half(0x6480))));
+}
+// Selectors for i8pair_to_h2: bytes (0,1) and (2,3) of the word, 0x64 from the second operand.
+constexpr uint32_t SEL_B01 = 0x4140;
+constexpr uint32_t SEL_B23 = 0x4342;
+
+// Byte i of `wa` and byte i of `wb` (unbiased) to half2(a_i, b_i): the transposing conversion used
+// for V, where the two values of a pair come from two different token rows.
+__device__ __forceinline__ uint32_t i8cross_to_h2(uint32_t wa, uint32_t wb, uint32_t i) {
+    const uint32_t x = __byte_perm(wa, wb, i | ((4u + i) << 8));
+    const uint32_t y = (x & 0x00FF00FFu) ^ 0x64806480u;
+    return h2_as_u32(__hsub2(u32_as_h2(y), __half2half2(__ushort_as_half(0x6480))));
+}
+
+// ---- work units ---------------------------------------------------------------------------------
+
+// One work unit is one split-K partition [t0, t1) of one sequence b for one group of query heads
+// that share a KV head. Units are numbered sequence-major, then head group, then partition.
+struct Unit {
+    int b, hg, part;
+    int kvh, h0, nh;  // KV head, first query head, heads in the group
+    int len;          // sequence length (validated)
+    int t0, t1;       // token range of the partition
+    int nparts;       // partitions of this sequence (0 when empty or invalid)
+    bool bad;         // the length is out of range: outputs get NaN
+};
+
+// Partitions of a sequence of length len, or 0 for an empty or invalid one; invalid lengths are
+// reported in *bad. Every (sequence, head group) owns max(1, partitions) units.
+__device__ __forceinline__ int seq_partitions(const DecodeParams& p, int len, bool* bad) {
+    *bad = len < 0 || len > p.max_len || (long long)len > (long long)p.max_blocks * p.page;
+    if (*bad || len == 0) return 0;
+    return (len + p.part_tokens - 1) / p.part_tokens;
+}
+
+__device__ __forceinline__ Unit make_unit(const DecodeParams& p, int b, int hg, int part, int len) {
+    Unit u;
+    u.b = b;
+    u.hg = hg;
+    u.part = part;
+    u.len = len;
+    u.nparts = seq_partitions(p, len, &u.bad);
+    u.kvh = hg / p.gpk;
+    u.h0 = u.kvh * p.G + (hg % p.gpk) * p.qg;
+    u.nh = min(p.qg, p.G - (hg % p.gpk) * p.qg);
+    u.t0 = part * p.part_tokens;
+    u.t1 = u.nparts ? min(len, u.t0 + p.part_tokens) : 0;
+    return u;
+}
+
+// Iterates this CTA's units (static round robin over the grid). With B <= KVB_PREFIX_MAX the
+// units are packed through a prefix sum over sequences kept in shared memory (`prefix`, B + 1
+// ints, filled by build_unit_prefix); otherwise every (b, hg, part < max_parts) slot is visited and
+// slots past a sequence's partitions are skipped.
+struct UnitCursor {
+    const DecodeParams* p;
+    const int* prefix;  // nullptr: dense enumeration
+    long long next, total;
+
+    __device__ __forceinline__ bool advance(Unit& u) {
+        const DecodeParams& P = *p;
+        while (next < total) {
+            const long long idx = next;
+            next += gridDim.x;
+            if (prefix) {
+                // largest b with prefix[b] <= idx
+                int lo = 0, hi = P.B - 1;
+                while (lo < hi) {
+                    const int mid = (lo + hi + 1) >> 1;
+                    if (prefix[mid] <= idx) lo = mid;
+                    else hi = mid - 1;
+                }
+                const int b = lo;
+                const int len = __ldg(P.seq_lens + b);
+                bool bad;
+                const int per = max(1, seq_partitions(P, len, &bad));
+                const int local = int(idx - prefix[b]);
+                u = make_unit(P, b, local / per, local % per, len);
+                return true;
+            }
+            const long long per_seq = (long long)P.nhg * P.max_parts;
+            const int b = int(idx / per_seq);
+            const int rem = int(idx % per_seq);
+            const int hg = rem / P.max_parts, part = rem % P.max_parts;
+            const int len = __ldg(P.seq_lens + b);
+            bool bad;
+            const int np = seq_partitions(P, len, &bad);
+            if (part >= max(1, np)) continue;
+            u = make_unit(P, b, hg, part, len);
+            return true;
+        }
+        return false;
+    }
+};
+
+// Fills prefix[0..B] with the running count of units per sequence (nhg * max(1, partitions)).
+// Called by `nthreads` threads (a multiple of 32) that then synchronize on barrier `bar_id`.
+__device__ __forceinline__ void build_unit_prefix(const DecodeParams& p, int* prefix, int tid, int nthreads,
+                                                  uint32_t bar_id) {
+    // Each thread counts a contiguous slice, then warp 0 scans the slice totals.
+    const int per = (p.B + nthreads - 1) / nthreads;
+    const int s0 = min(p.B, tid * per), s1 = min(p.B, s0 + per);
+    int sum = 0;
+    for (int b = s0; b < s1; ++b) {
+        bool bad;
+        sum += p.nhg * max(1, seq_partitions(p, __ldg(p.seq_lens + b), &bad));
+        prefix[b + 1] = sum;  // slice-local inclusive sums for now
+    }
+    __shared__ int slice_total[KVB_MAX_THREADS];
+    slice_total[tid] = sum;
+    named_barrier(bar_id, nthreads);
+    if (tid < 32) {
+        int carry = 0;
+        for (int base = 0; base < nthreads; base += 32) {
+            int v = slice_total[base + tid];
+            int incl = v;
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, incl, o);
+                if (tid >= o) incl += n;
+            }
+            slice_total[base + tid] = carry + incl - v;  // exclusive offset of this slice
+            carry += __shfl_sync(0xffffffffu, incl, 31);
+        }
+    }
+    named_barrier(bar_id, nthreads);
+    const int off = slice_total[tid];
+    for (int b = s0; b < s1; ++b) prefix[b + 1] += off;
+    if (tid == 0) prefix[0] = 0;
+    named_barrier(bar_id, nthreads);
+}
+
+__device__ __forceinline__ long long unit_total(const DecodeParams& p, const int* prefix) {
+    return prefix ? (long long)prefix[p.B] : (long long)p.B * p.nhg * p.max_parts;
+}
+
+// ---- epilogue -----------------------------------------------------------------------------------
+
+// Finishes one unit once its per-slot online-softmax states are in shared memory:
+//   slot_o  [nslots][KVB_EPI_HEADS][D]  unnormalized accumulators (already scaled by `o_scale`
+//                                       when read), slot_ml [nslots][KVB_EPI_HEADS] (m, l), m in
+//                                       log2 units.
+// Heads are processed in rounds of KVB_EPI_HEADS by the caller; this handles heads
+// [g0, g0 + ng) of unit u. A single-partition sequence writes `out` directly; otherwise the
+// partition is stored to the workspace and the last partition to arrive (atomic counter per
+// (sequence, head group)) merges all of them into `out`.
+//
+// Threads: `nthreads` consecutive threads starting at tid 0 of the group, barrier `bar_id`.
+template <int D>
+__device__ __forceinline__ void merge_slots_and_store(const DecodeParams& p, const Unit& u, const float* slot_o,
+                                                      const float2* slot_ml, int nslots, int g0, int ng,
+                                                      float o_scale, int tid, int nthreads) {
+    for (int idx = tid; idx < ng * D; idx += nthreads) {
+        const int g = idx / D, d = idx % D;
+        float M = NEG_BIG;
+        for (int s = 0; s < nslots; ++s) M = fmaxf(M, slot_ml[s * KVB_EPI_HEADS + g].x);
+        float L = 0.f, o = 0.f;
+        for (int s = 0; s < nslots; ++s) {
+            const float2 ml = slot_ml[s * KVB_EPI_HEADS + g];
+            const float w = exp2f(ml.x - M);
+            L += ml.y * w;
+            o += slot_o[(s * KVB_EPI_HEADS + g) * D + d] * w;
+        }
+        o *= o_scale;
+        const int h = u.h0 + g0 + g;
+        if (u.nparts == 1) {
+            p.out[((size_t)u.b * p.H + h) * D + d] = o / L;
+        } else {
+            const size_t slot = ((size_t)u.b * p.H + h) * p.max_parts + u.part;
+            p.part_o[slot * D + d] = o / L;
+            if (d == 0) p.part_ml[slot] = make_float2(M, L);
+        }
+    }
+}
+
+// After every round of merge_slots_and_store for a multi-partition unit: counts the partition
+// in and, if it was the last one, merges all partitions of (b, head group) into `out`.
+template <int D>
+__device__ __forceinline__ void finish_partition(const DecodeParams& p, const Unit& u, int tid, int nthreads,
+                                                 uint32_t bar_id, int* s_flag) {
+    if (u.nparts <= 1) return;
+    __threadfence();
+    named_barrier(bar_id, nthreads);
+    if (tid == 0) {
+        unsigned* ctr = p.counters + (size_t)u.b * p.nhg + u.hg;
+        const unsigned prev = atomicAdd(ctr, 1u);
+        const int last = prev == unsigned(u.nparts - 1);
+        if (last) *ctr = 0u;  // ready for the next launch (stream order)
+        *s_flag = last;
+    }
+    named_barrier(bar_id, nthreads);
+    if (!*s_flag) return;
+    __threadfence();
+    for (int idx = tid; idx < u.nh * D; idx += nthreads) {
+        const int g = idx / D, d = idx % D, h = u.h0 + g;
+        const size_t base = ((size_t)u.b * p.H + h) * p.max_parts;
+        float M = NEG_BIG;
+        for (int i = 0; i < u.nparts; ++i) M = fmaxf(M, __ldcg(&p.part_ml[base + i].x));
+        float L = 0.f, o = 0.f;
+        for (int i = 0; i < u.nparts; ++i) {
+            const float2 ml = __ldcg(&p.part_ml[base + i]);
+            const float w = ml.y * exp2f(ml.x - M);
+            L += w;
+            o += w * __ldcg(&p.part_o[(base + i) * D + d]);
+        }
+        p.out[((size_t)u.b * p.H + h) * D + d] = o / L;
+    }
+}
+
+// Units with no tokens: an empty sequence attends to nothing and gives exactly 0; a sequence whose
+// length was refused gives NaN and raises the error flag.
+template <int D>
+__device__ __forceinline__ void store_tokenless_unit(const DecodeParams& p, const Unit& u, int tid, int nthreads) {
+    if (u.bad && tid == 0) raise_error(p.error_flag, KVB_DEVERR_LENGTH);
+    const float val = u.bad ? __int_as_float(0x7fc00000) : 0.0f;
+    for (int idx = tid; idx < u.nh * D; idx += nthreads)
+        p.out[((size_t)u.b * p.H + u.h0 + idx / D) * D + idx % D] = val;
+}
+
+}  // namespace kvb_dev

@@ -1,0 +1,92 @@
+// Types and constants shared by the host launchers (kvb_capi.cu) and the kernels. Not part of the
+// public ABI (that is include/kvb_cuda.h).
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include <cuda_runtime.h>
+
+// Bounded device waits give up after this much wall time (the kernel then reports
+// KVB_DEVERR_TIMEOUT and returns instead of hanging the GPU).
+#define KVB_WAIT_LIMIT_NS 2000000000ull
+
+// Bits of the workspace error word.
+#define KVB_DEVERR_LENGTH 1u    // a sequence length outside [0, min(max_len, max_blocks * page)]
+#define KVB_DEVERR_BLOCK 2u     // a live block id outside [0, num_blocks)
+#define KVB_DEVERR_TIMEOUT 4u   // a bounded wait gave up
+
+// Sequences up to this batch size are enumerated through a prefix sum in shared memory.
+#define KVB_PREFIX_MAX 1024
+// Largest CTA of any decode kernel.
+#define KVB_MAX_THREADS 256
+// Heads merged per epilogue round (bounds the epilogue's shared memory).
+#define KVB_EPI_HEADS 4
+// Tokens per TMA stage of the tensor-core kernel.
+#define KVB_CHUNK 64
+
+// Everything a decode launch needs. Pointers are device pointers.
+struct DecodeParams {
+    const float* q;          // [B][H][D]
+    const void* k;           // pools [num_blocks][Hkv][page][D]
+    const void* v;
+    const int* block_table;  // [B][max_blocks]
+    const int* seq_lens;     // [B]
+    const float* k_scale;    // [num_blocks][Hkv] (int8)
+    const float* v_scale;
+    float* out;              // [B][H][D]
+    // workspace
+    float* part_o;           // [B][H][max_parts][D], partition outputs (normalized)
+    float2* part_ml;         // [B][H][max_parts], (max in log2 units, sum)
+    unsigned* counters;      // [B][nhg], partitions finished per (sequence, head group)
+    unsigned* error_flag;    // KVB_DEVERR_* bits
+    // shape
+    int B, H, Hkv, G;
+    int qg;    // query heads per head group (<= 8)
+    int gpk;   // head groups per KV head
+    int nhg;   // head groups per sequence = Hkv * gpk
+    int page, max_blocks, max_len, part_tokens, max_parts;
+    long long num_blocks;
+    float q_scale;  // log2(e) / sqrt(D): scores come out in log2 units
+};
+
+// Workspace layout (offsets in bytes), shared by the size query and the launcher.
+struct WorkspaceLayout {
+    size_t flag_off, counters_off, ml_off, o_off, total;
+};
+
+constexpr inline size_t kvb_align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+inline WorkspaceLayout kvb_workspace_layout(int B, int H, int nhg, int max_parts, int D) {
+    WorkspaceLayout w;
+    w.flag_off = 0;
+    w.counters_off = 256;
+    w.ml_off = kvb_align_up(w.counters_off + sizeof(unsigned) * (size_t)B * nhg, 256);
+    w.o_off = kvb_align_up(w.ml_off + sizeof(float) * 2 * (size_t)B * H * max_parts, 256);
+    w.total = kvb_align_up(w.o_off + sizeof(float) * (size_t)B * H * max_parts * D, 256);
+    return w;
+}
+
+// Kernel launchers (one per kernel family), implemented next to the kernels.
+struct LaunchInfo {
+    int num_sms;
+    cudaStream_t stream;
+};
+
+// CUDA-core kernel: every storage type, page size, head dim and group size.
+cudaError_t kvb_launch_decode_simt(const DecodeParams& p, int kv_type, int D, const LaunchInfo& li);
+
+// TMA + tensor-core kernel: fp16/int8 with 128- or 256-byte rows, page % 8 == 0 and page | 64 or
+// 64 | page (page <= 256), qg <= 8. `tmap_k`/`tmap_v` are CUtensorMap objects over the pools.
+bool kvb_mma_supported(int kv_type, int D, int page, int qg);
+cudaError_t kvb_launch_decode_mma(const DecodeParams& p, int kv_type, int D, const void* tmap_k,
+                                  const void* tmap_v, const LaunchInfo& li);
+
+// Naive three-pass baseline on the contiguous cache.
+cudaError_t kvb_launch_naive(const float* q, const void* k, const void* v, const int* seq_lens, float* out,
+                             float* scores, int B, int H, int Hkv, int D, int max_len, int kv_type,
+                             cudaStream_t stream);
+
+// Streaming read probe and L2 flush.
+cudaError_t kvb_launch_read_bw(const void* src, size_t bytes, float* sink, int num_sms, cudaStream_t stream);
+cudaError_t kvb_launch_fill(void* dst, size_t bytes, uint32_t value, int num_sms, cudaStream_t stream);

@@ -1,0 +1,80 @@
+"""CPU-side checks of the C ABI boundary: the library loads, exports every symbol include/kvb_cuda.h
+declares, and refuses bad arguments with KVB_ERR_INVALID before touching a device. No kernel is
+launched here (no GPU)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+import kv_cache_bench_b200 as kvb
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    syms = set()
+    for fn in os.listdir(os.path.join(ROOT, "include")):
+        if fn.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", fn)).read()
+            syms |= set(re.findall(r"^\s*(?:const\s+)?\w[\w\s\*]*?\b(kvb_\w+)\s*\(", text, re.M))
+    return syms
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(kvb.library_path())
+    syms = declared_symbols()
+    assert len(syms) >= 17, syms
+    for s in sorted(syms):
+        assert hasattr(lib, s), s
+
+
+def test_reference_auto_part_tokens_thresholds():
+    # the thresholds pinned by the reference's boundary tests (tests/boundary_tests.cpp:86-92)
+    s = kvb.Shape(2, 32, 8, 128)
+    want = {0: 64, 1: 64, 3968: 64, 3969: 128, 7936: 128, 7937: 256, 15872: 256, 15873: 512, 1 << 20: 512}
+    for L, part in want.items():
+        assert kvb.auto_part_tokens(s, L) == part
+
+
+def _args(**over):
+    base = dict(shape=kvb.Shape(1, 8, 2, 128), type=kvb.KvType.f16, page_size=16, max_blocks=1, max_len=1,
+                part_tokens=0, num_blocks=1)
+    base.update(over)
+    return kvb.PagedArgs(**base)
+
+
+@pytest.mark.parametrize("over,msg", [
+    (dict(page_size=0), "page_size"),
+    (dict(part_tokens=-1), "part_tokens"),
+    (dict(max_len=-1), "max_len"),
+    (dict(type=kvb.KvType.i8), "scales"),
+    (dict(shape=kvb.Shape(1, 8, 2, 96)), "head_dim"),
+    (dict(shape=kvb.Shape(1, 6, 4, 128)), "Hkv"),
+])
+def test_static_refusals_need_no_device(over, msg):
+    with pytest.raises(ValueError, match=msg):
+        kvb.run_paged(_args(**over))
+
+
+def test_naive_refuses_int8():
+    with pytest.raises(ValueError, match="f32 or f16"):
+        kvb.run_naive(kvb.NaiveArgs(kvb.Shape(1, 8, 2, 128), kvb.KvType.i8, 4))
+
+
+def test_workspace_layout_is_monotone_in_partitions():
+    # paged_workspace_bytes needs the device's SM count only for part_tokens == 0; with an explicit
+    # partition size it is pure arithmetic, but the ABI still asks the runtime for the device, so
+    # without a GPU it must fail cleanly instead of crashing.
+    c = kvb.device_args(kvb.Shape(1, 8, 2, 128), kvb.KvType.f16, 16, 4, 64, q=16, k=16, v=16, block_table=16,
+                        seq_lens=16, out=16, num_blocks=4, part_tokens=16)
+    if kvb.metal_available():
+        pytest.skip("device present: covered by the GPU tests")
+    with pytest.raises(RuntimeError):
+        kvb.paged_workspace_bytes(c)
+
+
+def test_available_is_false_without_gpu_or_true_with():
+    import torch
+    assert kvb.metal_available() == torch.cuda.is_available()

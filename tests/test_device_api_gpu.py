@@ -1,0 +1,109 @@
+"""The stream-level C ABI (kvb_paged_decode_async) with torch tensors as device buffers: parity,
+workspace reuse across calls and shapes, CUDA-graph capture, and the device-side refusal of bad
+lengths and block ids (NaN outputs plus an error flag, no out-of-bounds access)."""
+import numpy as np
+import pytest
+import torch
+
+import kv_cache_bench_b200 as kvb
+import oracle
+from kv_cache_bench_b200.torch_ops import PagedDecoder
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-5
+
+
+def _dev(case, device="cuda"):
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)  # noqa: E731
+    d = dict(q=t(case.q), k=t(case.k), v=t(case.v), table=t(case.table), lens=t(case.lens.astype(np.int32)))
+    if case.k_scale is not None:
+        d["ks"], d["vs"] = t(case.k_scale), t(case.v_scale)
+    return d
+
+
+def _call(dec, d, max_len, **kw):
+    return dec(d["q"], d["k"], d["v"], d["table"], d["lens"], max_len, k_scale=d.get("ks"), v_scale=d.get("vs"),
+               **kw)
+
+
+@pytest.mark.parametrize("kv_type", [oracle.F32, oracle.F16, oracle.I8])
+def test_async_matches_oracle_and_reuses_workspace(kv_type):
+    dec = PagedDecoder()
+    for seed, lens in enumerate([[3000, 5, 0, 700], [64, 65], [9000]]):
+        case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=lens, kv_type=kv_type, page=64,
+                                seed=seed)
+        d = _dev(case)
+        ref = case.reference()
+        for part in (0, 128, 0):  # the same workspace across calls, shapes and partition sizes
+            out = _call(dec, d, case.max_len, part_tokens=part)
+            torch.cuda.synchronize()
+            assert oracle.max_abs_diff(out.cpu().numpy(), ref) <= TOL, (lens, part)
+        assert dec.error_flag() == 0
+
+
+def test_cuda_graph_replay():
+    case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=[5000, 300], kv_type=oracle.I8,
+                            page=128, seed=3)
+    d = _dev(case)
+    dec = PagedDecoder()
+    out = torch.empty_like(d["q"])
+    _call(dec, d, case.max_len, out=out)  # sizes the workspace outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            _call(dec, d, case.max_len, out=out)
+    out.fill_(float("nan"))
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    assert oracle.max_abs_diff(out.cpu().numpy(), case.reference()) <= TOL
+    del g
+
+
+@pytest.mark.parametrize("kernel", [kvb.Kernel.simt, kvb.Kernel.mma])
+def test_device_refuses_bad_lengths_with_nan_and_flag(kernel):
+    case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=[300, 200, 100], kv_type=oracle.F16,
+                            page=64, seed=4)
+    d = _dev(case)
+    dec = PagedDecoder()
+    ref = case.reference()
+    # sequence 1 claims more tokens than max_len (and than its block table holds)
+    d["lens"][1] = 10_000
+    out = _call(dec, d, case.max_len, kernel=kernel)
+    torch.cuda.synchronize()
+    o = out.cpu().numpy()
+    assert np.isnan(o[1]).all()
+    assert oracle.max_abs_diff(o[[0, 2]], ref[[0, 2]]) <= TOL
+    assert dec.error_flag() & 1
+    assert dec.error_flag() == 0  # reading clears it
+    # a negative length
+    d["lens"][1] = -5
+    o = _call(dec, d, case.max_len, kernel=kernel).cpu().numpy()
+    assert np.isnan(o[1]).all() and dec.error_flag() & 1
+
+
+@pytest.mark.parametrize("kernel", [kvb.Kernel.simt, kvb.Kernel.mma])
+def test_device_refuses_bad_block_ids_with_nan_and_flag(kernel):
+    case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=[300, 200], kv_type=oracle.I8,
+                            page=64, seed=6)
+    d = _dev(case)
+    dec = PagedDecoder()
+    ref = case.reference()
+    for bad in (case.num_blocks, 1 << 30, -7):
+        d["table"][0, 2] = bad
+        o = _call(dec, d, case.max_len, kernel=kernel).cpu().numpy()
+        assert np.isnan(o[0]).all(), bad
+        assert oracle.max_abs_diff(o[1], ref[1]) <= TOL
+        assert dec.error_flag() & 2
+
+
+def test_host_path_refuses_bad_block_ids_before_launch():
+    case = oracle.make_case(num_heads=8, num_kv_heads=2, head_dim=128, lens=[40], kv_type=oracle.F16, page=16,
+                            seed=8)
+    case.table[0, 1] = case.num_blocks + 3
+    from tests.cuda_runner import run_case
+    with pytest.raises(ValueError, match="block"):
+        run_case(case)

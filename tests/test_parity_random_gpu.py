@@ -1,0 +1,114 @@
+"""CUDA path vs the C oracle on seeded synthetic decode steps beyond the golden vectors.
+
+Covers what the reference's grid does not reach on this kernel's design: GQA groups of 1, 3, 4, 8
+and 16 (head groups split across CTAs), every page size the tensor-core path takes (8 ... 256) and
+some it does not (7, 24, 48), ragged batches with empty sequences and lengths at chunk and page
+boundaries, explicit and automatic split-K partitions, large |q| (the fp16 split of q must not
+overflow), int8 with per-block magnitudes, pools with slack, and NaN written into every pool slot
+that holds no live token (no kernel may let one reach an output). Tolerance: 2e-5 absolute against
+the fp64 oracle on the stored or dequantized values, as in the reference's tests.
+"""
+import zlib
+
+import numpy as np
+import pytest
+
+import kv_cache_bench_b200 as kvb
+import oracle
+from tests.cuda_runner import mma_ok, run_case
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-5
+
+EDGE = [0, 1, 7, 63, 64, 65, 127, 128, 129, 300, 1025]
+
+CASES = [
+    # name, H, Hkv, D, kv_type, page, lens, parts, extra
+    ("gqa4_f16_p16_edges", 32, 8, 128, oracle.F16, 16, EDGE, [0, 64, 100], {}),
+    ("gqa4_i8_p16_edges", 32, 8, 128, oracle.I8, 16, EDGE, [0, 64, 100], dict(varied=True)),
+    ("gqa4_f32_p16_edges", 32, 8, 128, oracle.F32, 16, EDGE, [0, 64], {}),
+    ("gqa4_f16_p8", 32, 8, 128, oracle.F16, 8, [5, 130, 999], [0, 128], {}),
+    ("gqa4_f16_p32", 32, 8, 128, oracle.F16, 32, [33, 700, 64], [0, 192], {}),
+    ("gqa4_f16_p64", 32, 8, 128, oracle.F16, 64, [2000, 64, 65], [0, 256], {}),
+    ("gqa4_f16_p128", 32, 8, 128, oracle.F16, 128, [4000, 129, 1], [0, 512], {}),
+    ("gqa4_f16_p256", 32, 8, 128, oracle.F16, 256, [1000, 257, 3], [0, 64], {}),
+    ("gqa4_i8_p128", 32, 8, 128, oracle.I8, 128, [4000, 129, 1], [0, 512], dict(varied=True)),
+    ("gqa4_i8_p256", 32, 8, 128, oracle.I8, 256, [600, 256], [0], {}),
+    ("gqa4_i8_p8", 32, 8, 128, oracle.I8, 8, [77, 8, 9], [0, 64], {}),
+    ("gqa4_f16_p24_simt", 32, 8, 128, oracle.F16, 24, [100, 23, 24, 25], [0, 64], {}),
+    ("gqa4_i8_p48_simt", 32, 8, 128, oracle.I8, 48, [100, 48, 49], [0, 64], {}),
+    ("gqa4_f32_p7_simt", 32, 8, 128, oracle.F32, 7, [50, 7, 8], [0, 3], {}),
+    ("gqa8_f16_p64", 64, 8, 128, oracle.F16, 64, [3000, 17, 0], [0, 512], {}),
+    ("gqa8_i8_p64", 64, 8, 128, oracle.I8, 64, [3000, 17, 0], [0, 512], dict(varied=True)),
+    ("gqa16_f16_p16", 16, 1, 128, oracle.F16, 16, [500, 31], [0, 64], {}),
+    ("gqa3_f16_d64_p32", 12, 4, 64, oracle.F16, 32, [200, 5], [0], {}),
+    ("mha_f16_d64_p16", 4, 4, 64, oracle.F16, 16, [300, 1, 0], [0, 64], {}),
+    ("mha_i8_d64_p16_simt", 4, 4, 64, oracle.I8, 16, [300, 1], [0, 64], {}),
+    ("mha_f16_d128_p64", 8, 8, 128, oracle.F16, 64, [700, 70], [0], {}),
+    ("q_amp8_i8", 32, 8, 128, oracle.I8, 64, [1500, 3], [0], dict(q_amp=8.0, varied=True)),
+    ("q_amp1000_f16", 32, 8, 128, oracle.F16, 64, [500, 64], [0], dict(q_amp=1000.0)),
+    ("q_amp1000_i8", 32, 8, 128, oracle.I8, 32, [500, 64], [0], dict(q_amp=1000.0)),
+    ("nan_dead_slots_f16", 32, 8, 128, oracle.F16, 64, [100, 1, 65, 0], [0, 64], dict(dead_fill=np.nan)),
+    ("nan_dead_slots_f32", 32, 8, 128, oracle.F32, 16, [100, 1, 17, 0], [0, 64], dict(dead_fill=np.nan)),
+    ("slack_f16_p16", 32, 8, 128, oracle.F16, 16, [1000, 333], [0], dict(pool_slack=2.0)),
+    ("long_i8_p128", 32, 8, 128, oracle.I8, 128, [20000], [0, 4096], {}),
+    ("long_f16_p64", 32, 8, 128, oracle.F16, 64, [9000, 2500], [0, 512], {}),
+    ("batch_ragged_f16_p16", 32, 8, 128, oracle.F16, 16, list(range(0, 1200, 37)), [0], dict(pool_slack=1.1)),
+]
+
+
+@pytest.mark.parametrize("name,H,Hkv,D,kv_type,page,lens,parts,extra", CASES, ids=[c[0] for c in CASES])
+def test_random_case(name, H, Hkv, D, kv_type, page, lens, parts, extra):
+    case = oracle.make_case(num_heads=H, num_kv_heads=Hkv, head_dim=D, lens=lens, kv_type=kv_type, page=page,
+                            seed=zlib.crc32(name.encode()), **extra)
+    ref = case.reference()
+    kernels = [kvb.Kernel.simt, kvb.Kernel.auto]
+    if mma_ok(kv_type, D, page, H // Hkv):
+        kernels.append(kvb.Kernel.mma)
+    elif name.endswith("_simt"):
+        with pytest.raises(ValueError):
+            run_case(case, kernel=kvb.Kernel.mma)
+    failures = []
+    for kernel in kernels:
+        for part in parts:
+            out = run_case(case, part=part, kernel=kernel)
+            err = oracle.max_abs_diff(out, ref)
+            if not err <= TOL:
+                failures.append(f"kernel={kernel.name} part={part}: {err:.3g}")
+            for b, L in enumerate(case.lens):
+                if L == 0 and np.any(out[b] != 0):
+                    failures.append(f"kernel={kernel.name} part={part}: empty sequence {b} not 0")
+    if H // Hkv > 1:  # per-query-head ablation
+        out = run_case(case, share_kv=False)
+        if not oracle.max_abs_diff(out, ref) <= TOL:
+            failures.append("share_kv=0")
+    assert not failures, "\n".join(failures)
+
+
+def test_steps_accumulate_nothing():
+    """run_paged_steps repeats the same step: the output equals one step's (the split-K counters and
+    partials in the workspace are reset by every launch)."""
+    case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=[3000, 100], kv_type=oracle.F16,
+                            page=16, seed=11)
+    one = run_case(case, part=256)
+    many = run_case(case, part=256, steps=7)
+    assert np.array_equal(one, many)
+
+
+def test_block_permutation_invariance():
+    """Moving every block to another physical slot (and the table with it) gives bit-identical
+    output: the kernel reads pages only through the block table."""
+    case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=[2000, 77], kv_type=oracle.I8,
+                            page=64, seed=5, pool_slack=1.5)
+    out1 = run_case(case)
+    rng = np.random.default_rng(1)
+    perm = rng.permutation(case.num_blocks)  # new slot of old block i is perm[i]
+    k2 = np.empty_like(case.k)
+    v2 = np.empty_like(case.v)
+    ks2 = np.empty_like(case.k_scale)
+    vs2 = np.empty_like(case.v_scale)
+    k2[perm], v2[perm], ks2[perm], vs2[perm] = case.k, case.v, case.k_scale, case.v_scale
+    table2 = np.where(case.table >= 0, perm[np.maximum(case.table, 0)], -1).astype(np.int32)
+    case.k, case.v, case.k_scale, case.v_scale, case.table = k2, v2, ks2, vs2, table2
+    out2 = run_case(case)
+    assert np.array_equal(out1, out2)
