@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -101,6 +102,8 @@ Geometry geometry(const kvb_paged_args* a, int num_sms) {
     return g;
 }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 // Checks everything that can be checked without reading device data. Messages follow the
 // reference's std::invalid_argument texts where it has one.
 int check_static(const kvb_paged_args* a) {
@@ -120,12 +123,19 @@ int check_static(const kvb_paged_args* a) {
         if (!a->k || !a->v || !a->block_table) return fail(KVB_ERR_INVALID, "null k, v or block_table");
         if (a->num_blocks <= 0) return fail(KVB_ERR_INVALID, "num_blocks must be > 0 for a non-empty cache");
     }
+    if ((s.batch > 0) && (!aligned16(a->q) || !aligned16(a->out)))
+        return fail(KVB_ERR_INVALID, "q and out must be 16-byte aligned");
     if ((long long)s.batch * s.num_heads * s.head_dim > (1LL << 31))
         return fail(KVB_ERR_INVALID, "q/out larger than 2^31 elements");
     return KVB_OK;
 }
 
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+// Launch ids for the split-K arrival counters: distinct per launch within the process, high bit set
+// (never 0, never the bits of a small float a stale workspace could hold).
+unsigned next_launch_id() {
+    static std::atomic<unsigned> n{0};
+    return 0x80000000u | (n.fetch_add(1, std::memory_order_relaxed) & 0x7fffffffu);
+}
 
 // Encodes the tile map of one pool: rows of D elements, num_blocks * Hkv * page rows, boxes of
 // (128 bytes) x min(page, 64) rows, 128-byte swizzle.
@@ -167,7 +177,7 @@ int launch_paged(const kvb_paged_args* a, void* ws, cudaStream_t stream) {
     p.out = a->out;
     p.part_o = reinterpret_cast<float*>(wsb + w.o_off);
     p.part_ml = reinterpret_cast<float2*>(wsb + w.ml_off);
-    p.counters = reinterpret_cast<unsigned*>(wsb + w.counters_off);
+    p.counters = reinterpret_cast<unsigned long long*>(wsb + w.counters_off);
     p.error_flag = reinterpret_cast<unsigned*>(wsb + w.flag_off);
     p.B = s.batch;
     p.H = s.num_heads;
@@ -183,11 +193,13 @@ int launch_paged(const kvb_paged_args* a, void* ws, cudaStream_t stream) {
     p.max_parts = g.max_parts;
     p.num_blocks = a->num_blocks;
     p.q_scale = 1.4426950408889634f / std::sqrt(float(s.head_dim));
+    p.launch = next_launch_id();
 
     const long long rows = (long long)a->num_blocks * s.num_kv_heads * a->page_size;
     const bool mma_ok = a->max_len > 0 && kvb_mma_supported(a->kv_type, s.head_dim, a->page_size, g.qg) &&
                         rows < (1LL << 31) && aligned16(a->k) && aligned16(a->v);
-    if (a->kernel == KVB_KERNEL_MMA && !mma_ok)
+    // With max_len == 0 no kernel reads the cache; the CUDA-core kernel writes the zeros.
+    if (a->kernel == KVB_KERNEL_MMA && !mma_ok && a->max_len > 0)
         return fail(KVB_ERR_INVALID, "the tensor-core kernel does not support this shape, page size or dtype");
     LaunchInfo li{f.num_sms, stream};
     cudaError_t e;

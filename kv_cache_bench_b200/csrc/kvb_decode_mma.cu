@@ -30,8 +30,8 @@
 // Softmax. Scores are in log2 units (q is pre-scaled by log2(e)/sqrt(D)); per warp an online
 // max/sum per head; the accumulator is rescaled only when a row max grows. int8 scales are applied
 // to the scores (k) and folded into the probabilities (v). Tokens outside the partition are
-// masked by select; fp16 rows past the sequence end are zeroed in shared memory before PV so
-// stale or uninitialized pool slots cannot inject NaN through 0 * NaN.
+// masked by select; fp16 rows past the partition end are zeroed in shared memory before PV so
+// dead pool slots or stale rows cannot inject NaN through 0 * NaN (int8 values are always finite).
 //
 // Epilogue. The four warp states merge in shared memory; single-partition sequences write the
 // output directly, otherwise the partition goes to the workspace and the last CTA to finish a
@@ -48,7 +48,7 @@ using namespace kvb_dev;
 constexpr int NCW = 4;                      // consumer warps
 constexpr int MMA_THREADS = (NCW + 1) * 32;  // + producer warp
 constexpr int SUB_BYTES = KVB_CHUNK * 128;   // one 64-row x 128-byte swizzled tile
-constexpr int WIN = 256;                     // pages of block-table metadata per window
+constexpr int WIN = 64;                      // pages of block-table metadata per window
 constexpr float PV_PRESCALE_I8 = 1024.0f;    // keeps the low fp16 half of p * v_scale normal (int8)
 
 struct StageMeta {
@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
     __syncthreads();
     const int* prefix = nullptr;
     if (p.B <= KVB_PREFIX_MAX) {
-        build_unit_prefix(p, s_prefix, tid, MMA_THREADS, 1);
+        build_unit_prefix(p, s_prefix, reinterpret_cast<int*>(epi_o), tid, MMA_THREADS, 1);
         prefix = s_prefix;
     }
     const long long total = unit_total(p, prefix);
@@ -154,6 +154,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
             if (u.nparts == 0) continue;
             const int* bt = p.block_table + (size_t)u.b * p.max_blocks;
             const int nblk_live = (u.len + p.page - 1) / p.page;
+            const int unit_last = (u.t1 - 1) / p.page;  // last page this unit reads
             int w0 = -1;  // first page of the metadata window
             const int c0 = u.t0 / KVB_CHUNK, c1 = (u.t1 + KVB_CHUNK - 1) / KVB_CHUNK;
             for (int c = c0; c < c1; ++c) {
@@ -161,24 +162,31 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                 const int i_first = tok0 / p.page;
                 const int i_last = min((tok0 + KVB_CHUNK - 1) / p.page, nblk_live - 1);
                 if (w0 < 0 || i_first < w0 || i_last >= w0 + WIN) {
+                    // Block ids (and int8 scales) of the next WIN pages this unit reads, one page per
+                    // lane and pass: every lane's loads are independent, so a window costs about two
+                    // memory round trips.
                     __syncwarp();
                     w0 = i_first;
-                    for (int k = lane; k < WIN; k += 32) {
-                        const int i = w0 + k;
-                        int blk = -1;
+                    const int w_end = min(w0 + WIN, unit_last + 1);
+                    int blk[WIN / 32];
+#pragma unroll
+                    for (int r = 0; r < WIN / 32; ++r) {
+                        const int i = w0 + r * 32 + lane;
+                        blk[r] = i < w_end ? __ldg(bt + i) : -1;
+                    }
+#pragma unroll
+                    for (int r = 0; r < WIN / 32; ++r) {
+                        const int i = w0 + r * 32 + lane;
                         float ks = 0.f, vs = 0.f;
-                        if (i < nblk_live) {
-                            blk = __ldg(bt + i);
-                            if (blk < 0 || (long long)blk >= p.num_blocks) {
-                                blk = -2;  // refused
-                            } else if (KVT == 2) {
-                                ks = __ldg(p.k_scale + (size_t)blk * p.Hkv + u.kvh);
-                                vs = __ldg(p.v_scale + (size_t)blk * p.Hkv + u.kvh);
-                            }
+                        if (i < w_end && (blk[r] < 0 || (long long)blk[r] >= p.num_blocks)) {
+                            blk[r] = -2;  // refused
+                        } else if (KVT == 2 && i < w_end) {
+                            ks = __ldg(p.k_scale + (size_t)blk[r] * p.Hkv + u.kvh);
+                            vs = __ldg(p.v_scale + (size_t)blk[r] * p.Hkv + u.kvh);
                         }
-                        win_blk[k] = blk;
-                        win_ks[k] = ks;
-                        win_vs[k] = vs;
+                        win_blk[r * 32 + lane] = blk[r];
+                        win_ks[r * 32 + lane] = ks;
+                        win_vs[r * 32 + lane] = vs;
                     }
                     __syncwarp();
                 }
@@ -191,7 +199,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                     int bad = 0;
                     for (int nt = 0; nt < KVB_CHUNK / 8; ++nt) {
                         const int k = (tok0 + 8 * nt) / p.page - w0;
-                        const bool live = k + w0 < nblk_live;
+                        const bool live = k + w0 <= min(unit_last, nblk_live - 1);
                         m.ks[nt] = live ? win_ks[k] : 0.f;
                         m.vs[nt] = live ? win_vs[k] : 0.f;
                     }
@@ -200,7 +208,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                     uint32_t bytes = 0;
                     for (int j = 0; j < nbox; ++j) {
                         const int i = (tok0 + j * box_rows) / p.page;
-                        if (i >= nblk_live) break;
+                        if (i > unit_last) break;
                         if (win_blk[i - w0] < 0) bad = 1;
                         else bytes += 2u * NSUB * box_rows * 128u;
                     }
@@ -214,7 +222,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                         for (int j = 0; j < nbox; ++j) {
                             const int tok = tok0 + j * box_rows;
                             const int i = tok / p.page;
-                            if (i >= nblk_live) break;
+                            if (i > unit_last) break;
                             const int blk = win_blk[i - w0];
                             if (blk < 0) continue;
                             const int y = (blk * p.Hkv + u.kvh) * p.page + tok % p.page;
@@ -388,9 +396,10 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                     }
                     split_hi_lo(pv[0], pv[1], pa[2 * t2], pa[2 * t2 + 1]);
                 }
-                // ---- fp16 rows past the sequence end: zero them before they meet p = 0
-                if (KVT == 1 && tok_w + 16 > u.len) {
-                    const int first = max(0, u.len - tok_w);
+                // ---- fp16 rows past the partition end (dead pool slots, or pages this unit did not
+                // load, which hold stale data): zero them before they meet p = 0
+                if (KVT == 1 && tok_w + 16 > u.t1) {
+                    const int first = max(0, u.t1 - tok_w);
                     for (int idx = lane; idx < (16 - first) * 8 * NSUB; idx += 32) {
                         const int row = r_base + first + idx / (8 * NSUB);
                         const int rest = idx % (8 * NSUB);
@@ -464,7 +473,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
             merge_slots_and_store<D>(p, u, epi_o, epi_ml, NCW, g0, min(KVB_EPI_HEADS, u.nh - g0), o_scale, tid,
                                      NCW * 32);
         }
-        finish_partition<D>(p, u, tid, NCW * 32, 1, s_flag);
+        finish_partition<D>(p, u, tid, NCW * 32, 1, s_flag, epi_o, NCW * KVB_EPI_HEADS * D);
         named_barrier(1, NCW * 32);
     }
 }

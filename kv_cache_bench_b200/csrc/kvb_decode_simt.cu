@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(SIMT_THREADS) decode_simt_kernel(const DecodeP
     const int slot = tid >> 4;
     const int* prefix = nullptr;
     if (p.B <= KVB_PREFIX_MAX) {
-        build_unit_prefix(p, s_prefix, tid, SIMT_THREADS, 1);
+        build_unit_prefix(p, s_prefix, reinterpret_cast<int*>(s_slot_o), tid, SIMT_THREADS, 1);
         prefix = s_prefix;
     }
     UnitCursor cur{&p, prefix, (long long)blockIdx.x, unit_total(p, prefix)};
@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(SIMT_THREADS) decode_simt_kernel(const DecodeP
             merge_slots_and_store<D>(p, u, s_slot_o, s_slot_ml, SIMT_SLOTS, g0, min(KVB_EPI_HEADS, u.nh - g0),
                                      o_scale, tid, SIMT_THREADS);
         }
-        finish_partition<D>(p, u, tid, SIMT_THREADS, 1, &s_flag);
+        finish_partition<D>(p, u, tid, SIMT_THREADS, 1, &s_flag, s_slot_o, SIMT_SLOTS * KVB_EPI_HEADS * D);
         __syncthreads();
     }
 }

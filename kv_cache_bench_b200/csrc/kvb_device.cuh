@@ -273,9 +273,10 @@ struct UnitCursor {
 };
 
 // Fills prefix[0..B] with the running count of units per sequence (nhg * max(1, partitions)).
-// Called by `nthreads` threads (a multiple of 32) that then synchronize on barrier `bar_id`.
-__device__ __forceinline__ void build_unit_prefix(const DecodeParams& p, int* prefix, int tid, int nthreads,
-                                                  uint32_t bar_id) {
+// Called by `nthreads` threads (a multiple of 32, at most 1024) that then synchronize on barrier
+// `bar_id`; `scratch` holds nthreads ints of shared memory.
+__device__ __forceinline__ void build_unit_prefix(const DecodeParams& p, int* prefix, int* scratch, int tid,
+                                                  int nthreads, uint32_t bar_id) {
     // Each thread counts a contiguous slice, then warp 0 scans the slice totals.
     const int per = (p.B + nthreads - 1) / nthreads;
     const int s0 = min(p.B, tid * per), s1 = min(p.B, s0 + per);
@@ -285,24 +286,23 @@ __device__ __forceinline__ void build_unit_prefix(const DecodeParams& p, int* pr
         sum += p.nhg * max(1, seq_partitions(p, __ldg(p.seq_lens + b), &bad));
         prefix[b + 1] = sum;  // slice-local inclusive sums for now
     }
-    __shared__ int slice_total[KVB_MAX_THREADS];
-    slice_total[tid] = sum;
+    scratch[tid] = sum;
     named_barrier(bar_id, nthreads);
     if (tid < 32) {
         int carry = 0;
         for (int base = 0; base < nthreads; base += 32) {
-            int v = slice_total[base + tid];
+            int v = scratch[base + tid];
             int incl = v;
             for (int o = 1; o < 32; o <<= 1) {
                 const int n = __shfl_up_sync(0xffffffffu, incl, o);
                 if (tid >= o) incl += n;
             }
-            slice_total[base + tid] = carry + incl - v;  // exclusive offset of this slice
+            scratch[base + tid] = carry + incl - v;  // exclusive offset of this slice
             carry += __shfl_sync(0xffffffffu, incl, 31);
         }
     }
     named_barrier(bar_id, nthreads);
-    const int off = slice_total[tid];
+    const int off = scratch[tid];
     for (int b = s0; b < s1; ++b) prefix[b + 1] += off;
     if (tid == 0) prefix[0] = 0;
     named_barrier(bar_id, nthreads);
@@ -353,33 +353,93 @@ __device__ __forceinline__ void merge_slots_and_store(const DecodeParams& p, con
 
 // After every round of merge_slots_and_store for a multi-partition unit: counts the partition
 // in and, if it was the last one, merges all partitions of (b, head group) into `out`.
+//
+// The arrival counter of (b, head group) is a 64-bit word (launch id << 32 | arrivals). A value
+// from any other launch -- the previous one, or stale workspace contents left by a call with
+// another layout -- counts as zero arrivals, so the workspace never needs clearing between calls;
+// the last arrival writes 0 so that a replayed launch (same id, e.g. from a CUDA graph) starts over.
 template <int D>
 __device__ __forceinline__ void finish_partition(const DecodeParams& p, const Unit& u, int tid, int nthreads,
-                                                 uint32_t bar_id, int* s_flag) {
+                                                 uint32_t bar_id, int* s_flag, float* scratch, int scratch_floats) {
     if (u.nparts <= 1) return;
     __threadfence();
     named_barrier(bar_id, nthreads);
     if (tid == 0) {
-        unsigned* ctr = p.counters + (size_t)u.b * p.nhg + u.hg;
-        const unsigned prev = atomicAdd(ctr, 1u);
-        const int last = prev == unsigned(u.nparts - 1);
-        if (last) *ctr = 0u;  // ready for the next launch (stream order)
+        unsigned long long* ctr = p.counters + (size_t)u.b * p.nhg + u.hg;
+        const unsigned long long mine = (unsigned long long)p.launch << 32;
+        unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(ctr), seen;
+        unsigned arrived;
+        do {
+            seen = old;
+            arrived = (seen >> 32) == p.launch ? unsigned(seen) + 1u : 1u;
+            old = atomicCAS(ctr, seen, mine | arrived);
+        } while (old != seen);
+        const int last = arrived == unsigned(u.nparts);
+        if (last) atomicExch(ctr, 0ull);
         *s_flag = last;
     }
     named_barrier(bar_id, nthreads);
     if (!*s_flag) return;
     __threadfence();
+    const int np = u.nparts, warps = nthreads >> 5, lane = tid & 31;
+    if (u.nh * (np + 1) <= scratch_floats) {
+        // Weights w_i = L_i * 2^(M_i - max M) per head, one warp per head (all partitions of a head
+        // load in parallel across lanes), then out[d] = sum_i w_i o_i[d] / sum_i w_i with independent
+        // 16-byte loads of the partials.
+        float* w = scratch;               // [nh][np]
+        float* wsum = scratch + u.nh * np;  // [nh]
+        for (int g = tid >> 5; g < u.nh; g += warps) {
+            const size_t base = ((size_t)u.b * p.H + u.h0 + g) * p.max_parts;
+            float M = NEG_BIG;
+            for (int i = lane; i < np; i += 32) M = fmaxf(M, __ldcg(&p.part_ml[base + i].x));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            float L = 0.f;
+            for (int i = lane; i < np; i += 32) {
+                const float2 ml = __ldcg(&p.part_ml[base + i]);
+                const float wi = ml.y * exp2f(ml.x - M);
+                w[g * np + i] = wi;
+                L += wi;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+            if (lane == 0) wsum[g] = L;
+        }
+        named_barrier(bar_id, nthreads);
+        for (int idx = tid; idx < u.nh * (D / 4); idx += nthreads) {
+            const int g = idx / (D / 4), d4 = idx % (D / 4), h = u.h0 + g;
+            const float4* po = reinterpret_cast<const float4*>(p.part_o + ((size_t)u.b * p.H + h) * p.max_parts * D) + d4;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+            for (int i = 0; i < np; ++i) {
+                const float4 oi = __ldcg(po + (size_t)i * (D / 4));
+                const float wi = w[g * np + i];
+                acc.x = fmaf(wi, oi.x, acc.x);
+                acc.y = fmaf(wi, oi.y, acc.y);
+                acc.z = fmaf(wi, oi.z, acc.z);
+                acc.w = fmaf(wi, oi.w, acc.w);
+            }
+            const float inv = 1.f / wsum[g];
+            reinterpret_cast<float4*>(p.out + ((size_t)u.b * p.H + h) * D)[d4] =
+                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        }
+        named_barrier(bar_id, nthreads);  // the scratch is free again
+        return;
+    }
+    // Many partitions: one pass of online merging per output element.
     for (int idx = tid; idx < u.nh * D; idx += nthreads) {
         const int g = idx / D, d = idx % D, h = u.h0 + g;
         const size_t base = ((size_t)u.b * p.H + h) * p.max_parts;
-        float M = NEG_BIG;
-        for (int i = 0; i < u.nparts; ++i) M = fmaxf(M, __ldcg(&p.part_ml[base + i].x));
-        float L = 0.f, o = 0.f;
-        for (int i = 0; i < u.nparts; ++i) {
+        float M = NEG_BIG, L = 0.f, o = 0.f;
+#pragma unroll 8
+        for (int i = 0; i < np; ++i) {
             const float2 ml = __ldcg(&p.part_ml[base + i]);
-            const float w = ml.y * exp2f(ml.x - M);
-            L += w;
-            o += w * __ldcg(&p.part_o[(base + i) * D + d]);
+            const float oi = __ldcg(&p.part_o[(base + i) * D + d]);
+            const float Mn = fmaxf(M, ml.x);
+            const float a = exp2f(M - Mn), c = ml.y * exp2f(ml.x - Mn);
+            L = L * a + c;
+            o = o * a + c * oi;
+            M = Mn;
         }
         p.out[((size_t)u.b * p.H + h) * D + d] = o / L;
     }

@@ -17,9 +17,7 @@
 #define KVB_DEVERR_TIMEOUT 4u   // a bounded wait gave up
 
 // Sequences up to this batch size are enumerated through a prefix sum in shared memory.
-#define KVB_PREFIX_MAX 1024
-// Largest CTA of any decode kernel.
-#define KVB_MAX_THREADS 256
+#define KVB_PREFIX_MAX 256
 // Heads merged per epilogue round (bounds the epilogue's shared memory).
 #define KVB_EPI_HEADS 4
 // Tokens per TMA stage of the tensor-core kernel.
@@ -38,7 +36,7 @@ struct DecodeParams {
     // workspace
     float* part_o;           // [B][H][max_parts][D], partition outputs (normalized)
     float2* part_ml;         // [B][H][max_parts], (max in log2 units, sum)
-    unsigned* counters;      // [B][nhg], partitions finished per (sequence, head group)
+    unsigned long long* counters;  // [B][nhg]: (launch id << 32) | partitions finished
     unsigned* error_flag;    // KVB_DEVERR_* bits
     // shape
     int B, H, Hkv, G;
@@ -47,7 +45,8 @@ struct DecodeParams {
     int nhg;   // head groups per sequence = Hkv * gpk
     int page, max_blocks, max_len, part_tokens, max_parts;
     long long num_blocks;
-    float q_scale;  // log2(e) / sqrt(D): scores come out in log2 units
+    float q_scale;     // log2(e) / sqrt(D): scores come out in log2 units
+    unsigned launch;   // launch id (high bit set): tells this launch's counter values from stale ones
 };
 
 // Workspace layout (offsets in bytes), shared by the size query and the launcher.
@@ -61,7 +60,7 @@ inline WorkspaceLayout kvb_workspace_layout(int B, int H, int nhg, int max_parts
     WorkspaceLayout w;
     w.flag_off = 0;
     w.counters_off = 256;
-    w.ml_off = kvb_align_up(w.counters_off + sizeof(unsigned) * (size_t)B * nhg, 256);
+    w.ml_off = kvb_align_up(w.counters_off + sizeof(unsigned long long) * (size_t)B * nhg, 256);
     w.o_off = kvb_align_up(w.ml_off + sizeof(float) * 2 * (size_t)B * H * max_parts, 256);
     w.total = kvb_align_up(w.o_off + sizeof(float) * (size_t)B * H * max_parts * D, 256);
     return w;

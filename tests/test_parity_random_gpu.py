@@ -62,6 +62,9 @@ def test_random_case(name, H, Hkv, D, kv_type, page, lens, parts, extra):
     case = oracle.make_case(num_heads=H, num_kv_heads=Hkv, head_dim=D, lens=lens, kv_type=kv_type, page=page,
                             seed=zlib.crc32(name.encode()), **extra)
     ref = case.reference()
+    # The reference's 2e-5 is derived for |q| <= 8 (README "Tolerances": score error ~ |s| * 2^-24 *
+    # log2(D)); scores grow with q_amp, and so does the fp32 rounding of any kernel.
+    tol = TOL * max(1.0, extra.get("q_amp", 1.0) / 8.0)
     kernels = [kvb.Kernel.simt, kvb.Kernel.auto]
     if mma_ok(kv_type, D, page, H // Hkv):
         kernels.append(kvb.Kernel.mma)
@@ -73,15 +76,16 @@ def test_random_case(name, H, Hkv, D, kv_type, page, lens, parts, extra):
         for part in parts:
             out = run_case(case, part=part, kernel=kernel)
             err = oracle.max_abs_diff(out, ref)
-            if not err <= TOL:
+            if not err <= tol:
                 failures.append(f"kernel={kernel.name} part={part}: {err:.3g}")
             for b, L in enumerate(case.lens):
                 if L == 0 and np.any(out[b] != 0):
                     failures.append(f"kernel={kernel.name} part={part}: empty sequence {b} not 0")
     if H // Hkv > 1:  # per-query-head ablation
         out = run_case(case, share_kv=False)
-        if not oracle.max_abs_diff(out, ref) <= TOL:
-            failures.append("share_kv=0")
+        err = oracle.max_abs_diff(out, ref)
+        if not err <= tol:
+            failures.append(f"share_kv=0: {err:.3g}")
     assert not failures, "\n".join(failures)
 
 
