@@ -57,7 +57,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, default=3, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--dtype", choices=["f32", "f16", "i8"], default=None)
-    ap.add_argument("--kernel", choices=["auto", "simt", "mma"], default="auto")
+    ap.add_argument("--kernel", choices=["auto", "simt", "mma", "umma"], default="auto")
     ap.add_argument("--part", type=int, default=None, help="override the split-K partition size")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -369,7 +369,8 @@ def main():
     live_est = float(sum(w["lens"])) * w["Hkv"] * w["D"] * 2 * elem / (world if w["shard"] != "replica" else 1)
     copies = max(1, min(64, math.ceil(4 * l2 / max(live_est, 1)))) if w["shard"] == "replica" else 1
     s = Shard(torch, w, rank, world, device, copies)
-    kernel = {"auto": kvb.Kernel.auto, "simt": kvb.Kernel.simt, "mma": kvb.Kernel.mma}[args.kernel]
+    kernel = {"auto": kvb.Kernel.auto, "simt": kvb.Kernel.simt, "mma": kvb.Kernel.mma,
+              "umma": kvb.Kernel.umma}[args.kernel]
     part = w["part"] if args.part is None else args.part
     dec = PagedDecoder(device)
     stream = torch.cuda.Stream(device)

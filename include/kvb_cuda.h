@@ -47,10 +47,14 @@ enum {
 /* Storage type of the K/V pools: src/metal_attn.hpp:37 (KvType). */
 enum { KVB_F32 = 0, KVB_F16 = 1, KVB_I8 = 2 };
 
-/* Kernel selection for kvb_paged_args.kernel. AUTO picks the TMA + tensor-core kernel when the
- * shape allows it (fp16/int8, page size a multiple of 8 dividing or divided by 64, at most 8
- * query heads per KV head group) and the CUDA-core kernel otherwise. */
-enum { KVB_KERNEL_AUTO = 0, KVB_KERNEL_SIMT = 1, KVB_KERNEL_MMA = 2 };
+/* Kernel selection for kvb_paged_args.kernel. AUTO picks, in order, the first kernel that supports
+ * the call:
+ *   UMMA  tcgen05 tensor cores + TMA + tensor memory: fp16/int8, head dim 128, page size 8, 16, 32,
+ *         64, 128 or 256, at most 8 query heads per KV-head group;
+ *   MMA   mma.sync tensor cores + TMA: fp16/int8 with 128- or 256-byte rows, page size 8, 16, 32,
+ *         64, 128 or 256, at most 8 query heads per group;
+ *   SIMT  CUDA cores: every storage type, page size, head dim and group size. */
+enum { KVB_KERNEL_AUTO = 0, KVB_KERNEL_SIMT = 1, KVB_KERNEL_MMA = 2, KVB_KERNEL_UMMA = 3 };
 
 /* src/reference.hpp:17-23 (Shape). */
 typedef struct kvb_shape {

@@ -149,6 +149,7 @@ class Kernel(enum.IntEnum):
     auto = 0
     simt = 1
     mma = 2
+    umma = 3
 
 
 def name(t: KvType) -> str:

@@ -75,9 +75,32 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // ---- geometry of a paged call ------------------------------------------------------------------
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 struct Geometry {
     int G, qg, gpk, nhg, part, max_parts;
+    int kernel;  // KVB_KERNEL_SIMT / MMA / UMMA actually used
 };
+
+bool pool_rows_fit(const kvb_paged_args* a) {
+    return (long long)a->num_blocks * a->shape.num_kv_heads * a->page_size < (1LL << 31);
+}
+
+// The kernel a call runs: the requested one, or for AUTO the first of UMMA, MMA, SIMT that supports
+// the shape. Returns -1 when a specific tensor-core kernel was requested for a shape it cannot run.
+int choose_kernel(const kvb_paged_args* a, int qg) {
+    const int D = a->shape.head_dim;
+    const bool tma_ok = a->max_len > 0 && pool_rows_fit(a) && aligned16(a->k) && aligned16(a->v);
+    const bool umma = tma_ok && kvb_umma_supported(a->kv_type, D, a->page_size, qg);
+    const bool mma = tma_ok && kvb_mma_supported(a->kv_type, D, a->page_size, qg);
+    if (a->max_len == 0) return KVB_KERNEL_SIMT;  // nothing to read: the CUDA-core kernel writes the zeros
+    switch (a->kernel) {
+    case KVB_KERNEL_SIMT: return KVB_KERNEL_SIMT;
+    case KVB_KERNEL_MMA: return mma ? KVB_KERNEL_MMA : -1;
+    case KVB_KERNEL_UMMA: return umma ? KVB_KERNEL_UMMA : -1;
+    default: return umma ? KVB_KERNEL_UMMA : mma ? KVB_KERNEL_MMA : KVB_KERNEL_SIMT;
+    }
+}
 
 Geometry geometry(const kvb_paged_args* a, int num_sms) {
     Geometry g;
@@ -86,23 +109,27 @@ Geometry geometry(const kvb_paged_args* a, int num_sms) {
     g.qg = a->share_kv ? std::min(g.G, 8) : 1;
     g.gpk = (g.G + g.qg - 1) / g.qg;
     g.nhg = s.num_kv_heads * g.gpk;
+    g.kernel = choose_kernel(a, g.qg);
     if (a->part_tokens > 0) {
         g.part = a->part_tokens;
     } else {
-        // B200 rule: enough partitions per (sequence, head group) that the units of the longest
-        // sequence fill every CTA slot once (two CTAs per SM), and no partition longer than 2048
-        // tokens (bounded per-unit work for load balance); rounded up to whole 64-token chunks.
+        // B200 rule: split each (sequence, head group) into as many partitions as keep all units in one
+        // wave of the kernel's CTA slots (one CTA per SM for the tcgen05 kernel, two otherwise), and into
+        // partitions of at most part_max tokens (bounded per-unit work balances ragged batches); rounded
+        // up to whole chunks of the kernel.
+        const bool umma = g.kernel == KVB_KERNEL_UMMA;
+        const long long chunk = umma ? 128 : KVB_CHUNK;
+        const long long part_max = umma ? 4096 : 2048;
         const long long S = std::max<long long>(1, (long long)s.batch * g.nhg);
-        const long long slots = 2LL * std::max(1, num_sms);
-        const long long n = std::max<long long>({1, (slots + S - 1) / S, ((long long)a->max_len + 2047) / 2048});
+        const long long slots = (umma ? 1LL : 2LL) * std::max(1, num_sms);
+        long long n = S < slots ? std::max<long long>(1, slots / S) : 1;
+        n = std::max<long long>(n, ((long long)a->max_len + part_max - 1) / part_max);
         const long long per = ((long long)a->max_len + n - 1) / n;
-        g.part = (int)std::max<long long>(KVB_CHUNK, (per + KVB_CHUNK - 1) / KVB_CHUNK * KVB_CHUNK);
+        g.part = (int)std::max<long long>(chunk, (per + chunk - 1) / chunk * chunk);
     }
     g.max_parts = std::max(1, (int)(((long long)a->max_len + g.part - 1) / g.part));
     return g;
 }
-
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Checks everything that can be checked without reading device data. Messages follow the
 // reference's std::invalid_argument texts where it has one.
@@ -117,7 +144,7 @@ int check_static(const kvb_paged_args* a) {
     if (s.head_dim != 64 && s.head_dim != 128) return fail(KVB_ERR_INVALID, "head_dim must be 64 or 128");
     if (s.num_heads % s.num_kv_heads != 0) return fail(KVB_ERR_INVALID, "H % Hkv != 0");
     if (a->max_blocks < 0) return fail(KVB_ERR_INVALID, "max_blocks < 0");
-    if (a->kernel < KVB_KERNEL_AUTO || a->kernel > KVB_KERNEL_MMA) return fail(KVB_ERR_INVALID, "unknown kernel");
+    if (a->kernel < KVB_KERNEL_AUTO || a->kernel > KVB_KERNEL_UMMA) return fail(KVB_ERR_INVALID, "unknown kernel");
     if (s.batch > 0 && (!a->q || !a->out || !a->seq_lens)) return fail(KVB_ERR_INVALID, "null q, out or seq_lens");
     if (s.batch > 0 && a->max_len > 0) {
         if (!a->k || !a->v || !a->block_table) return fail(KVB_ERR_INVALID, "null k, v or block_table");
@@ -139,14 +166,14 @@ unsigned next_launch_id() {
 
 // Encodes the tile map of one pool: rows of D elements, num_blocks * Hkv * page rows, boxes of
 // (128 bytes) x min(page, 64) rows, 128-byte swizzle.
-int encode_pool_map(CUtensorMap* map, const void* pool, const kvb_paged_args* a) {
+int encode_pool_map(CUtensorMap* map, const void* pool, const kvb_paged_args* a, int box_rows_max) {
     PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
     if (!enc) return fail(KVB_ERR_DEVICE, "cuTensorMapEncodeTiled is unavailable");
     const size_t es = elem_size(a->kv_type);
     const cuuint64_t rows = (cuuint64_t)a->num_blocks * a->shape.num_kv_heads * a->page_size;
     const cuuint64_t dims[2] = {(cuuint64_t)a->shape.head_dim, rows};
     const cuuint64_t strides[1] = {(cuuint64_t)a->shape.head_dim * es};
-    const cuuint32_t box[2] = {(cuuint32_t)(128 / es), (cuuint32_t)std::min(a->page_size, KVB_CHUNK)};
+    const cuuint32_t box[2] = {(cuuint32_t)(128 / es), (cuuint32_t)std::min(a->page_size, box_rows_max)};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = enc(map, a->kv_type == KVB_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
                            2, const_cast<void*>(pool), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -195,19 +222,17 @@ int launch_paged(const kvb_paged_args* a, void* ws, cudaStream_t stream) {
     p.q_scale = 1.4426950408889634f / std::sqrt(float(s.head_dim));
     p.launch = next_launch_id();
 
-    const long long rows = (long long)a->num_blocks * s.num_kv_heads * a->page_size;
-    const bool mma_ok = a->max_len > 0 && kvb_mma_supported(a->kv_type, s.head_dim, a->page_size, g.qg) &&
-                        rows < (1LL << 31) && aligned16(a->k) && aligned16(a->v);
-    // With max_len == 0 no kernel reads the cache; the CUDA-core kernel writes the zeros.
-    if (a->kernel == KVB_KERNEL_MMA && !mma_ok && a->max_len > 0)
-        return fail(KVB_ERR_INVALID, "the tensor-core kernel does not support this shape, page size or dtype");
+    if (g.kernel < 0)
+        return fail(KVB_ERR_INVALID, "the requested tensor-core kernel does not support this shape, page size or dtype");
     LaunchInfo li{f.num_sms, stream};
     cudaError_t e;
-    if (mma_ok && a->kernel != KVB_KERNEL_SIMT) {
+    if (g.kernel == KVB_KERNEL_UMMA || g.kernel == KVB_KERNEL_MMA) {
+        const int box_rows = g.kernel == KVB_KERNEL_UMMA ? 128 : KVB_CHUNK;
         CUtensorMap tk, tv;
-        if (int rc = encode_pool_map(&tk, a->k, a)) return rc;
-        if (int rc = encode_pool_map(&tv, a->v, a)) return rc;
-        e = kvb_launch_decode_mma(p, a->kv_type, s.head_dim, &tk, &tv, li);
+        if (int rc = encode_pool_map(&tk, a->k, a, box_rows)) return rc;
+        if (int rc = encode_pool_map(&tv, a->v, a, box_rows)) return rc;
+        e = g.kernel == KVB_KERNEL_UMMA ? kvb_launch_decode_umma(p, a->kv_type, s.head_dim, &tk, &tv, li)
+                                         : kvb_launch_decode_mma(p, a->kv_type, s.head_dim, &tk, &tv, li);
     } else {
         e = kvb_launch_decode_simt(p, a->kv_type, s.head_dim, li);
     }

@@ -1,6 +1,6 @@
-// Paged split-K decode for fp16 and int8 caches on B200: TMA-staged pages and tensor-core
-// contractions. This is the kernel the common shapes run (page size a multiple of 8 that divides
-// or is divided by 64, rows of 128 or 256 bytes, up to 8 query heads per KV-head group).
+// Paged split-K decode for fp16 and int8 caches on B200: TMA-staged pages and mma.sync tensor-core
+// contractions (page size a power of two from 8 to 256, rows of 128 or 256 bytes, up to 8 query
+// heads per KV-head group). It serves the shapes the tcgen05 kernel does not (head dim 64).
 //
 // Computes what the reference's paged_decode + paged_reduce compute (src/kernels.metal:43-147):
 // per (sequence, KV-head group, partition) an fp32 online softmax over the partition's tokens,
@@ -150,17 +150,18 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
         int stage = 0;
         uint32_t phase = 0;
         const int box_rows = p.page < KVB_CHUNK ? p.page : KVB_CHUNK;
+        const int nbox = KVB_CHUNK / box_rows;
+        const int lp = __ffs(p.page) - 1;  // pages are powers of two on this path
         while (cur.advance(u)) {
             if (u.nparts == 0) continue;
             const int* bt = p.block_table + (size_t)u.b * p.max_blocks;
-            const int nblk_live = (u.len + p.page - 1) / p.page;
-            const int unit_last = (u.t1 - 1) / p.page;  // last page this unit reads
+            const int unit_last = (u.t1 - 1) >> lp;  // last page this unit reads
             int w0 = -1;  // first page of the metadata window
             const int c0 = u.t0 / KVB_CHUNK, c1 = (u.t1 + KVB_CHUNK - 1) / KVB_CHUNK;
             for (int c = c0; c < c1; ++c) {
                 const int tok0 = c * KVB_CHUNK;
-                const int i_first = tok0 / p.page;
-                const int i_last = min((tok0 + KVB_CHUNK - 1) / p.page, nblk_live - 1);
+                const int i_first = tok0 >> lp;
+                const int i_last = min((tok0 + KVB_CHUNK - 1) >> lp, unit_last);
                 if (w0 < 0 || i_first < w0 || i_last >= w0 + WIN) {
                     // Block ids (and int8 scales) of the next WIN pages this unit reads, one page per
                     // lane and pass: every lane's loads are independent, so a window costs about two
@@ -190,50 +191,54 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
                     }
                     __syncwarp();
                 }
+                // Lane t < 8 fills the metadata of 8-token group t, lane j < nbox owns box j; lane 0 arms
+                // the barrier with the byte count, then every owning lane issues its own tile loads.
+                if (lane == 0 && !*s_abort && !mbar_wait_bounded(&empty[stage], phase ^ 1u, s_abort)) {
+                    *s_abort = 1;
+                    raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
+                }
+                __syncwarp();
+                StageMeta& m = meta[stage];
+                if (lane < KVB_CHUNK / 8) {
+                    const int i = (tok0 + 8 * lane) >> lp;
+                    const bool live = i <= unit_last;
+                    m.ks[lane] = live ? win_ks[i - w0] : 0.f;
+                    m.vs[lane] = live ? win_vs[i - w0] : 0.f;
+                }
+                int blk = -1;
+                bool mine = false, refused = false;
+                if (lane < nbox) {
+                    const int i = (tok0 + lane * box_rows) >> lp;
+                    if (i <= unit_last) {
+                        blk = win_blk[i - w0];
+                        refused = blk < 0;
+                        mine = !refused;
+                    }
+                }
+                const unsigned owned = __ballot_sync(0xffffffffu, mine);
+                const bool bad = __any_sync(0xffffffffu, refused);
+                const uint32_t bytes = uint32_t(__popc(owned)) * 2u * NSUB * box_rows * 128u;
+                const bool abort_now = *s_abort;
                 if (lane == 0) {
-                    if (!*s_abort && !mbar_wait_bounded(&empty[stage], phase ^ 1u, s_abort)) {
-                        *s_abort = 1;
-                        raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
-                    }
-                    StageMeta& m = meta[stage];
-                    int bad = 0;
-                    for (int nt = 0; nt < KVB_CHUNK / 8; ++nt) {
-                        const int k = (tok0 + 8 * nt) / p.page - w0;
-                        const bool live = k + w0 <= min(unit_last, nblk_live - 1);
-                        m.ks[nt] = live ? win_ks[k] : 0.f;
-                        m.vs[nt] = live ? win_vs[k] : 0.f;
-                    }
-                    // boxes of this chunk: one per page (page <= 64) or one 64-row slice of a page
-                    const int nbox = KVB_CHUNK / box_rows;
-                    uint32_t bytes = 0;
-                    for (int j = 0; j < nbox; ++j) {
-                        const int i = (tok0 + j * box_rows) / p.page;
-                        if (i > unit_last) break;
-                        if (win_blk[i - w0] < 0) bad = 1;
-                        else bytes += 2u * NSUB * box_rows * 128u;
-                    }
                     m.bad = bad;
                     if (bad) raise_error(p.error_flag, KVB_DEVERR_BLOCK);
-                    if (*s_abort || bytes == 0) {
-                        mbar_arrive(&full[stage]);  // nothing in flight: complete the phase directly
-                    } else {
-                        mbar_arrive_expect_tx(&full[stage], bytes);
-                        const uint32_t sbase = ring + stage * C::STAGE_BYTES;
-                        for (int j = 0; j < nbox; ++j) {
-                            const int tok = tok0 + j * box_rows;
-                            const int i = tok / p.page;
-                            if (i > unit_last) break;
-                            const int blk = win_blk[i - w0];
-                            if (blk < 0) continue;
-                            const int y = (blk * p.Hkv + u.kvh) * p.page + tok % p.page;
-                            for (int sb = 0; sb < NSUB; ++sb) {
-                                const int x = sb * (128 / C::ELEM);
-                                const uint32_t off = sb * SUB_BYTES + j * box_rows * 128;
-                                tma_load_2d(smem + (sbase - ring) + off, &tmk, &full[stage], x, y, policy);
-                                tma_load_2d(smem + (sbase - ring) + NSUB * SUB_BYTES + off, &tmv, &full[stage], x,
-                                            y, policy);
-                            }
-                        }
+                }
+                __syncwarp();  // the metadata writes of every lane happen before the arrive below
+                if (lane == 0) {
+                    if (abort_now || bytes == 0) mbar_arrive(&full[stage]);
+                    else mbar_arrive_expect_tx(&full[stage], bytes);
+                }
+                __syncwarp();
+                if (mine && !abort_now) {
+                    const int tok = tok0 + lane * box_rows;
+                    const int y = (blk * p.Hkv + u.kvh) * p.page + (tok & (p.page - 1));
+                    uint8_t* stg = smem + stage * C::STAGE_BYTES;
+#pragma unroll
+                    for (int sb = 0; sb < NSUB; ++sb) {
+                        const int x = sb * (128 / C::ELEM);
+                        const uint32_t off = sb * SUB_BYTES + lane * box_rows * 128;
+                        tma_load_2d(stg + off, &tmk, &full[stage], x, y, policy);
+                        tma_load_2d(stg + NSUB * SUB_BYTES + off, &tmv, &full[stage], x, y, policy);
                     }
                 }
                 __syncwarp();
@@ -512,8 +517,7 @@ bool kvb_mma_supported(int kv_type, int D, int page, int qg) {
     const int row_bytes = D * (kv_type == 1 ? 2 : 1);
     if (kv_type != 1 && kv_type != 2) return false;
     if (row_bytes != 128 && row_bytes != 256) return false;
-    if (page % 8 != 0 || page > 256) return false;
-    if (!(KVB_CHUNK % page == 0 || page % KVB_CHUNK == 0)) return false;
+    if (page < 8 || page > 256 || (page & (page - 1)) != 0) return false;  // 8, 16, ..., 256
     return qg >= 1 && qg <= 8;
 }
 

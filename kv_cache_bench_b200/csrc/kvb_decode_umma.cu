@@ -1,0 +1,832 @@
+// Paged split-K decode on B200 with tcgen05 (UMMA) tensor cores, TMA and tensor memory.
+//
+// Computes what the reference's paged_decode + paged_reduce compute (src/kernels.metal:43-147):
+// per (sequence, KV-head group, partition) an fp32-accurate online softmax over the partition's
+// tokens, then a weighted merge of the partitions. Shapes: head dim 128, fp16 or int8 pools, page
+// size 8, 16, 32, 64, 128 or 256, up to 8 query heads per KV-head group.
+//
+// One CTA per SM, warp-specialized:
+//   warp 0      TMA producer: for each 128-token chunk, 2-D tile loads of the K and V rows of every
+//               page in the chunk (128-byte swizzle) into a ring of shared-memory stages.
+//   warp 1      MMA issuer (one thread): per chunk
+//                 S^T[128 tokens x N] = K[128 x 128] . Qhat^T[128 x N]      (tensor memory)
+//                 O^T[128 dims x N]   = V^T[128 x 128 tokens] . Phat^T       (tensor memory)
+//               reading K (K-major) and V (MN-major, the transposed view of the same TMA tile)
+//               straight from the stage. tcgen05.commit releases the stage and signals the softmax.
+//   warps 2-5   softmax and accumulation (128 threads, one per tensor-memory lane): thread t reads
+//               token t's scores, the four warps agree on the chunk max per head, write Phat^T to
+//               shared memory, and after the PV product thread d folds O^T row d into registers.
+//
+// Exactness. The operands are exact in the MMA's input type, so the contraction is exact up to the
+// accumulator:
+//   int8 (kind::i8, int32 accumulate): K and V are the stored int8 values. q (per head) and the
+//     probabilities (per chunk) are integers below 2^30 written as four signed 8-bit limbs,
+//     x = ((l0*256 + l1)*256 + l2)*256 + l3, so S and O come out as four exact int32 partial
+//     products recombined in fp32. The int8 scales are applied outside the MMA: k_scale to the
+//     scores, v_scale folded into the probability integers (relative to the chunk's largest scale).
+//   fp16 (kind::f16, fp32 accumulate): K and V are the stored halves; q and p are split as
+//     fp16(x) + fp16(x - fp16(x)) (about 22 significant bits), q prescaled per head by a power of two.
+// N = (limbs or halves) x (query heads, padded): int8 4 x {1,2,4,8} -> 8..32, fp16 2 x {4,8} -> 8, 16.
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include "kvb_device.cuh"
+
+namespace {
+
+using namespace kvb_dev;
+
+constexpr int UM_CHUNK = 128;         // tokens per stage = MMA M for QK^T
+constexpr int UM_THREADS = 10 * 32;   // producer, MMA, two groups of 4 softmax warps
+constexpr int UM_SOFT = 128;          // threads of one softmax group
+constexpr int UM_D = 128;             // head dim
+constexpr int TILE = UM_CHUNK * 128;  // bytes of one [128 rows][128 B] swizzled tile
+constexpr int UM_WIN = 64;            // pages of block-table metadata per window
+constexpr int UM_NT = UM_CHUNK / 8;   // 8-token groups per chunk (the smallest page)
+
+// ---- tcgen05 wrappers -----------------------------------------------------------------------------
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_alloc(uint32_t* smem_dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tc_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Arrives on `bar` once every tcgen05.mma this thread issued before has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+template <int KIND>  // 1: kind::f16, 2: kind::i8
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    if constexpr (KIND == 1) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
+            : "memory");
+    }
+}
+
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 8 consecutive 32-bit tensor-memory columns of this thread's lane.
+__device__ __forceinline__ void tc_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+
+// Shared-memory matrix descriptor: 128-byte swizzle, 1024-byte atoms (8 rows of 128 B).
+// lbo / sbo in bytes (leading: stride between 128-byte column groups of an MN-major operand;
+// stride: between 8-row groups).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+    d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor: D format (1 = f32, 2 = s32), A and B format (kind::f16: 0 = f16; kind::i8:
+// 0 = unsigned, 1 = signed 8-bit), A/B major (0 = K-major, 1 = MN-major), N >> 3, M >> 4.
+__host__ __device__ constexpr uint32_t instr_desc(uint32_t dfmt, uint32_t afmt, uint32_t bfmt, uint32_t a_mn,
+                                                  uint32_t b_mn, uint32_t N, uint32_t M) {
+    return (dfmt << 4) | (afmt << 7) | (bfmt << 10) | (a_mn << 15) | (b_mn << 16) | ((N >> 3) << 17) |
+           ((M >> 4) << 24);
+}
+
+// Byte offset of (row, byte column) in a [rows][128 B] tile with the 128-byte swizzle (1024-aligned).
+__device__ __forceinline__ uint32_t swz_off(int row, int col) {
+    return row * 128 + ((((col >> 4) ^ row) & 7) << 4) + (col & 15);
+}
+
+// Splits a non-negative or signed integer |x| < 2^30 into four signed 8-bit limbs, high first.
+__device__ __forceinline__ void limbs4(int x, int8_t (&l)[4]) {
+#pragma unroll
+    for (int i = 3; i > 0; --i) {
+        const int lo = ((x + 128) & 255) - 128;
+        l[i] = (int8_t)lo;
+        x = (x - lo) >> 8;
+    }
+    l[0] = (int8_t)x;
+}
+
+struct UStageMeta {
+    float ks[UM_NT];  // K scale of each 8-token group (int8)
+    float vs[UM_NT];
+    float vsmax;      // largest V scale of the chunk
+    int bad;          // a block id of this chunk was refused
+    int pad[2];
+};
+
+template <int KVT>
+struct UCfg {
+    static constexpr int NSUB = KVT == 1 ? 2 : 1;             // 128-byte column slices of a row
+    static constexpr int STAGE = 2 * NSUB * TILE;              // K tiles, then V tiles
+    static constexpr int STAGES = KVT == 1 ? 3 : 5;
+    static constexpr int NMAX = KVT == 1 ? 16 : 32;            // MMA N (rows of Qhat / Phat)
+    static constexpr int QBUF = NMAX * 128 * NSUB;             // one Qhat^T buffer ([N][128 B] per slice)
+    static constexpr int PBUF = NMAX * 128 * NSUB;             // one Phat^T buffer
+    static constexpr size_t RING = size_t(STAGES) * STAGE;
+    static constexpr size_t Q_OFF = RING;                      // 2 Qhat buffers (1024-aligned)
+    static constexpr size_t P_OFF = Q_OFF + 2 * QBUF;          // 2 Phat buffers
+    static constexpr size_t META_OFF = P_OFF + 2 * PBUF;
+    static constexpr size_t BAR_OFF = META_OFF + STAGES * sizeof(UStageMeta);
+    static constexpr int NBARS = 2 * STAGES + 2 * 6;           // full/empty + q_full/q_free/s_full/s_free/p_full/o_full x2
+    static constexpr size_t RED_OFF = kvb_align_up(BAR_OFF + NBARS * sizeof(uint64_t), 16);
+    static constexpr size_t RED_FLOATS = 2 * 128;              // per group: cross-warp reductions [warp][head] x 4 uses
+    static constexpr size_t WIN_OFF = RED_OFF + RED_FLOATS * sizeof(float);
+    static constexpr size_t PREFIX_OFF = WIN_OFF + 3 * sizeof(int) * UM_WIN;
+    static constexpr size_t SCRATCH_OFF = kvb_align_up(PREFIX_OFF + sizeof(int) * (KVB_PREFIX_MAX + 1), 16);
+    static constexpr size_t SCRATCH_FLOATS = 2048;             // final merge weights, prefix scan
+    static constexpr size_t XBUF_OFF = SCRATCH_OFF + SCRATCH_FLOATS * sizeof(float);
+    static constexpr size_t XBUF_FLOATS = 8 * 128 + 2 * 8 + 4;  // group 1's O rows, max, sums, bad flag
+    static constexpr size_t MISC_OFF = kvb_align_up(XBUF_OFF + XBUF_FLOATS * sizeof(float), 64);
+    static constexpr size_t SMEM = MISC_OFF + 64 + 1024;
+};
+
+static_assert(UCfg<1>::SMEM <= 227 * 1024 && UCfg<2>::SMEM <= 227 * 1024, "shared memory budget");
+static_assert(UCfg<1>::BAR_OFF % 8 == 0 && UCfg<2>::BAR_OFF % 8 == 0, "mbarrier alignment");
+static_assert(UCfg<1>::MISC_OFF % 64 == 0 && UCfg<2>::MISC_OFF % 64 == 0, "mbarrier alignment");
+static_assert(UCfg<1>::Q_OFF % 1024 == 0 && UCfg<1>::P_OFF % 1024 == 0 && UCfg<2>::P_OFF % 1024 == 0,
+              "swizzled operands need 1024-byte alignment");
+
+template <int KVT, int QGP>  // QGP: query heads per group, padded to 1, 2, 4 or 8
+__global__ void __launch_bounds__(UM_THREADS, 1)
+    decode_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                       const DecodeParams p) {
+    using C = UCfg<KVT>;
+    constexpr int NSUB = C::NSUB, STAGES = C::STAGES;
+    constexpr int qgp = QGP;
+    constexpr int RPH = KVT == 1 ? 2 : 4;  // rows of Qhat/Phat per head (halves or limbs)
+    constexpr int N = RPH * qgp < 8 ? 8 : RPH * qgp;  // MMA N
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sbase = smem_u32(smem);
+    UStageMeta* meta = reinterpret_cast<UStageMeta*>(smem + C::META_OFF);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + STAGES;
+    uint64_t* q_full = bars + 2 * STAGES;  // [2] Qhat^T written (softmax -> MMA)
+    uint64_t* q_free = q_full + 2;         // [2] QK^T of the unit done (MMA -> softmax)
+    uint64_t* s_full = q_full + 4;         // [2] S^T ready (MMA -> softmax)
+    uint64_t* s_free = q_full + 6;         // [2] S^T read (softmax -> MMA)
+    uint64_t* p_full = q_full + 8;         // [2] Phat^T written (softmax -> MMA)
+    uint64_t* o_full = q_full + 10;        // [2] O^T ready; also: O^T read (softmax -> MMA) via o_free below
+    float* red = reinterpret_cast<float*>(smem + C::RED_OFF);
+    int* win_blk = reinterpret_cast<int*>(smem + C::WIN_OFF);
+    float* win_ks = reinterpret_cast<float*>(win_blk + UM_WIN);
+    float* win_vs = win_ks + UM_WIN;
+    int* s_prefix = reinterpret_cast<int*>(smem + C::PREFIX_OFF);
+    float* scratch = reinterpret_cast<float*>(smem + C::SCRATCH_OFF);
+    float* xbuf = reinterpret_cast<float*>(smem + C::XBUF_OFF);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::MISC_OFF);
+    int* s_flag = reinterpret_cast<int*>(smem + C::MISC_OFF + 8);
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF + 16);
+    uint64_t* o_free = reinterpret_cast<uint64_t*>(smem + C::MISC_OFF + 32);  // [2] O^T read (softmax -> MMA)
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // Zero the ring (rows never loaded must hold finite values), set up barriers, allocate TMEM.
+    for (int i = tid; i < int(C::RING / 16); i += UM_THREADS) sts128_zero(sbase + 16 * i);
+    for (int i = tid; i < int((2 * C::QBUF + 2 * C::PBUF) / 16); i += UM_THREADS)
+        sts128_zero(sbase + uint32_t(C::Q_OFF) + 16 * i);
+    fence_proxy_async_smem();
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&q_full[i], UM_SOFT / 32);
+            mbar_init(&q_free[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_free[i], UM_SOFT / 32);
+            mbar_init(&p_full[i], UM_SOFT / 32);
+            mbar_init(&o_full[i], 1);
+            mbar_init(&o_free[i], UM_SOFT / 32);
+        }
+        *s_abort = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 1) {
+        tc_alloc(s_tmem, 128);
+        tc_relinquish();
+    }
+    if (tid == 0) {
+        prefetch_tensormap(&tmk);
+        prefetch_tensormap(&tmv);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *s_tmem;
+    // tensor-memory columns: S^T buffers at 0 and 32, O^T buffers at 64 and 96
+    const int* prefix = nullptr;
+    if (p.B <= KVB_PREFIX_MAX) {
+        build_unit_prefix(p, s_prefix, reinterpret_cast<int*>(scratch), tid, UM_THREADS, 1);
+        prefix = s_prefix;
+    }
+    const long long total = unit_total(p, prefix);
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        const uint64_t policy = l2_evict_first_policy();
+        UnitCursor cur{&p, prefix, (long long)blockIdx.x, total};
+        Unit u;
+        int stage = 0;
+        uint32_t phase = 0;
+        const int box_rows = p.page < UM_CHUNK ? p.page : UM_CHUNK;
+        const int nbox = UM_CHUNK / box_rows;
+        const int lp = __ffs(p.page) - 1;  // pages are powers of two on this path
+        while (cur.advance(u)) {
+            if (u.nparts == 0) continue;
+            const int* bt = p.block_table + (size_t)u.b * p.max_blocks;
+            const int unit_last = (u.t1 - 1) >> lp;
+            int w0 = -1;
+            const int c0 = u.t0 / UM_CHUNK, c1 = (u.t1 + UM_CHUNK - 1) / UM_CHUNK;
+            for (int c = c0; c < c1; ++c) {
+                const int tok0 = c * UM_CHUNK;
+                const int i_first = tok0 >> lp;
+                const int i_last = min((tok0 + UM_CHUNK - 1) >> lp, unit_last);
+                if (w0 < 0 || i_first < w0 || i_last >= w0 + UM_WIN) {
+                    __syncwarp();
+                    w0 = i_first;
+                    const int w_end = min(w0 + UM_WIN, unit_last + 1);
+                    int blk[UM_WIN / 32];
+#pragma unroll
+                    for (int r = 0; r < UM_WIN / 32; ++r) {
+                        const int i = w0 + r * 32 + lane;
+                        blk[r] = i < w_end ? __ldg(bt + i) : -1;
+                    }
+#pragma unroll
+                    for (int r = 0; r < UM_WIN / 32; ++r) {
+                        const int i = w0 + r * 32 + lane;
+                        float ks = 0.f, vs = 0.f;
+                        if (i < w_end && (blk[r] < 0 || (long long)blk[r] >= p.num_blocks)) {
+                            blk[r] = -2;
+                        } else if (KVT == 2 && i < w_end) {
+                            ks = __ldg(p.k_scale + (size_t)blk[r] * p.Hkv + u.kvh);
+                            vs = __ldg(p.v_scale + (size_t)blk[r] * p.Hkv + u.kvh);
+                        }
+                        win_blk[r * 32 + lane] = blk[r];
+                        win_ks[r * 32 + lane] = ks;
+                        win_vs[r * 32 + lane] = vs;
+                    }
+                    __syncwarp();
+                }
+                // The whole warp prepares the chunk: lane t < UM_NT fills the metadata of 8-token group
+                // t, lane j < nbox owns box j (one page, or 128 rows of a larger page); lane 0 arms the
+                // barrier with the byte count, then every owning lane issues its own tile loads.
+                if (lane == 0 && !*s_abort && !mbar_wait_bounded(&empty[stage], phase ^ 1u, s_abort)) {
+                    *s_abort = 1;
+                    raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
+                }
+                __syncwarp();
+                UStageMeta& m = meta[stage];
+                float vs_lane = 0.f;
+                if (lane < UM_NT) {
+                    const int i = (tok0 + 8 * lane) >> lp;
+                    const bool live = i <= unit_last;
+                    m.ks[lane] = live ? win_ks[i - w0] : 0.f;
+                    vs_lane = live ? win_vs[i - w0] : 0.f;
+                    m.vs[lane] = vs_lane;
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) vs_lane = fmaxf(vs_lane, __shfl_xor_sync(0xffffffffu, vs_lane, off));
+                int blk = -1;
+                bool mine = false, refused = false;
+                if (lane < nbox) {
+                    const int i = (tok0 + lane * box_rows) >> lp;
+                    if (i <= unit_last) {
+                        blk = win_blk[i - w0];
+                        refused = blk < 0;
+                        mine = !refused;
+                    }
+                }
+                const unsigned owned = __ballot_sync(0xffffffffu, mine);
+                const bool bad = __any_sync(0xffffffffu, refused);
+                const uint32_t bytes = uint32_t(__popc(owned)) * 2u * NSUB * box_rows * 128u;
+                const bool abort_now = *s_abort;
+                if (lane == 0) {
+                    m.vsmax = vs_lane;
+                    m.bad = bad;
+                    if (bad) raise_error(p.error_flag, KVB_DEVERR_BLOCK);
+                }
+                __syncwarp();  // the metadata writes of every lane happen before the arrive below
+                if (lane == 0) {
+                    if (abort_now || bytes == 0) mbar_arrive(&full[stage]);
+                    else mbar_arrive_expect_tx(&full[stage], bytes);
+                }
+                __syncwarp();
+                if (mine && !abort_now) {
+                    const int tok = tok0 + lane * box_rows;
+                    const int y = (blk * p.Hkv + u.kvh) * p.page + (tok & (p.page - 1));
+                    uint8_t* st = smem + stage * C::STAGE;
+#pragma unroll
+                    for (int sb = 0; sb < NSUB; ++sb) {
+                        const int x = sb * (KVT == 1 ? 64 : 128);
+                        const uint32_t off = sb * TILE + lane * box_rows * 128;
+                        tma_load_2d(st + off, &tmk, &full[stage], x, y, policy);
+                        tma_load_2d(st + NSUB * TILE + off, &tmv, &full[stage], x, y, policy);
+                    }
+                }
+                __syncwarp();
+                if (++stage == STAGES) stage = 0, phase ^= 1u;
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        // One thread, polling: each pass issues the next S^T product if its inputs are ready (stage
+        // loaded, group's S buffer free, unit's Qhat written) and the next O^T product if its inputs
+        // are ready (group's Phat written, O buffer folded), so neither waits behind the other.
+        // QK for int8: A = K (signed), B = q limbs (signed). PV: A = V (signed), B = probability
+        // bytes (unsigned).
+        if (lane == 0) {
+            const uint32_t idesc_qk =
+                KVT == 1 ? instr_desc(1, 0, 0, 0, 0, N, 128) : instr_desc(2, 1, 1, 0, 0, N, 128);
+            const uint32_t idesc_pv =
+                KVT == 1 ? instr_desc(1, 0, 0, 1, 0, N, 128) : instr_desc(2, 1, 0, 1, 0, N, 128);
+            constexpr int KQK = KVT == 1 ? 16 : 32;  // contraction elements per instruction
+            UnitCursor cur{&p, prefix, (long long)blockIdx.x, total};
+            Unit u;
+            bool have_unit = false, units_done = false, need_q = false;
+            int c_next = 0, c_end = 0, unit_no = -1, qb = 0;
+            long long kq = 0, kv = 0;      // next chunk for QK^T, next chunk for PV
+            int q_stage = 0;               // ring stage of chunk kq
+            uint32_t q_phase = 0;
+            int v_stage = 0;               // ring stage of chunk kv (chunks take stages in order)
+            uint64_t t_idle = 0;
+            uint32_t spins = 0;
+            while (!*s_abort) {
+                bool progress = false;
+                if (!have_unit && !units_done) {
+                    units_done = true;
+                    while (cur.advance(u)) {
+                        if (u.nparts == 0) continue;
+                        units_done = false;
+                        have_unit = true;
+                        need_q = true;
+                        ++unit_no;
+                        qb = unit_no & 1;
+                        c_next = u.t0 / UM_CHUNK;
+                        c_end = (u.t1 + UM_CHUNK - 1) / UM_CHUNK;
+                        break;
+                    }
+                }
+                // ---- S^T = K Qhat^T for chunk kq
+                if (have_unit) {
+                    const int b = int(kq & 1);
+                    const uint32_t use = uint32_t(kq >> 1);
+                    const bool ready = (!need_q || mbar_test(&q_full[qb], (unit_no >> 1) & 1)) &&
+                                       mbar_test(&full[q_stage], q_phase) &&
+                                       (use == 0 || mbar_test(&s_free[b], (use - 1) & 1));
+                    if (ready) {
+                        need_q = false;
+                        tc_fence_after();
+                        const uint32_t kt = sbase + q_stage * C::STAGE;
+                        const uint32_t qaddr = sbase + uint32_t(C::Q_OFF) + qb * C::QBUF;
+#pragma unroll
+                        for (int s = 0; s < UM_D / KQK; ++s) {
+                            // 32 bytes of the contraction per instruction: slice s*32/128, offset s*32%128
+                            const uint32_t off = (s * 32 / 128) * TILE + (s * 32) % 128;
+                            const uint32_t qoff = (s * 32 / 128) * (C::NMAX * 128) + (s * 32) % 128;
+                            tc_mma<KVT>(tmem + 32 * b, smem_desc(kt + off, 16, 1024),
+                                        smem_desc(qaddr + qoff, 16, 1024), idesc_qk, s > 0);
+                        }
+                        tc_commit(&s_full[b]);
+                        ++kq;
+                        if (++q_stage == STAGES) q_stage = 0, q_phase ^= 1u;
+                        if (++c_next == c_end) {
+                            tc_commit(&q_free[qb]);  // the unit's last read of its Qhat buffer
+                            have_unit = false;
+                        }
+                        progress = true;
+                    }
+                }
+                // ---- O^T = V^T Phat^T for chunk kv
+                if (kv < kq) {
+                    const int b = int(kv & 1);
+                    const uint32_t use = uint32_t(kv >> 1);
+                    const bool ready =
+                        mbar_test(&p_full[b], use & 1) && (use == 0 || mbar_test(&o_free[b], (use - 1) & 1));
+                    if (ready) {
+                        tc_fence_after();
+                        const int st = v_stage;
+                        const uint32_t vt = sbase + st * C::STAGE + NSUB * TILE;
+                        const uint32_t pb = sbase + uint32_t(C::P_OFF) + b * C::PBUF;
+#pragma unroll
+                        for (int s = 0; s < UM_CHUNK / KQK; ++s) {
+                            // V^T (MN-major): KQK token rows per instruction = KQK/8 atoms of 1024 B;
+                            // the second 64-dim slice of fp16 rows is the next tile (LBO).
+                            const uint32_t voff = s * (KQK / 8) * 1024;
+                            const uint32_t poff = (s * 32 / 128) * (C::NMAX * 128) + (s * 32) % 128;
+                            tc_mma<KVT>(tmem + 64 + 32 * b, smem_desc(vt + voff, TILE, 1024),
+                                        smem_desc(pb + poff, 16, 1024), idesc_pv, s > 0);
+                        }
+                        tc_commit(&o_full[b]);
+                        tc_commit(&empty[st]);  // K and V of chunk kv are no longer read
+                        if (++v_stage == STAGES) v_stage = 0;
+                        ++kv;
+                        progress = true;
+                    }
+                }
+                if (units_done && !have_unit && kv == kq) break;
+                // bounded idling: give up (and report) after KVB_WAIT_LIMIT_NS without progress
+                if (progress) {
+                    spins = 0;
+                } else if (++spins == 1024u) {
+                    t_idle = globaltimer_ns();
+                } else if (spins > 1024u && (spins & 1023u) == 0 && globaltimer_ns() - t_idle > KVB_WAIT_LIMIT_NS) {
+                    *s_abort = 1;
+                    raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
+                }
+            }
+        }
+    } else {
+        // ------------------------------------------------------------------ softmax / accumulation
+        // Two warpgroups take alternate chunks: group gi handles the chunks whose running index k has
+        // k & 1 == gi, with its own tensor-memory S/O buffers and Phat buffer, and its own running
+        // (max, sum, O). The groups merge once per unit.
+        const int gi = (warp - 2) >> 2;
+        const int gt = tid - 64 - gi * UM_SOFT;  // 0..127 within the group
+        const int sw = gt >> 5;                  // warp within the group
+        const uint32_t gbar = 2 + gi;            // named barrier of the group
+        // this warp's tensor-memory lane quarter is fixed by warp % 4
+        const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;
+        const int my_lane = (warp & 3) * 32 + lane;  // token in S^T, head dim in O^T
+        float* gred = red + gi * 128;                // [0,32) q absmax, [32,96) chunk max x2, [96,128) sums
+        UnitCursor cur{&p, prefix, (long long)blockIdx.x, total};
+        Unit u;
+        int stage = 0;
+        uint32_t phase = 0;
+        long long k = 0;
+        int unit_no = 0;
+        while (cur.advance(u)) {
+            if (u.nparts == 0) {
+                if (gi == 0) store_tokenless_unit<UM_D>(p, u, gt, UM_SOFT);
+                continue;
+            }
+            const int qb = unit_no & 1;
+            // ---- Qhat^T for this unit (written by group 0): row (head g, part r) = fp16 half r of q,
+            // or int8 limb r. Both groups compute the per-head factors.
+            if (gi == 0 && unit_no >= 2) {
+                if (!*s_abort && !mbar_wait_bounded(&q_free[qb], ((unit_no - 2) >> 1) & 1, s_abort)) {
+                    *s_abort = 1;
+                    raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
+                }
+            }
+            float qscale[QGP];  // per head: the factor that turns the combined MMA result into a log2 score
+            {
+                const int d = my_lane;  // one head-dim element per thread
+                float x[QGP], amax[QGP];
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) {
+                    x[g] = g < u.nh ? __ldg(p.q + ((size_t)u.b * p.H + u.h0 + g) * UM_D + d) * p.q_scale : 0.f;
+                    float a = fabsf(x[g]);
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+                    amax[g] = a;
+                }
+                if (lane == 0) {
+#pragma unroll
+                    for (int g = 0; g < QGP; ++g) gred[sw * 8 + g] = amax[g];
+                }
+                named_barrier(gbar, UM_SOFT);
+#pragma unroll
+                for (int g = 0; g < QGP; ++g)
+                    amax[g] = fmaxf(fmaxf(gred[g], gred[8 + g]), fmaxf(gred[16 + g], gred[24 + g]));
+                uint8_t* qbuf = smem + C::Q_OFF + qb * C::QBUF;
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) {
+                    int e = 0;
+                    frexpf(amax[g], &e);
+                    const bool live = amax[g] > 0.f && amax[g] < 3.0e38f;
+                    if constexpr (KVT == 1) {
+                        // x * 2^(14 - e) in [-2^14, 2^14): hi + lo halves
+                        const float pre = live ? ldexpf(1.f, 14 - e) : 1.f;
+                        qscale[g] = 1.f / pre;
+                        if (gi == 0) {
+                            const float xs = x[g] * pre;
+                            const __half hi = __float2half_rn(xs);
+                            const __half lo = __float2half_rn(xs - __half2float(hi));
+                            const int col = (d % 64) * 2, sb = d / 64;
+                            *reinterpret_cast<__half*>(qbuf + sb * (C::NMAX * 128) + swz_off(g, col)) = hi;
+                            *reinterpret_cast<__half*>(qbuf + sb * (C::NMAX * 128) + swz_off(QGP + g, col)) = lo;
+                        }
+                    } else {
+                        // integer x * 2^(30 - e) with |.| < 2^30, as four signed limbs
+                        const float pre = live ? ldexpf(1.f, 30 - e) : 1.f;
+                        qscale[g] = 1.f / pre;
+                        if (gi == 0) {
+                            int8_t l[4];
+                            limbs4(__float2int_rn(x[g] * pre), l);
+#pragma unroll
+                            for (int r = 0; r < 4; ++r) *reinterpret_cast<int8_t*>(qbuf + swz_off(g * 4 + r, d)) = l[r];
+                        }
+                    }
+                }
+            }
+            if (gi == 0) {
+                fence_proxy_async_smem();  // generic writes of Qhat^T before the MMA reads them
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&q_full[qb]);
+            }
+
+            // ---- chunks
+            float m[QGP], lsum[QGP], o[QGP];  // running max (group-uniform), this thread's sum share, O row
+#pragma unroll
+            for (int g = 0; g < QGP; ++g) m[g] = NEG_BIG, lsum[g] = 0.f, o[g] = 0.f;
+            float m_prev[QGP];   // max the group's previous chunk's probabilities were computed with
+            float vscale_prev = 0.f;
+            bool have_prev = false;
+            long long k_own = -1;  // running index of this group's previous chunk
+            int bad = 0;
+            const uint32_t obuf = tmem + lane_base + 64 + 32 * gi;
+
+            // Folds O^T of this group's previous chunk (running index kp; its PV product completes the
+            // buffer's (kp >> 1)-th use) into the registers.
+            auto fold_prev = [&](long long kp) {
+                if (!*s_abort && !mbar_wait_bounded(&o_full[gi], uint32_t(kp >> 1) & 1, s_abort)) {
+                    *s_abort = 1;
+                    raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
+                }
+                tc_fence_after();
+                uint32_t r[32];
+                tc_ld8(obuf, *reinterpret_cast<uint32_t(*)[8]>(&r[0]));
+                if (N > 8) tc_ld8(obuf + 8, *reinterpret_cast<uint32_t(*)[8]>(&r[8]));
+                if (N > 16) {
+                    tc_ld8(obuf + 16, *reinterpret_cast<uint32_t(*)[8]>(&r[16]));
+                    tc_ld8(obuf + 24, *reinterpret_cast<uint32_t(*)[8]>(&r[24]));
+                }
+                tc_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&o_free[gi]);
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) {
+                    float v;
+                    if constexpr (KVT == 1) {
+                        v = __uint_as_float(r[g]) + __uint_as_float(r[QGP + g]);
+                    } else {
+                        v = (((float(int(r[4 * g])) * 256.f + float(int(r[4 * g + 1]))) * 256.f +
+                              float(int(r[4 * g + 2]))) * 256.f + float(int(r[4 * g + 3]))) *
+                            (vscale_prev * 9.313225746154785e-10f);  // 2^-30
+                    }
+                    // o and the previous chunk are both relative to m_prev; move them to the current max
+                    o[g] = (o[g] + v) * exp2f(m_prev[g] - m[g]);
+                }
+            };
+
+            const int c0 = u.t0 / UM_CHUNK, c1 = (u.t1 + UM_CHUNK - 1) / UM_CHUNK;
+            for (int c = c0; c < c1; ++c, ++k) {
+                const int cur_stage = stage;
+                const uint32_t cur_phase = phase;
+                if (++stage == STAGES) stage = 0, phase ^= 1u;
+                if (int(k & 1) != gi) continue;
+                const uint32_t use = uint32_t(k >> 1);
+                // The stage's full barrier makes the producer's metadata and the TMA bytes visible here
+                // (the fp16 path writes zeros into dead V rows, which must land after the TMA bytes).
+                const UStageMeta& md = meta[cur_stage];
+                bool ok = true;
+                if (!*s_abort) ok = mbar_wait_bounded(&full[cur_stage], cur_phase, s_abort);
+                if (ok && !*s_abort) ok = mbar_wait_bounded(&s_full[gi], use & 1, s_abort);
+                if (!ok) {
+                    *s_abort = 1;
+                    raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
+                }
+                tc_fence_after();
+                const int tok = c * UM_CHUNK + my_lane;
+                const bool valid = tok >= u.t0 && tok < u.t1;
+                uint32_t r[32];
+                const uint32_t sa = tmem + lane_base + 32 * gi;
+                tc_ld8(sa, *reinterpret_cast<uint32_t(*)[8]>(&r[0]));
+                if (N > 8) tc_ld8(sa + 8, *reinterpret_cast<uint32_t(*)[8]>(&r[8]));
+                if (N > 16) {
+                    tc_ld8(sa + 16, *reinterpret_cast<uint32_t(*)[8]>(&r[16]));
+                    tc_ld8(sa + 24, *reinterpret_cast<uint32_t(*)[8]>(&r[24]));
+                }
+                tc_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_free[gi]);
+                // scores (log2 units) of this token for each head
+                const float ks = KVT == 2 ? md.ks[my_lane >> 3] : 1.f;
+                float sc[QGP];
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) {
+                    float v;
+                    if constexpr (KVT == 1) {
+                        v = __uint_as_float(r[g]) + __uint_as_float(r[QGP + g]);
+                    } else {
+                        v = ((float(int(r[4 * g])) * 256.f + float(int(r[4 * g + 1]))) * 256.f +
+                             float(int(r[4 * g + 2]))) * 256.f + float(int(r[4 * g + 3]));
+                    }
+                    sc[g] = (valid && g < u.nh) ? v * qscale[g] * ks : NEG_BIG;
+                }
+                bad |= md.bad;
+                // chunk max per head: warp, then across the group's four warps
+                float mc[QGP];
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) {
+                    float a = sc[g];
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
+                    mc[g] = a;
+                }
+                float* rb = gred + 32 * (1 + int(use & 1));  // two alternating reduction slots
+                if (lane == 0) {
+#pragma unroll
+                    for (int g = 0; g < QGP; ++g) rb[sw * 8 + g] = mc[g];
+                }
+                named_barrier(gbar, UM_SOFT);
+                float pr[QGP];
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) {
+                    const float cm = fmaxf(fmaxf(rb[g], rb[8 + g]), fmaxf(rb[16 + g], rb[24 + g]));
+                    const float mn = fmaxf(m[g], cm);
+                    lsum[g] *= exp2f(m[g] - mn);
+                    m[g] = mn;
+                    pr[g] = sc[g] > 0.5f * NEG_BIG ? exp2f(sc[g] - mn) : 0.f;
+                    lsum[g] += pr[g];
+                }
+                // The group's Phat buffer was last read by the PV product of its previous chunk: fold that
+                // chunk's O first (this also waits for that product), then overwrite.
+                if (have_prev) fold_prev(k_own);
+                uint8_t* pbuf = smem + C::P_OFF + gi * C::PBUF;
+                float vscale_cur = 0.f;
+                if constexpr (KVT == 1) {
+                    const int col = (my_lane % 64) * 2, sb = my_lane / 64;
+#pragma unroll
+                    for (int g = 0; g < QGP; ++g) {
+                        const __half hi = __float2half_rn(pr[g]);
+                        const __half lo = __float2half_rn(pr[g] - __half2float(hi));
+                        *reinterpret_cast<__half*>(pbuf + sb * (C::NMAX * 128) + swz_off(g, col)) = hi;
+                        *reinterpret_cast<__half*>(pbuf + sb * (C::NMAX * 128) + swz_off(QGP + g, col)) = lo;
+                    }
+                    // fp16 V rows past the partition end may hold stale data or dead pool slots:
+                    // zero this token's V row so 0 * NaN cannot reach O.
+                    if (!valid && tok >= u.t1) {
+                        uint8_t* vrow = smem + cur_stage * C::STAGE + NSUB * TILE;
+#pragma unroll
+                        for (int sb2 = 0; sb2 < NSUB; ++sb2)
+#pragma unroll
+                            for (int ch = 0; ch < 8; ++ch)
+                                sts128_zero(smem_u32(vrow + sb2 * TILE + my_lane * 128 + ch * 16));
+                    }
+                } else {
+                    // probability * v_scale / (largest v_scale of the chunk) as an unsigned integer below
+                    // 2^30 whose four bytes are the four limbs
+                    vscale_cur = md.vsmax;
+                    const float vs = md.vs[my_lane >> 3];
+                    const float f = vscale_cur > 0.f ? vs / vscale_cur * 1073741824.f : 0.f;  // 2^30
+#pragma unroll
+                    for (int g = 0; g < QGP; ++g) {
+                        const uint32_t xi = __float2uint_rn(pr[g] * f);
+#pragma unroll
+                        for (int r2 = 0; r2 < 4; ++r2)
+                            *(pbuf + swz_off(g * 4 + r2, my_lane)) = uint8_t(xi >> (24 - 8 * r2));
+                    }
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[gi]);
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) m_prev[g] = m[g];
+                vscale_prev = vscale_cur;
+                have_prev = true;
+                k_own = k;
+            }
+            if (have_prev) fold_prev(k_own);
+            // ---- unit epilogue: group sums across its 128 tokens, then the two groups merge
+            float L[QGP];
+#pragma unroll
+            for (int g = 0; g < QGP; ++g) {
+                float a = lsum[g];
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+                L[g] = a;
+            }
+            if (lane == 0) {
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) gred[96 + sw * 8 + g] = L[g];
+            }
+            const int grp_bad = named_barrier_or(gbar, UM_SOFT, bad);
+#pragma unroll
+            for (int g = 0; g < QGP; ++g) L[g] = (gred[96 + g] + gred[104 + g]) + (gred[112 + g] + gred[120 + g]);
+            float* xo = xbuf;                  // [QGP][128] group 1's O rows
+            float* xml = xbuf + QGP * UM_D;    // [QGP] m, [QGP] L, [1] bad
+            if (gi == 1) {
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) xo[g * UM_D + my_lane] = o[g];
+                if (gt == 0) {
+#pragma unroll
+                    for (int g = 0; g < QGP; ++g) xml[g] = m[g], xml[QGP + g] = L[g];
+                    xml[2 * QGP] = grp_bad ? 1.f : 0.f;
+                }
+                named_barrier(4, 2 * UM_SOFT);  // group 1's state is written
+                named_barrier(4, 2 * UM_SOFT);  // group 0 has read it
+            } else {
+                named_barrier(4, 2 * UM_SOFT);
+                const bool any_bad = grp_bad || xml[2 * QGP] != 0.f;
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) {
+                    const float m1 = xml[g], l1 = xml[QGP + g];
+                    const float mm = fmaxf(m[g], m1);
+                    const float w0 = exp2f(m[g] - mm), w1 = exp2f(m1 - mm);
+                    o[g] = o[g] * w0 + xo[g * UM_D + my_lane] * w1;
+                    L[g] = L[g] * w0 + l1 * w1;
+                    m[g] = mm;
+                }
+                named_barrier(4, 2 * UM_SOFT);
+                const float nanv = __int_as_float(0x7fc00000);
+                const int d = my_lane;
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) {
+                    if (g >= u.nh) break;
+                    const int h = u.h0 + g;
+                    const float val = any_bad ? nanv : o[g] / L[g];
+                    if (u.nparts == 1) {
+                        p.out[((size_t)u.b * p.H + h) * UM_D + d] = val;
+                    } else {
+                        const size_t slot = ((size_t)u.b * p.H + h) * p.max_parts + u.part;
+                        p.part_o[slot * UM_D + d] = val;
+                        if (d == 0) p.part_ml[slot] = make_float2(m[g], any_bad ? nanv : L[g]);
+                    }
+                }
+                finish_partition<UM_D>(p, u, gt, UM_SOFT, gbar, s_flag, scratch, int(C::SCRATCH_FLOATS));
+                named_barrier(gbar, UM_SOFT);
+            }
+            ++unit_no;
+        }
+    }
+
+    // every role done: release tensor memory
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tc_dealloc(tmem, 128);
+}
+
+template <int KVT, int QGP>
+cudaError_t launch_one(const DecodeParams& p, const CUtensorMap& tk, const CUtensorMap& tv, const LaunchInfo& li) {
+    using C = UCfg<KVT>;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(decode_umma_kernel<KVT, QGP>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(C::SMEM));
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    const long long upper = (long long)p.B * p.nhg * p.max_parts;
+    const long long grid = std::min<long long>(upper, (long long)li.num_sms);
+    if (grid <= 0) return cudaSuccess;
+    decode_umma_kernel<KVT, QGP><<<(unsigned)grid, UM_THREADS, C::SMEM, li.stream>>>(tk, tv, p);
+    return cudaGetLastError();
+}
+
+template <int KVT>
+cudaError_t launch_kvt(const DecodeParams& p, const CUtensorMap& tk, const CUtensorMap& tv, const LaunchInfo& li) {
+    if (p.qg <= 1) return launch_one<KVT, 1>(p, tk, tv, li);
+    if (p.qg <= 2) return launch_one<KVT, 2>(p, tk, tv, li);
+    if (p.qg <= 4) return launch_one<KVT, 4>(p, tk, tv, li);
+    return launch_one<KVT, 8>(p, tk, tv, li);
+}
+
+}  // namespace
+
+bool kvb_umma_supported(int kv_type, int D, int page, int qg) {
+    if (kv_type != 1 && kv_type != 2) return false;
+    if (D != 128) return false;
+    if (!(page == 8 || page == 16 || page == 32 || page == 64 || page == 128 || page == 256)) return false;
+    return qg >= 1 && qg <= 8;
+}
+
+cudaError_t kvb_launch_decode_umma(const DecodeParams& p, int kv_type, int D, const void* tmap_k, const void* tmap_v,
+                                   const LaunchInfo& li) {
+    (void)D;
+    const CUtensorMap& tk = *static_cast<const CUtensorMap*>(tmap_k);
+    const CUtensorMap& tv = *static_cast<const CUtensorMap*>(tmap_v);
+    return kv_type == 1 ? launch_kvt<1>(p, tk, tv, li) : launch_kvt<2>(p, tk, tv, li);
+}

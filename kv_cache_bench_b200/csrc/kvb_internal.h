@@ -75,11 +75,17 @@ struct LaunchInfo {
 // CUDA-core kernel: every storage type, page size, head dim and group size.
 cudaError_t kvb_launch_decode_simt(const DecodeParams& p, int kv_type, int D, const LaunchInfo& li);
 
-// TMA + tensor-core kernel: fp16/int8 with 128- or 256-byte rows, page % 8 == 0 and page | 64 or
-// 64 | page (page <= 256), qg <= 8. `tmap_k`/`tmap_v` are CUtensorMap objects over the pools.
+// mma.sync + TMA kernel: fp16/int8 with 128- or 256-byte rows, page a power of two in [8, 256],
+// qg <= 8. `tmap_k`/`tmap_v` are CUtensorMap objects over the pools.
 bool kvb_mma_supported(int kv_type, int D, int page, int qg);
 cudaError_t kvb_launch_decode_mma(const DecodeParams& p, int kv_type, int D, const void* tmap_k,
                                   const void* tmap_v, const LaunchInfo& li);
+
+// tcgen05 kernel: fp16/int8, head dim 128, page 8/16/32/64/128/256, qg <= 8; tensor maps with boxes of
+// (128 bytes) x min(page, 128) rows.
+bool kvb_umma_supported(int kv_type, int D, int page, int qg);
+cudaError_t kvb_launch_decode_umma(const DecodeParams& p, int kv_type, int D, const void* tmap_k,
+                                   const void* tmap_v, const LaunchInfo& li);
 
 // Naive three-pass baseline on the contiguous cache.
 cudaError_t kvb_launch_naive(const float* q, const void* k, const void* v, const int* seq_lens, float* out,

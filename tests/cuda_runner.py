@@ -54,5 +54,19 @@ def run_naive(case):
 def mma_ok(kv_type, head_dim, page, group, share_kv=True):
     qg = min(group, 8) if share_kv else 1
     row = head_dim * (2 if kv_type == 1 else 1)
-    return (kv_type in (1, 2) and row in (128, 256) and page % 8 == 0 and page <= 256
-            and (64 % page == 0 or page % 64 == 0) and 1 <= qg <= 8)
+    return kv_type in (1, 2) and row in (128, 256) and page in (8, 16, 32, 64, 128, 256) and 1 <= qg <= 8
+
+
+def umma_ok(kv_type, head_dim, page, group, share_kv=True):
+    qg = min(group, 8) if share_kv else 1
+    return kv_type in (1, 2) and head_dim == 128 and page in (8, 16, 32, 64, 128, 256) and 1 <= qg <= 8
+
+
+def kernels_for(kv_type, head_dim, page, group, share_kv=True):
+    """Every kernel that supports the shape, plus the automatic choice."""
+    ks = [kvb.Kernel.simt, kvb.Kernel.auto]
+    if mma_ok(kv_type, head_dim, page, group, share_kv):
+        ks.append(kvb.Kernel.mma)
+    if umma_ok(kv_type, head_dim, page, group, share_kv):
+        ks.append(kvb.Kernel.umma)
+    return ks

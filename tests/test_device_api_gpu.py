@@ -63,7 +63,7 @@ def test_cuda_graph_replay():
     del g
 
 
-@pytest.mark.parametrize("kernel", [kvb.Kernel.simt, kvb.Kernel.mma])
+@pytest.mark.parametrize("kernel", [kvb.Kernel.simt, kvb.Kernel.mma, kvb.Kernel.umma])
 def test_device_refuses_bad_lengths_with_nan_and_flag(kernel):
     case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=[300, 200, 100], kv_type=oracle.F16,
                             page=64, seed=4)
@@ -85,7 +85,7 @@ def test_device_refuses_bad_lengths_with_nan_and_flag(kernel):
     assert np.isnan(o[1]).all() and dec.error_flag() & 1
 
 
-@pytest.mark.parametrize("kernel", [kvb.Kernel.simt, kvb.Kernel.mma])
+@pytest.mark.parametrize("kernel", [kvb.Kernel.simt, kvb.Kernel.mma, kvb.Kernel.umma])
 def test_device_refuses_bad_block_ids_with_nan_and_flag(kernel):
     case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=[300, 200], kv_type=oracle.I8,
                             page=64, seed=6)

@@ -11,18 +11,15 @@ import pytest
 
 import kv_cache_bench_b200 as kvb
 import oracle
-from tests.cuda_runner import mma_ok, run_case, run_naive
+from tests.cuda_runner import kernels_for, run_case, run_naive
 
 pytestmark = pytest.mark.gpu
 TOL = 2e-5
 
 
 def _kernels(c, share_kv=True):
-    ks = [kvb.Kernel.simt, kvb.Kernel.auto]
     G = c["num_heads"] // c["num_kv_heads"]
-    if mma_ok(c["kv_type"], c["head_dim"], c["page_size"], G, share_kv):
-        ks.append(kvb.Kernel.mma)
-    return ks
+    return kernels_for(c["kv_type"], c["head_dim"], c["page_size"], G, share_kv)
 
 
 def _parts(c):

@@ -15,7 +15,7 @@ import pytest
 
 import kv_cache_bench_b200 as kvb
 import oracle
-from tests.cuda_runner import mma_ok, run_case
+from tests.cuda_runner import kernels_for, mma_ok, run_case, umma_ok
 
 pytestmark = pytest.mark.gpu
 TOL = 2e-5
@@ -54,6 +54,12 @@ CASES = [
     ("long_i8_p128", 32, 8, 128, oracle.I8, 128, [20000], [0, 4096], {}),
     ("long_f16_p64", 32, 8, 128, oracle.F16, 64, [9000, 2500], [0, 512], {}),
     ("batch_ragged_f16_p16", 32, 8, 128, oracle.F16, 16, list(range(0, 1200, 37)), [0], dict(pool_slack=1.1)),
+    ("chunk128_edges_i8_p32", 32, 8, 128, oracle.I8, 32, [127, 128, 129, 255, 256, 257, 384], [0, 128, 200], {}),
+    ("chunk128_edges_f16_p128", 32, 8, 128, oracle.F16, 128, [127, 128, 129, 255, 256, 257], [0, 128, 200], {}),
+    ("gqa2_i8_p64", 16, 8, 128, oracle.I8, 64, [700, 1], [0], dict(varied=True)),
+    ("gqa1_f16_p256", 8, 8, 128, oracle.F16, 256, [1000, 300], [0, 256], {}),
+    ("nan_dead_slots_f16_p8", 32, 8, 128, oracle.F16, 8, [100, 1, 131, 0], [0, 64], dict(dead_fill=np.nan)),
+    ("zero_slices_i8", 32, 8, 128, oracle.I8, 64, [300, 70], [0], dict(varied=True, q_amp=3.0)),
 ]
 
 
@@ -65,12 +71,12 @@ def test_random_case(name, H, Hkv, D, kv_type, page, lens, parts, extra):
     # The reference's 2e-5 is derived for |q| <= 8 (README "Tolerances": score error ~ |s| * 2^-24 *
     # log2(D)); scores grow with q_amp, and so does the fp32 rounding of any kernel.
     tol = TOL * max(1.0, extra.get("q_amp", 1.0) / 8.0)
-    kernels = [kvb.Kernel.simt, kvb.Kernel.auto]
-    if mma_ok(kv_type, D, page, H // Hkv):
-        kernels.append(kvb.Kernel.mma)
-    elif name.endswith("_simt"):
-        with pytest.raises(ValueError):
-            run_case(case, kernel=kvb.Kernel.mma)
+    kernels = kernels_for(kv_type, D, page, H // Hkv)
+    if name.endswith("_simt"):
+        assert not mma_ok(kv_type, D, page, H // Hkv) and not umma_ok(kv_type, D, page, H // Hkv)
+        for k in (kvb.Kernel.mma, kvb.Kernel.umma):
+            with pytest.raises(ValueError):
+                run_case(case, kernel=k)
     failures = []
     for kernel in kernels:
         for part in parts:
