@@ -171,7 +171,10 @@ int kvb_paged_workspace_bytes(const kvb_paged_args* args, size_t* bytes);
 int kvb_paged_decode_async(const kvb_paged_args* args, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Reads and clears the error flag of a workspace (synchronizes `stream`). *flag = 0: no bad
- * length or block id since the last read. */
+ * length or block id since the last read. Bits: 1 bad length, 2 bad block id, 4 a bounded device
+ * wait gave up, 8 a split-K arrival counter counted past its partition count (two launches sharing
+ * the workspace at once, or an earlier launch that gave up); after 4 or 8 this call also resets
+ * the counters, so the workspace can be used again. */
 int kvb_paged_error_flag(void* workspace, void* stream, int* flag);
 
 #ifdef __cplusplus

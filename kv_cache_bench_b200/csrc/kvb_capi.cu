@@ -157,15 +157,16 @@ int check_static(const kvb_paged_args* a) {
     return KVB_OK;
 }
 
+// Encodes the tile map of one pool: rows of D elements, num_blocks * Hkv * page rows, boxes of
+// (128 bytes) x min(page, 64) rows, 128-byte swizzle.
 // Launch ids for the split-K arrival counters: distinct per launch within the process, high bit set
-// (never 0, never the bits of a small float a stale workspace could hold).
+// (never 0 or KVB_CTR_CLEAN, and as a float the bits of a negative denormal that no stored partial
+// result holds).
 unsigned next_launch_id() {
     static std::atomic<unsigned> n{0};
     return 0x80000000u | (n.fetch_add(1, std::memory_order_relaxed) & 0x7fffffffu);
 }
 
-// Encodes the tile map of one pool: rows of D elements, num_blocks * Hkv * page rows, boxes of
-// (128 bytes) x min(page, 64) rows, 128-byte swizzle.
 int encode_pool_map(CUtensorMap* map, const void* pool, const kvb_paged_args* a, int box_rows_max) {
     PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
     if (!enc) return fail(KVB_ERR_DEVICE, "cuTensorMapEncodeTiled is unavailable");
@@ -347,14 +348,27 @@ int begin_timed(State& S, cudaEvent_t* e0, cudaEvent_t* e1) {
     return KVB_OK;
 }
 
+// Reads and clears the error word of a workspace; after a TIMEOUT or STATE error also zeroes the
+// arrival counters the last launch used (their count is workspace word 1), so the workspace is
+// ready for the next call.
+int read_clear_flag(void* ws, cudaStream_t s, unsigned* flag) {
+    unsigned h[2] = {0, 0};
+    KVB_CUDA(cudaMemcpyAsync(h, ws, sizeof h, cudaMemcpyDeviceToHost, s));
+    KVB_CUDA(cudaStreamSynchronize(s));
+    *flag = h[0];
+    if (!h[0]) return KVB_OK;
+    KVB_CUDA(cudaMemsetAsync(ws, 0, sizeof h[0], s));
+    if (h[0] & (KVB_DEVERR_TIMEOUT | KVB_DEVERR_STATE))
+        KVB_CUDA(cudaMemsetAsync(static_cast<char*>(ws) + 256, 0, sizeof(unsigned long long) * (size_t)h[1], s));
+    KVB_CUDA(cudaStreamSynchronize(s));
+    return KVB_OK;
+}
+
 int check_flag(State& S) {
     if (!S.ws) return KVB_OK;
     unsigned flag = 0;
-    KVB_CUDA(cudaMemcpyAsync(&flag, S.ws, sizeof flag, cudaMemcpyDeviceToHost, S.stream));
-    KVB_CUDA(cudaStreamSynchronize(S.stream));
+    if (int rc = read_clear_flag(S.ws, S.stream, &flag)) return rc;
     if (!flag) return KVB_OK;
-    KVB_CUDA(cudaMemsetAsync(S.ws, 0, sizeof flag, S.stream));
-    KVB_CUDA(cudaStreamSynchronize(S.stream));
     return fail(KVB_ERR_DEVICE, "decode kernel reported error flags " + std::to_string(flag));
 }
 
@@ -462,13 +476,7 @@ int kvb_paged_decode_async(const kvb_paged_args* a, void* workspace, size_t work
 int kvb_paged_error_flag(void* workspace, void* stream, int* flag) {
     if (!workspace || !flag) return fail(KVB_ERR_INVALID, "null workspace or flag");
     unsigned h = 0;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    KVB_CUDA(cudaMemcpyAsync(&h, workspace, sizeof h, cudaMemcpyDeviceToHost, s));
-    KVB_CUDA(cudaStreamSynchronize(s));
-    if (h) {
-        KVB_CUDA(cudaMemsetAsync(workspace, 0, sizeof h, s));
-        KVB_CUDA(cudaStreamSynchronize(s));
-    }
+    if (int rc = read_clear_flag(workspace, static_cast<cudaStream_t>(stream), &h)) return rc;
     *flag = (int)h;
     return KVB_OK;
 }

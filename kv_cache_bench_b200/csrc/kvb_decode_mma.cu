@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
         prefix = s_prefix;
     }
     const long long total = unit_total(p, prefix);
+    note_counter_count(p);
 
     if (warp == NCW) {
         // ------------------------------------------------------------------ producer warp

@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(SIMT_THREADS) decode_simt_kernel(const DecodeP
         build_unit_prefix(p, s_prefix, reinterpret_cast<int*>(s_slot_o), tid, SIMT_THREADS, 1);
         prefix = s_prefix;
     }
+    note_counter_count(p);
     UnitCursor cur{&p, prefix, (long long)blockIdx.x, unit_total(p, prefix)};
 
     Unit u;

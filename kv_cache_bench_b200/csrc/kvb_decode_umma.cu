@@ -207,6 +207,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     uint64_t* o_free = reinterpret_cast<uint64_t*>(smem + C::MISC_OFF + 32);  // [2] O^T read (softmax -> MMA)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // the unit enumeration below starts with the sequence lengths: have them on the way to L2
+    if (tid < p.B && tid < KVB_PREFIX_MAX) prefetch_l2(p.seq_lens + tid);
 
     // Zero the ring (rows never loaded must hold finite values), set up barriers, allocate TMEM.
     for (int i = tid; i < int(C::RING / 16); i += UM_THREADS) sts128_zero(sbase + 16 * i);
@@ -249,6 +251,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         prefix = s_prefix;
     }
     const long long total = unit_total(p, prefix);
+    note_counter_count(p);
 
     if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer
@@ -265,35 +268,31 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             const int* bt = p.block_table + (size_t)u.b * p.max_blocks;
             const int unit_last = (u.t1 - 1) >> lp;
             int w0 = -1;
+            int wblk[UM_WIN / 32];  // this lane's block ids of the current window
             const int c0 = u.t0 / UM_CHUNK, c1 = (u.t1 + UM_CHUNK - 1) / UM_CHUNK;
             for (int c = c0; c < c1; ++c) {
                 const int tok0 = c * UM_CHUNK;
                 const int i_first = tok0 >> lp;
                 const int i_last = min((tok0 + UM_CHUNK - 1) >> lp, unit_last);
+                // A new window of block ids: the tile loads below need only the ids; the int8 scales
+                // (loads that depend on the ids) are fetched after the loads are issued.
+                bool scales_due = false;
                 if (w0 < 0 || i_first < w0 || i_last >= w0 + UM_WIN) {
                     __syncwarp();
                     w0 = i_first;
                     const int w_end = min(w0 + UM_WIN, unit_last + 1);
-                    int blk[UM_WIN / 32];
 #pragma unroll
                     for (int r = 0; r < UM_WIN / 32; ++r) {
                         const int i = w0 + r * 32 + lane;
-                        blk[r] = i < w_end ? __ldg(bt + i) : -1;
+                        wblk[r] = i < w_end ? __ldg(bt + i) : -1;
                     }
 #pragma unroll
                     for (int r = 0; r < UM_WIN / 32; ++r) {
                         const int i = w0 + r * 32 + lane;
-                        float ks = 0.f, vs = 0.f;
-                        if (i < w_end && (blk[r] < 0 || (long long)blk[r] >= p.num_blocks)) {
-                            blk[r] = -2;
-                        } else if (KVT == 2 && i < w_end) {
-                            ks = __ldg(p.k_scale + (size_t)blk[r] * p.Hkv + u.kvh);
-                            vs = __ldg(p.v_scale + (size_t)blk[r] * p.Hkv + u.kvh);
-                        }
-                        win_blk[r * 32 + lane] = blk[r];
-                        win_ks[r * 32 + lane] = ks;
-                        win_vs[r * 32 + lane] = vs;
+                        if (i < w_end && (wblk[r] < 0 || (long long)wblk[r] >= p.num_blocks)) wblk[r] = -2;
+                        win_blk[r * 32 + lane] = wblk[r];
                     }
+                    scales_due = KVT == 2;
                     __syncwarp();
                 }
                 // The whole warp prepares the chunk: lane t < UM_NT fills the metadata of 8-token group
@@ -304,17 +303,6 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
                 }
                 __syncwarp();
-                UStageMeta& m = meta[stage];
-                float vs_lane = 0.f;
-                if (lane < UM_NT) {
-                    const int i = (tok0 + 8 * lane) >> lp;
-                    const bool live = i <= unit_last;
-                    m.ks[lane] = live ? win_ks[i - w0] : 0.f;
-                    vs_lane = live ? win_vs[i - w0] : 0.f;
-                    m.vs[lane] = vs_lane;
-                }
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) vs_lane = fmaxf(vs_lane, __shfl_xor_sync(0xffffffffu, vs_lane, off));
                 int blk = -1;
                 bool mine = false, refused = false;
                 if (lane < nbox) {
@@ -329,16 +317,9 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 const bool bad = __any_sync(0xffffffffu, refused);
                 const uint32_t bytes = uint32_t(__popc(owned)) * 2u * NSUB * box_rows * 128u;
                 const bool abort_now = *s_abort;
-                if (lane == 0) {
-                    m.vsmax = vs_lane;
-                    m.bad = bad;
-                    if (bad) raise_error(p.error_flag, KVB_DEVERR_BLOCK);
-                }
-                __syncwarp();  // the metadata writes of every lane happen before the arrive below
-                if (lane == 0) {
-                    if (abort_now || bytes == 0) mbar_arrive(&full[stage]);
-                    else mbar_arrive_expect_tx(&full[stage], bytes);
-                }
+                // The stage completes on the byte count plus one arrival, which comes after the
+                // metadata below is written.
+                if (lane == 0 && !abort_now && bytes != 0) mbar_expect_tx(&full[stage], bytes);
                 __syncwarp();
                 if (mine && !abort_now) {
                     const int tok = tok0 + lane * box_rows;
@@ -352,6 +333,35 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                         tma_load_2d(st + NSUB * TILE + off, &tmv, &full[stage], x, y, policy);
                     }
                 }
+                if (KVT == 2 && scales_due) {
+                    const int w_end = min(w0 + UM_WIN, unit_last + 1);
+#pragma unroll
+                    for (int r = 0; r < UM_WIN / 32; ++r) {
+                        const int i = w0 + r * 32 + lane;
+                        const bool ok = i < w_end && wblk[r] >= 0;
+                        win_ks[r * 32 + lane] = ok ? __ldg(p.k_scale + (size_t)wblk[r] * p.Hkv + u.kvh) : 0.f;
+                        win_vs[r * 32 + lane] = ok ? __ldg(p.v_scale + (size_t)wblk[r] * p.Hkv + u.kvh) : 0.f;
+                    }
+                    __syncwarp();
+                }
+                UStageMeta& m = meta[stage];
+                float vs_lane = 0.f;
+                if (lane < UM_NT) {
+                    const int i = (tok0 + 8 * lane) >> lp;
+                    const bool live = i <= unit_last;
+                    if (KVT == 2) m.ks[lane] = live ? win_ks[i - w0] : 0.f;
+                    vs_lane = KVT == 2 && live ? win_vs[i - w0] : 0.f;
+                    if (KVT == 2) m.vs[lane] = vs_lane;
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) vs_lane = fmaxf(vs_lane, __shfl_xor_sync(0xffffffffu, vs_lane, off));
+                if (lane == 0) {
+                    m.vsmax = vs_lane;
+                    m.bad = bad;
+                    if (bad) raise_error(p.error_flag, KVB_DEVERR_BLOCK);
+                }
+                __syncwarp();  // the metadata writes of every lane happen before the arrive below
+                if (lane == 0) mbar_arrive(&full[stage]);
                 __syncwarp();
                 if (++stage == STAGES) stage = 0, phase ^= 1u;
             }

@@ -44,6 +44,12 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
+// Raises the transaction count the current phase waits for, without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -132,6 +138,10 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
 }
 
 // ---- shared-memory loads and tensor-core helpers -----------------------------------------------
@@ -325,6 +335,11 @@ __device__ __forceinline__ long long unit_total(const DecodeParams& p, const int
     return prefix ? (long long)prefix[p.B] : (long long)p.B * p.nhg * p.max_parts;
 }
 
+// Records in workspace word 1 how many arrival counters this launch uses (see KVB_DEVERR_STATE).
+__device__ __forceinline__ void note_counter_count(const DecodeParams& p) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) p.error_flag[1] = unsigned(p.B * p.nhg);
+}
+
 // ---- epilogue -----------------------------------------------------------------------------------
 
 // Finishes one unit once its per-slot online-softmax states are in shared memory:
@@ -367,10 +382,14 @@ __device__ __forceinline__ void merge_slots_and_store(const DecodeParams& p, con
 // After every round of merge_slots_and_store for a multi-partition unit: counts the partition
 // in and, if it was the last one, merges all partitions of (b, head group) into `out`.
 //
-// The arrival counter of (b, head group) is a 64-bit word (launch id << 32 | arrivals). A value
-// from any other launch -- the previous one, or stale workspace contents left by a call with
-// another layout -- counts as zero arrivals, so the workspace never needs clearing between calls;
-// the last arrival writes 0 so that a replayed launch (same id, e.g. from a CUDA graph) starts over.
+// The arrival counter of (b, head group) is a 64-bit word (epoch << 32 | arrivals), counted with
+// one atomic add per partition. The last arrival leaves it at (KVB_CTR_CLEAN << 32), which the next
+// launch counts from directly. Any other epoch that is not this launch's id is stale -- a zeroed
+// workspace, or partial results of a call with another layout where this call keeps its counters --
+// and an arrival that meets one claims the word for this launch (compare-and-swap to
+// launch << 32) and counts itself again, so only the first use after a layout change pays for a
+// compare-and-swap. An arrival past the partition count (two launches sharing one workspace at the
+// same time, or an aborted launch) raises KVB_DEVERR_STATE; the flag reader then resets the counters.
 template <int D>
 __device__ __forceinline__ void finish_partition(const DecodeParams& p, const Unit& u, int tid, int nthreads,
                                                  uint32_t bar_id, int* s_flag, float* scratch, int scratch_floats) {
@@ -379,16 +398,24 @@ __device__ __forceinline__ void finish_partition(const DecodeParams& p, const Un
     named_barrier(bar_id, nthreads);
     if (tid == 0) {
         unsigned long long* ctr = p.counters + (size_t)u.b * p.nhg + u.hg;
-        const unsigned long long mine = (unsigned long long)p.launch << 32;
-        unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(ctr), seen;
+        const unsigned long long old = atomicAdd(ctr, 1ull);
+        const unsigned epoch = unsigned(old >> 32);
         unsigned arrived;
-        do {
-            seen = old;
-            arrived = (seen >> 32) == p.launch ? unsigned(seen) + 1u : 1u;
-            old = atomicCAS(ctr, seen, mine | arrived);
-        } while (old != seen);
+        if (epoch == p.launch || epoch == KVB_CTR_CLEAN) {
+            arrived = unsigned(old) + 1u;
+        } else {
+            unsigned long long seen = old + 1ull;
+            for (;;) {
+                const unsigned long long cur = atomicCAS(ctr, seen, (unsigned long long)p.launch << 32);
+                const unsigned e = unsigned(cur >> 32);
+                if (cur == seen || e == p.launch || e == KVB_CTR_CLEAN) break;
+                seen = cur;
+            }
+            arrived = unsigned(atomicAdd(ctr, 1ull)) + 1u;
+        }
         const int last = arrived == unsigned(u.nparts);
-        if (last) atomicExch(ctr, 0ull);
+        if (arrived > unsigned(u.nparts)) raise_error(p.error_flag, KVB_DEVERR_STATE);
+        if (last) atomicExch(ctr, (unsigned long long)KVB_CTR_CLEAN << 32);
         *s_flag = last;
     }
     named_barrier(bar_id, nthreads);

@@ -15,6 +15,12 @@
 #define KVB_DEVERR_LENGTH 1u    // a sequence length outside [0, min(max_len, max_blocks * page)]
 #define KVB_DEVERR_BLOCK 2u     // a live block id outside [0, num_blocks)
 #define KVB_DEVERR_TIMEOUT 4u   // a bounded wait gave up
+#define KVB_DEVERR_STATE 8u     // a split-K arrival counter counted past its partition count
+// Epoch of an arrival counter that a completed launch left behind (a NaN payload that neither a
+// launch id nor a stored partial result takes).
+#define KVB_CTR_CLEAN 0x7fffffffu
+// Word 1 of the workspace holds the number of arrival counters the last launch used, so that the
+// flag reader can zero them after a TIMEOUT or STATE error (words 0 and 1 are the header).
 
 // Sequences up to this batch size are enumerated through a prefix sum in shared memory.
 #define KVB_PREFIX_MAX 256
@@ -36,7 +42,7 @@ struct DecodeParams {
     // workspace
     float* part_o;           // [B][H][max_parts][D], partition outputs (normalized)
     float2* part_ml;         // [B][H][max_parts], (max in log2 units, sum)
-    unsigned long long* counters;  // [B][nhg]: (launch id << 32) | partitions finished
+    unsigned long long* counters;  // [B][nhg]: (epoch << 32) | partitions finished
     unsigned* error_flag;    // KVB_DEVERR_* bits
     // shape
     int B, H, Hkv, G;
