@@ -91,7 +91,7 @@ bool pool_rows_fit(const kvb_paged_args* a) {
 int choose_kernel(const kvb_paged_args* a, int qg) {
     const int D = a->shape.head_dim;
     const bool tma_ok = a->max_len > 0 && pool_rows_fit(a) && aligned16(a->k) && aligned16(a->v);
-    const bool umma = tma_ok && kvb_umma_supported(a->kv_type, D, a->page_size, qg);
+    const bool umma = tma_ok && kvb_umma_supported(a->kv_type, D, a->page_size, qg, a->part_tokens);
     const bool mma = tma_ok && kvb_mma_supported(a->kv_type, D, a->page_size, qg);
     if (a->max_len == 0) return KVB_KERNEL_SIMT;  // nothing to read: the CUDA-core kernel writes the zeros
     switch (a->kernel) {

@@ -135,6 +135,8 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
         prefetch_tensormap(&tmv);
     }
     __syncthreads();
+    pdl_wait();
+    pdl_trigger();
     const int* prefix = nullptr;
     if (p.B <= KVB_PREFIX_MAX) {
         build_unit_prefix(p, s_prefix, reinterpret_cast<int*>(epi_o), tid, MMA_THREADS, 1);
@@ -500,8 +502,7 @@ cudaError_t launch_one(const DecodeParams& p, const CUtensorMap& tk, const CUten
     const long long upper = (long long)p.B * p.nhg * p.max_parts;
     const long long grid = std::min<long long>(upper, (long long)li.num_sms * blocks_per_sm);
     if (grid <= 0) return cudaSuccess;
-    decode_mma_kernel<KVT, D, QGM><<<(unsigned)grid, MMA_THREADS, C::SMEM, li.stream>>>(tk, tv, p);
-    return cudaGetLastError();
+    return kvb_launch_pdl(decode_mma_kernel<KVT, D, QGM>, (unsigned)grid, MMA_THREADS, C::SMEM, li.stream, tk, tv, p);
 }
 
 template <int KVT, int D>

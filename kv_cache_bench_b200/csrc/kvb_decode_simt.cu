@@ -105,6 +105,8 @@ __global__ void __launch_bounds__(SIMT_THREADS) decode_simt_kernel(const DecodeP
 
     const int tid = threadIdx.x, lane = tid & 31, l16 = lane & 15;
     const int slot = tid >> 4;
+    pdl_wait();
+    pdl_trigger();
     const int* prefix = nullptr;
     if (p.B <= KVB_PREFIX_MAX) {
         build_unit_prefix(p, s_prefix, reinterpret_cast<int*>(s_slot_o), tid, SIMT_THREADS, 1);
@@ -250,8 +252,7 @@ cudaError_t launch_one(const DecodeParams& p, const LaunchInfo& li) {
     const long long upper = (long long)p.B * p.nhg * p.max_parts;
     const long long grid = std::min<long long>(upper, (long long)li.num_sms * blocks_per_sm);
     if (grid <= 0) return cudaSuccess;
-    decode_simt_kernel<KVT, D, QGM><<<(unsigned)grid, SIMT_THREADS, 0, li.stream>>>(p);
-    return cudaGetLastError();
+    return kvb_launch_pdl(decode_simt_kernel<KVT, D, QGM>, (unsigned)grid, SIMT_THREADS, 0, li.stream, p);
 }
 
 template <int KVT, int D>

@@ -5,17 +5,20 @@
 // tokens, then a weighted merge of the partitions. Shapes: head dim 128, fp16 or int8 pools, page
 // size 8, 16, 32, 64, 128 or 256, up to 8 query heads per KV-head group.
 //
-// One CTA per SM, warp-specialized:
-//   warp 0      TMA producer: for each 128-token chunk, 2-D tile loads of the K and V rows of every
-//               page in the chunk (128-byte swizzle) into a ring of shared-memory stages.
-//   warp 1      MMA issuer (one thread): per chunk
+// One CTA per SM, warp-specialized (11 warps):
+//   warp 0      TMA producer: reads the unit's block ids (and int8 scales) once into a shared-memory
+//               page table, then for each 128-token chunk issues 2-D tile loads of the K and V rows
+//               of every page in the chunk (128-byte swizzle) into a ring of shared-memory stages.
+//   warps 1, 10 MMA issuers (one thread each), for the even and the odd chunks of the running chunk
+//               index:
 //                 S^T[128 tokens x N] = K[128 x 128] . Qhat^T[128 x N]      (tensor memory)
 //                 O^T[128 dims x N]   = V^T[128 x 128 tokens] . Phat^T       (tensor memory)
 //               reading K (K-major) and V (MN-major, the transposed view of the same TMA tile)
 //               straight from the stage. tcgen05.commit releases the stage and signals the softmax.
-//   warps 2-5   softmax and accumulation (128 threads, one per tensor-memory lane): thread t reads
-//               token t's scores, the four warps agree on the chunk max per head, write Phat^T to
-//               shared memory, and after the PV product thread d folds O^T row d into registers.
+//   warps 2-9   two softmax groups of 4 warps (128 threads, one per tensor-memory lane), group g for
+//               the chunks of parity g: thread t reads token t's scores, the four warps agree on the
+//               chunk max per head, write Phat^T to shared memory, and after the PV product thread d
+//               folds O^T row d into registers. The groups merge once per unit.
 //
 // Exactness. The operands are exact in the MMA's input type, so the contraction is exact up to the
 // accumulator:
@@ -37,12 +40,13 @@ namespace {
 using namespace kvb_dev;
 
 constexpr int UM_CHUNK = 128;         // tokens per stage = MMA M for QK^T
-constexpr int UM_THREADS = 10 * 32;   // producer, MMA, two groups of 4 softmax warps
+constexpr int UM_WARPS = 11;          // producer, MMA (even chunks), 8 softmax, MMA (odd chunks)
+constexpr int UM_THREADS = UM_WARPS * 32;
 constexpr int UM_SOFT = 128;          // threads of one softmax group
 constexpr int UM_D = 128;             // head dim
 constexpr int TILE = UM_CHUNK * 128;  // bytes of one [128 rows][128 B] swizzled tile
-constexpr int UM_WIN = 64;            // pages of block-table metadata per window
-constexpr int UM_NT = UM_CHUNK / 8;   // 8-token groups per chunk (the smallest page)
+constexpr int UM_PT = 528;            // page-table entries: pages of one partition, at most
+constexpr int UM_GRED = 160;          // reduction floats per softmax group
 
 // ---- tcgen05 wrappers -----------------------------------------------------------------------------
 
@@ -73,14 +77,14 @@ __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t
     if constexpr (KIND == 1) {
         asm volatile(
             "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(tmem_d),
-            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
             : "memory");
     } else {
         asm volatile(
             "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(tmem_d),
-            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
+            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
             : "memory");
     }
 }
@@ -131,14 +135,6 @@ __device__ __forceinline__ void limbs4(int x, int8_t (&l)[4]) {
     l[0] = (int8_t)x;
 }
 
-struct UStageMeta {
-    float ks[UM_NT];  // K scale of each 8-token group (int8)
-    float vs[UM_NT];
-    float vsmax;      // largest V scale of the chunk
-    int bad;          // a block id of this chunk was refused
-    int pad[2];
-};
-
 template <int KVT>
 struct UCfg {
     static constexpr int NSUB = KVT == 1 ? 2 : 1;             // 128-byte column slices of a row
@@ -150,15 +146,18 @@ struct UCfg {
     static constexpr size_t RING = size_t(STAGES) * STAGE;
     static constexpr size_t Q_OFF = RING;                      // 2 Qhat buffers (1024-aligned)
     static constexpr size_t P_OFF = Q_OFF + 2 * QBUF;          // 2 Phat buffers
-    static constexpr size_t META_OFF = P_OFF + 2 * PBUF;
-    static constexpr size_t BAR_OFF = META_OFF + STAGES * sizeof(UStageMeta);
-    static constexpr int NBARS = 2 * STAGES + 2 * 6;           // full/empty + q_full/q_free/s_full/s_free/p_full/o_full x2
+    static constexpr size_t BAD_OFF = P_OFF + 2 * PBUF;        // [STAGES] a block id of the chunk was refused
+    static constexpr size_t BAR_OFF = kvb_align_up(BAD_OFF + STAGES * sizeof(int), 64);
+    // full per (stage, chunk parity); empty per stage; q_full, q_free, s_full, s_free, p_full,
+    // o_full, pt_free x2
+    static constexpr int NBARS = 3 * STAGES + 2 * 7;
     static constexpr size_t RED_OFF = kvb_align_up(BAR_OFF + NBARS * sizeof(uint64_t), 16);
-    static constexpr size_t RED_FLOATS = 2 * 128;              // per group: cross-warp reductions [warp][head] x 4 uses
-    static constexpr size_t WIN_OFF = RED_OFF + RED_FLOATS * sizeof(float);
-    static constexpr size_t PREFIX_OFF = WIN_OFF + 3 * sizeof(int) * UM_WIN;
+    static constexpr size_t WIN_OFF = RED_OFF + 2 * UM_GRED * sizeof(float);
+    // page table: block ids [UM_PT]; int8: scales [2 buffers][UM_PT] for K and for V
+    static constexpr size_t PT_BYTES = sizeof(int) * UM_PT * (KVT == 2 ? 5 : 1);
+    static constexpr size_t PREFIX_OFF = WIN_OFF + PT_BYTES;
     static constexpr size_t SCRATCH_OFF = kvb_align_up(PREFIX_OFF + sizeof(int) * (KVB_PREFIX_MAX + 1), 16);
-    static constexpr size_t SCRATCH_FLOATS = 2048;             // final merge weights, prefix scan
+    static constexpr size_t SCRATCH_FLOATS = 1024;             // final merge weights, prefix scan
     static constexpr size_t XBUF_OFF = SCRATCH_OFF + SCRATCH_FLOATS * sizeof(float);
     static constexpr size_t XBUF_FLOATS = 8 * 128 + 2 * 8 + 4;  // group 1's O rows, max, sums, bad flag
     static constexpr size_t MISC_OFF = kvb_align_up(XBUF_OFF + XBUF_FLOATS * sizeof(float), 64);
@@ -166,10 +165,11 @@ struct UCfg {
 };
 
 static_assert(UCfg<1>::SMEM <= 227 * 1024 && UCfg<2>::SMEM <= 227 * 1024, "shared memory budget");
-static_assert(UCfg<1>::BAR_OFF % 8 == 0 && UCfg<2>::BAR_OFF % 8 == 0, "mbarrier alignment");
-static_assert(UCfg<1>::MISC_OFF % 64 == 0 && UCfg<2>::MISC_OFF % 64 == 0, "mbarrier alignment");
+static_assert(UCfg<1>::BAR_OFF % 64 == 0 && UCfg<2>::BAR_OFF % 64 == 0, "mbarrier alignment");
+static_assert(UCfg<1>::MISC_OFF % 64 == 0 && UCfg<2>::MISC_OFF % 64 == 0, "alignment");
 static_assert(UCfg<1>::Q_OFF % 1024 == 0 && UCfg<1>::P_OFF % 1024 == 0 && UCfg<2>::P_OFF % 1024 == 0,
               "swizzled operands need 1024-byte alignment");
+static_assert(UCfg<2>::SCRATCH_FLOATS >= UM_THREADS, "prefix scan scratch");
 
 template <int KVT, int QGP>  // QGP: query heads per group, padded to 1, 2, 4 or 8
 __global__ void __launch_bounds__(UM_THREADS, 1)
@@ -184,50 +184,61 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
-    UStageMeta* meta = reinterpret_cast<UStageMeta*>(smem + C::META_OFF);
+    int* stage_bad = reinterpret_cast<int*>(smem + C::BAD_OFF);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+    // Chunk k (running index over the CTA's units) lives in stage k % STAGES and is announced on
+    // full[k % (2 * STAGES)]: a stage alternates between even and odd chunks, whose consumers (MMA
+    // warp and softmax group of that parity) each wait on their own barrier in chunk order, so a
+    // parity wait never matches a phase two uses old.
     uint64_t* full = bars;
-    uint64_t* empty = bars + STAGES;
-    uint64_t* q_full = bars + 2 * STAGES;  // [2] Qhat^T written (softmax -> MMA)
-    uint64_t* q_free = q_full + 2;         // [2] QK^T of the unit done (MMA -> softmax)
-    uint64_t* s_full = q_full + 4;         // [2] S^T ready (MMA -> softmax)
+    uint64_t* empty = bars + 2 * STAGES;
+    uint64_t* q_full = bars + 3 * STAGES;  // [2] Qhat^T written (softmax group 0 -> MMA)
+    uint64_t* q_free = q_full + 2;         // [2] the unit's QK^T products done (both MMA warps -> softmax)
+    uint64_t* s_full = q_full + 4;         // [2] S^T ready (MMA -> softmax), one per chunk parity
     uint64_t* s_free = q_full + 6;         // [2] S^T read (softmax -> MMA)
-    uint64_t* p_full = q_full + 8;         // [2] Phat^T written (softmax -> MMA)
-    uint64_t* o_full = q_full + 10;        // [2] O^T ready; also: O^T read (softmax -> MMA) via o_free below
+    uint64_t* p_full = q_full + 8;         // [2] Phat^T written, previous O^T folded (softmax -> MMA)
+    uint64_t* o_full = q_full + 10;        // [2] O^T ready (MMA -> softmax)
+    uint64_t* pt_free = q_full + 12;       // [2] int8 scale buffer read (softmax -> producer)
     float* red = reinterpret_cast<float*>(smem + C::RED_OFF);
-    int* win_blk = reinterpret_cast<int*>(smem + C::WIN_OFF);
-    float* win_ks = reinterpret_cast<float*>(win_blk + UM_WIN);
-    float* win_vs = win_ks + UM_WIN;
+    int* pt_blk = reinterpret_cast<int*>(smem + C::WIN_OFF);
+    float* pt_ks = reinterpret_cast<float*>(pt_blk + UM_PT);  // int8 only: [2][UM_PT]
+    float* pt_vs = pt_ks + 2 * UM_PT;                         // int8 only: [2][UM_PT]
     int* s_prefix = reinterpret_cast<int*>(smem + C::PREFIX_OFF);
     float* scratch = reinterpret_cast<float*>(smem + C::SCRATCH_OFF);
     float* xbuf = reinterpret_cast<float*>(smem + C::XBUF_OFF);
     volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::MISC_OFF);
     int* s_flag = reinterpret_cast<int*>(smem + C::MISC_OFF + 8);
     uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF + 16);
-    uint64_t* o_free = reinterpret_cast<uint64_t*>(smem + C::MISC_OFF + 32);  // [2] O^T read (softmax -> MMA)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // the unit enumeration below starts with the sequence lengths: have them on the way to L2
+    // The unit enumeration starts with the sequence lengths and the block table: have them on the
+    // way to L2 while the CTA sets up (the table cooperatively across CTAs, when it is small).
     if (tid < p.B && tid < KVB_PREFIX_MAX) prefetch_l2(p.seq_lens + tid);
+    {
+        const size_t tb = (size_t)p.B * p.max_blocks * sizeof(int);
+        if (tb <= (size_t(256) << 10))
+            for (size_t off = ((size_t)blockIdx.x * UM_THREADS + tid) * 128; off < tb;
+                 off += (size_t)gridDim.x * UM_THREADS * 128)
+                prefetch_l2(reinterpret_cast<const char*>(p.block_table) + off);
+    }
 
-    // Zero the ring (rows never loaded must hold finite values), set up barriers, allocate TMEM.
-    for (int i = tid; i < int(C::RING / 16); i += UM_THREADS) sts128_zero(sbase + 16 * i);
+    // Barriers and tensor memory. The ring is not cleared: rows a chunk does not load are either
+    // masked (K: the token's score is not used) or multiplied by an exactly zero probability (int8
+    // V) or cleared by the softmax before the PV product (fp16 V, where 0 * NaN would not be 0).
     for (int i = tid; i < int((2 * C::QBUF + 2 * C::PBUF) / 16); i += UM_THREADS)
         sts128_zero(sbase + uint32_t(C::Q_OFF) + 16 * i);
     fence_proxy_async_smem();
     if (tid == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
-        }
+        for (int s = 0; s < 2 * STAGES; ++s) mbar_init(&full[s], 1);
+        for (int s = 0; s < STAGES; ++s) mbar_init(&empty[s], 1);
         for (int i = 0; i < 2; ++i) {
             mbar_init(&q_full[i], UM_SOFT / 32);
-            mbar_init(&q_free[i], 1);
+            mbar_init(&q_free[i], 2);
             mbar_init(&s_full[i], 1);
             mbar_init(&s_free[i], UM_SOFT / 32);
             mbar_init(&p_full[i], UM_SOFT / 32);
             mbar_init(&o_full[i], 1);
-            mbar_init(&o_free[i], UM_SOFT / 32);
+            mbar_init(&pt_free[i], 2 * UM_SOFT / 32);
         }
         *s_abort = 0;
         fence_mbarrier_init();
@@ -244,7 +255,9 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
-    // tensor-memory columns: S^T buffers at 0 and 32, O^T buffers at 64 and 96
+    // tensor-memory columns: S^T buffers at 0 and 32, O^T buffers at 64 and 96 (one per chunk parity)
+    pdl_wait();
+    pdl_trigger();
     const int* prefix = nullptr;
     if (p.B <= KVB_PREFIX_MAX) {
         build_unit_prefix(p, s_prefix, reinterpret_cast<int*>(scratch), tid, UM_THREADS, 1);
@@ -252,6 +265,12 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     }
     const long long total = unit_total(p, prefix);
     note_counter_count(p);
+    const int lp = __ffs(p.page) - 1;  // pages are powers of two on this path
+
+    auto give_up = [&]() {
+        *s_abort = 1;
+        raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
+    };
 
     if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer
@@ -262,215 +281,208 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         uint32_t phase = 0;
         const int box_rows = p.page < UM_CHUNK ? p.page : UM_CHUNK;
         const int nbox = UM_CHUNK / box_rows;
-        const int lp = __ffs(p.page) - 1;  // pages are powers of two on this path
+        const uint32_t box_bytes = 2u * NSUB * uint32_t(box_rows) * 128u;
+        int unit_no = 0;
+        int kp = 0;  // running chunk index
         while (cur.advance(u)) {
             if (u.nparts == 0) continue;
             const int* bt = p.block_table + (size_t)u.b * p.max_blocks;
-            const int unit_last = (u.t1 - 1) >> lp;
-            int w0 = -1;
-            int wblk[UM_WIN / 32];  // this lane's block ids of the current window
+            const int pg0 = u.t0 >> lp, pg1 = (u.t1 - 1) >> lp;  // the unit's pages (pg1 - pg0 < UM_PT)
+            const int npg = min(pg1 - pg0 + 1, UM_PT);  // the host keeps partitions within UM_PT pages
+            const int sb = unit_no & 1;
+            // Block ids of the unit; refused ones (outside [0, num_blocks)) become -2.
+            __syncwarp();
+            for (int i = lane; i < npg; i += 32) {
+                int blk = __ldg(bt + pg0 + i);
+                if (blk < 0 || (long long)blk >= p.num_blocks) blk = -2;
+                pt_blk[i] = blk;
+            }
+            __syncwarp();
             const int c0 = u.t0 / UM_CHUNK, c1 = (u.t1 + UM_CHUNK - 1) / UM_CHUNK;
             for (int c = c0; c < c1; ++c) {
                 const int tok0 = c * UM_CHUNK;
-                const int i_first = tok0 >> lp;
-                const int i_last = min((tok0 + UM_CHUNK - 1) >> lp, unit_last);
-                // A new window of block ids: the tile loads below need only the ids; the int8 scales
-                // (loads that depend on the ids) are fetched after the loads are issued.
-                bool scales_due = false;
-                if (w0 < 0 || i_first < w0 || i_last >= w0 + UM_WIN) {
-                    __syncwarp();
-                    w0 = i_first;
-                    const int w_end = min(w0 + UM_WIN, unit_last + 1);
-#pragma unroll
-                    for (int r = 0; r < UM_WIN / 32; ++r) {
-                        const int i = w0 + r * 32 + lane;
-                        wblk[r] = i < w_end ? __ldg(bt + i) : -1;
-                    }
-#pragma unroll
-                    for (int r = 0; r < UM_WIN / 32; ++r) {
-                        const int i = w0 + r * 32 + lane;
-                        if (i < w_end && (wblk[r] < 0 || (long long)wblk[r] >= p.num_blocks)) wblk[r] = -2;
-                        win_blk[r * 32 + lane] = wblk[r];
-                    }
-                    scales_due = KVT == 2;
-                    __syncwarp();
-                }
-                // The whole warp prepares the chunk: lane t < UM_NT fills the metadata of 8-token group
-                // t, lane j < nbox owns box j (one page, or 128 rows of a larger page); lane 0 arms the
-                // barrier with the byte count, then every owning lane issues its own tile loads.
-                if (lane == 0 && !*s_abort && !mbar_wait_bounded(&empty[stage], phase ^ 1u, s_abort)) {
-                    *s_abort = 1;
-                    raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
-                }
+                if (lane == 0 && !*s_abort && !mbar_wait_bounded(&empty[stage], phase ^ 1u, s_abort)) give_up();
                 __syncwarp();
+                // lane j < nbox owns box j (one page, or 128 rows of a larger page)
                 int blk = -1;
                 bool mine = false, refused = false;
                 if (lane < nbox) {
                     const int i = (tok0 + lane * box_rows) >> lp;
-                    if (i <= unit_last) {
-                        blk = win_blk[i - w0];
+                    if (i >= pg0 && i <= pg1) {
+                        blk = pt_blk[i - pg0];
                         refused = blk < 0;
                         mine = !refused;
                     }
                 }
                 const unsigned owned = __ballot_sync(0xffffffffu, mine);
                 const bool bad = __any_sync(0xffffffffu, refused);
-                const uint32_t bytes = uint32_t(__popc(owned)) * 2u * NSUB * box_rows * 128u;
+                const uint32_t bytes = uint32_t(__popc(owned)) * box_bytes;
                 const bool abort_now = *s_abort;
-                // The stage completes on the byte count plus one arrival, which comes after the
-                // metadata below is written.
-                if (lane == 0 && !abort_now && bytes != 0) mbar_expect_tx(&full[stage], bytes);
+                // The unit's first int8 chunk also publishes the unit's scales, fetched after the tile
+                // loads are on their way: its stage completes on the bytes plus the arrival below.
+                const bool scales_due = KVT == 2 && c == c0;
+                uint64_t* fb = &full[kp % (2 * STAGES)];
+                if (lane == 0) {
+                    stage_bad[stage] = bad;
+                    if (bad) raise_error(p.error_flag, KVB_DEVERR_BLOCK);
+                    if (scales_due) {
+                        if (!abort_now && bytes) mbar_expect_tx(fb, bytes);
+                    } else if (abort_now || bytes == 0) {
+                        mbar_arrive(fb);
+                    } else {
+                        mbar_arrive_expect_tx(fb, bytes);
+                    }
+                }
                 __syncwarp();
                 if (mine && !abort_now) {
                     const int tok = tok0 + lane * box_rows;
                     const int y = (blk * p.Hkv + u.kvh) * p.page + (tok & (p.page - 1));
                     uint8_t* st = smem + stage * C::STAGE;
 #pragma unroll
-                    for (int sb = 0; sb < NSUB; ++sb) {
-                        const int x = sb * (KVT == 1 ? 64 : 128);
-                        const uint32_t off = sb * TILE + lane * box_rows * 128;
-                        tma_load_2d(st + off, &tmk, &full[stage], x, y, policy);
-                        tma_load_2d(st + NSUB * TILE + off, &tmv, &full[stage], x, y, policy);
+                    for (int s = 0; s < NSUB; ++s) {
+                        const int x = s * (KVT == 1 ? 64 : 128);
+                        const uint32_t off = s * TILE + lane * box_rows * 128;
+                        tma_load_2d(st + off, &tmk, fb, x, y, policy);
+                        tma_load_2d(st + NSUB * TILE + off, &tmv, fb, x, y, policy);
                     }
                 }
-                if (KVT == 2 && scales_due) {
-                    const int w_end = min(w0 + UM_WIN, unit_last + 1);
-#pragma unroll
-                    for (int r = 0; r < UM_WIN / 32; ++r) {
-                        const int i = w0 + r * 32 + lane;
-                        const bool ok = i < w_end && wblk[r] >= 0;
-                        win_ks[r * 32 + lane] = ok ? __ldg(p.k_scale + (size_t)wblk[r] * p.Hkv + u.kvh) : 0.f;
-                        win_vs[r * 32 + lane] = ok ? __ldg(p.v_scale + (size_t)wblk[r] * p.Hkv + u.kvh) : 0.f;
-                    }
+                if (scales_due) {
+                    // the softmax warps are done with this scale buffer's previous unit
+                    if (lane == 0 && unit_no >= 2 && !*s_abort &&
+                        !mbar_wait_bounded(&pt_free[sb], ((unit_no - 2) >> 1) & 1, s_abort))
+                        give_up();
                     __syncwarp();
+                    float* ks_b = pt_ks + sb * UM_PT;
+                    float* vs_b = pt_vs + sb * UM_PT;
+                    for (int i = lane; i < npg; i += 32) {
+                        const int b2 = pt_blk[i];
+                        ks_b[i] = b2 >= 0 ? __ldg(p.k_scale + (size_t)b2 * p.Hkv + u.kvh) : 0.f;
+                        vs_b[i] = b2 >= 0 ? __ldg(p.v_scale + (size_t)b2 * p.Hkv + u.kvh) : 0.f;
+                    }
+                    __syncwarp();  // every lane's scale writes happen before the arrive
+                    if (lane == 0) mbar_arrive(fb);
                 }
-                UStageMeta& m = meta[stage];
-                float vs_lane = 0.f;
-                if (lane < UM_NT) {
-                    const int i = (tok0 + 8 * lane) >> lp;
-                    const bool live = i <= unit_last;
-                    if (KVT == 2) m.ks[lane] = live ? win_ks[i - w0] : 0.f;
-                    vs_lane = KVT == 2 && live ? win_vs[i - w0] : 0.f;
-                    if (KVT == 2) m.vs[lane] = vs_lane;
-                }
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) vs_lane = fmaxf(vs_lane, __shfl_xor_sync(0xffffffffu, vs_lane, off));
-                if (lane == 0) {
-                    m.vsmax = vs_lane;
-                    m.bad = bad;
-                    if (bad) raise_error(p.error_flag, KVB_DEVERR_BLOCK);
-                }
-                __syncwarp();  // the metadata writes of every lane happen before the arrive below
-                if (lane == 0) mbar_arrive(&full[stage]);
                 __syncwarp();
+                ++kp;
                 if (++stage == STAGES) stage = 0, phase ^= 1u;
             }
+            ++unit_no;
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------------ MMA issuer
-        // One thread, polling: each pass issues the next S^T product if its inputs are ready (stage
-        // loaded, group's S buffer free, unit's Qhat written) and the next O^T product if its inputs
-        // are ready (group's Phat written, O buffer folded), so neither waits behind the other.
+    } else if (warp == 1 || warp == UM_WARPS - 1) {
+        // ------------------------------------------------------------------ MMA issuers
+        // Warp 1 issues the products of the even chunks (running index), warp 10 those of the odd
+        // ones, each into its own S^T and O^T buffers. One thread per warp polls: each pass issues the
+        // oldest pending O^T product if its Phat is written (that releases the stage to the producer),
+        // and the next S^T product if its stage is loaded and the previous S^T of this parity was read
+        // (so the softmax finds S^T_k ready when it finishes chunk k-2). Neither waits behind the other.
         // QK for int8: A = K (signed), B = q limbs (signed). PV: A = V (signed), B = probability
         // bytes (unsigned).
+        const int par = warp == 1 ? 0 : 1;
         if (lane == 0) {
             const uint32_t idesc_qk =
                 KVT == 1 ? instr_desc(1, 0, 0, 0, 0, N, 128) : instr_desc(2, 1, 1, 0, 0, N, 128);
             const uint32_t idesc_pv =
                 KVT == 1 ? instr_desc(1, 0, 0, 1, 0, N, 128) : instr_desc(2, 1, 0, 1, 0, N, 128);
             constexpr int KQK = KVT == 1 ? 16 : 32;  // contraction elements per instruction
+            const uint32_t s_tm = tmem + 32 * par, o_tm = tmem + 64 + 32 * par;
+            const uint32_t pb = sbase + uint32_t(C::P_OFF) + par * C::PBUF;
             UnitCursor cur{&p, prefix, (long long)blockIdx.x, total};
             Unit u;
             bool have_unit = false, units_done = false, need_q = false;
-            int c_next = 0, c_end = 0, unit_no = -1, qb = 0;
-            long long kq = 0, kv = 0;      // next chunk for QK^T, next chunk for PV
-            int q_stage = 0;               // ring stage of chunk kq
-            uint32_t q_phase = 0;
-            int v_stage = 0;               // ring stage of chunk kv (chunks take stages in order)
-            uint64_t t_idle = 0;
+            int unit_no = -1, qb = 0;
+            int qk = 0, k_end = 0;         // next own chunk for S^T; end of the current unit's chunks
+            // own chunks with S^T issued and O^T pending: the older one (pv_k0) and the newer one
+            int pv_k0 = 0, pv_st0 = 0, pv_k1 = 0, pv_st1 = 0, pv_n = 0;
             uint32_t spins = 0;
+            uint64_t t_idle = 0;
             while (!*s_abort) {
                 bool progress = false;
-                if (!have_unit && !units_done) {
-                    units_done = true;
-                    while (cur.advance(u)) {
-                        if (u.nparts == 0) continue;
-                        units_done = false;
-                        have_unit = true;
-                        need_q = true;
-                        ++unit_no;
-                        qb = unit_no & 1;
-                        c_next = u.t0 / UM_CHUNK;
-                        c_end = (u.t1 + UM_CHUNK - 1) / UM_CHUNK;
+                while (!have_unit && !units_done) {
+                    if (!cur.advance(u)) {
+                        units_done = true;
                         break;
                     }
+                    if (u.nparts == 0) continue;
+                    ++unit_no;
+                    qb = unit_no & 1;
+                    const int k_base = k_end;
+                    k_end = k_base + (u.t1 + UM_CHUNK - 1) / UM_CHUNK - u.t0 / UM_CHUNK;
+                    qk = k_base + ((k_base & 1) != par ? 1 : 0);
+                    if (qk >= k_end) {
+                        tc_commit(&q_free[qb]);  // no chunk of this parity: release the Qhat buffer now
+                        continue;
+                    }
+                    have_unit = true;
+                    need_q = true;
                 }
-                // ---- S^T = K Qhat^T for chunk kq
-                if (have_unit) {
-                    const int b = int(kq & 1);
-                    const uint32_t use = uint32_t(kq >> 1);
+                // ---- O^T = V^T Phat^T for the oldest pending chunk
+                if (pv_n > 0) {
+                    const int kk = pv_k0, st = pv_st0;
+                    if (mbar_test(&p_full[par], uint32_t(kk >> 1) & 1)) {
+                        tc_fence_after();
+                        const uint32_t vt = sbase + st * C::STAGE + NSUB * TILE;
+#pragma unroll
+                        for (int s = 0; s < UM_CHUNK / KQK; ++s) {
+                            // V^T (MN-major): KQK token rows per instruction = KQK/8 atoms of 1024 B; the
+                            // second 64-dim slice of fp16 rows is the next tile (LBO).
+                            const uint32_t voff = s * (KQK / 8) * 1024;
+                            const uint32_t poff = (s * 32 / 128) * (C::NMAX * 128) + (s * 32) % 128;
+                            tc_mma<KVT>(o_tm, smem_desc(vt + voff, TILE, 1024), smem_desc(pb + poff, 16, 1024),
+                                        idesc_pv, s > 0);
+                        }
+                        tc_commit(&o_full[par]);
+                        tc_commit(&empty[st]);  // K and V of chunk kk are no longer read
+                        pv_k0 = pv_k1;
+                        pv_st0 = pv_st1;
+                        --pv_n;
+                        progress = true;
+                    }
+                }
+                // ---- S^T = K Qhat^T for the next own chunk
+                if (have_unit && pv_n < 2) {
+                    const int st = qk % STAGES;
+                    const uint32_t use = uint32_t(qk >> 1);
                     const bool ready = (!need_q || mbar_test(&q_full[qb], (unit_no >> 1) & 1)) &&
-                                       mbar_test(&full[q_stage], q_phase) &&
-                                       (use == 0 || mbar_test(&s_free[b], (use - 1) & 1));
+                                       mbar_test(&full[qk % (2 * STAGES)], uint32_t(qk / (2 * STAGES)) & 1) &&
+                                       (use == 0 || mbar_test(&s_free[par], (use - 1) & 1));
                     if (ready) {
                         need_q = false;
                         tc_fence_after();
-                        const uint32_t kt = sbase + q_stage * C::STAGE;
+                        const uint32_t kt = sbase + st * C::STAGE;
                         const uint32_t qaddr = sbase + uint32_t(C::Q_OFF) + qb * C::QBUF;
 #pragma unroll
                         for (int s = 0; s < UM_D / KQK; ++s) {
                             // 32 bytes of the contraction per instruction: slice s*32/128, offset s*32%128
                             const uint32_t off = (s * 32 / 128) * TILE + (s * 32) % 128;
                             const uint32_t qoff = (s * 32 / 128) * (C::NMAX * 128) + (s * 32) % 128;
-                            tc_mma<KVT>(tmem + 32 * b, smem_desc(kt + off, 16, 1024),
-                                        smem_desc(qaddr + qoff, 16, 1024), idesc_qk, s > 0);
+                            tc_mma<KVT>(s_tm, smem_desc(kt + off, 16, 1024), smem_desc(qaddr + qoff, 16, 1024),
+                                        idesc_qk, s > 0);
                         }
-                        tc_commit(&s_full[b]);
-                        ++kq;
-                        if (++q_stage == STAGES) q_stage = 0, q_phase ^= 1u;
-                        if (++c_next == c_end) {
-                            tc_commit(&q_free[qb]);  // the unit's last read of its Qhat buffer
+                        tc_commit(&s_full[par]);
+                        if (pv_n == 0) {
+                            pv_k0 = qk;
+                            pv_st0 = st;
+                        } else {
+                            pv_k1 = qk;
+                            pv_st1 = st;
+                        }
+                        ++pv_n;
+                        qk += 2;
+                        if (qk >= k_end) {
+                            tc_commit(&q_free[qb]);  // this warp's last read of the unit's Qhat buffer
                             have_unit = false;
                         }
                         progress = true;
                     }
                 }
-                // ---- O^T = V^T Phat^T for chunk kv
-                if (kv < kq) {
-                    const int b = int(kv & 1);
-                    const uint32_t use = uint32_t(kv >> 1);
-                    const bool ready =
-                        mbar_test(&p_full[b], use & 1) && (use == 0 || mbar_test(&o_free[b], (use - 1) & 1));
-                    if (ready) {
-                        tc_fence_after();
-                        const int st = v_stage;
-                        const uint32_t vt = sbase + st * C::STAGE + NSUB * TILE;
-                        const uint32_t pb = sbase + uint32_t(C::P_OFF) + b * C::PBUF;
-#pragma unroll
-                        for (int s = 0; s < UM_CHUNK / KQK; ++s) {
-                            // V^T (MN-major): KQK token rows per instruction = KQK/8 atoms of 1024 B;
-                            // the second 64-dim slice of fp16 rows is the next tile (LBO).
-                            const uint32_t voff = s * (KQK / 8) * 1024;
-                            const uint32_t poff = (s * 32 / 128) * (C::NMAX * 128) + (s * 32) % 128;
-                            tc_mma<KVT>(tmem + 64 + 32 * b, smem_desc(vt + voff, TILE, 1024),
-                                        smem_desc(pb + poff, 16, 1024), idesc_pv, s > 0);
-                        }
-                        tc_commit(&o_full[b]);
-                        tc_commit(&empty[st]);  // K and V of chunk kv are no longer read
-                        if (++v_stage == STAGES) v_stage = 0;
-                        ++kv;
-                        progress = true;
-                    }
-                }
-                if (units_done && !have_unit && kv == kq) break;
+                if (units_done && !have_unit && pv_n == 0) break;
                 // bounded idling: give up (and report) after KVB_WAIT_LIMIT_NS without progress
                 if (progress) {
                     spins = 0;
                 } else if (++spins == 1024u) {
                     t_idle = globaltimer_ns();
                 } else if (spins > 1024u && (spins & 1023u) == 0 && globaltimer_ns() - t_idle > KVB_WAIT_LIMIT_NS) {
-                    *s_abort = 1;
-                    raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
+                    give_up();
                 }
             }
         }
@@ -486,12 +498,12 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         // this warp's tensor-memory lane quarter is fixed by warp % 4
         const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;
         const int my_lane = (warp & 3) * 32 + lane;  // token in S^T, head dim in O^T
-        float* gred = red + gi * 128;                // [0,32) q absmax, [32,96) chunk max x2, [96,128) sums
+        // [0,32) q absmax; [32,112) chunk max x2 ([warp][10]: 8 heads, V scale); [112,144) sums
+        float* gred = red + gi * UM_GRED;
         UnitCursor cur{&p, prefix, (long long)blockIdx.x, total};
         Unit u;
         int stage = 0;
-        uint32_t phase = 0;
-        long long k = 0;
+        int k = 0;  // running chunk index
         int unit_no = 0;
         while (cur.advance(u)) {
             if (u.nparts == 0) {
@@ -502,10 +514,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             // ---- Qhat^T for this unit (written by group 0): row (head g, part r) = fp16 half r of q,
             // or int8 limb r. Both groups compute the per-head factors.
             if (gi == 0 && unit_no >= 2) {
-                if (!*s_abort && !mbar_wait_bounded(&q_free[qb], ((unit_no - 2) >> 1) & 1, s_abort)) {
-                    *s_abort = 1;
-                    raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
-                }
+                if (!*s_abort && !mbar_wait_bounded(&q_free[qb], ((unit_no - 2) >> 1) & 1, s_abort)) give_up();
             }
             float qscale[QGP];  // per head: the factor that turns the combined MMA result into a log2 score
             {
@@ -571,17 +580,17 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             float m_prev[QGP];   // max the group's previous chunk's probabilities were computed with
             float vscale_prev = 0.f;
             bool have_prev = false;
-            long long k_own = -1;  // running index of this group's previous chunk
+            int k_own = -1;  // running index of this group's previous chunk
             int bad = 0;
             const uint32_t obuf = tmem + lane_base + 64 + 32 * gi;
+            const int pg0 = u.t0 >> lp, pg_hi = ((u.t1 - 1) >> lp) - pg0;
+            const float* ks_b = pt_ks + qb * UM_PT;  // int8 scales of the unit's pages
+            const float* vs_b = pt_vs + qb * UM_PT;
 
             // Folds O^T of this group's previous chunk (running index kp; its PV product completes the
             // buffer's (kp >> 1)-th use) into the registers.
-            auto fold_prev = [&](long long kp) {
-                if (!*s_abort && !mbar_wait_bounded(&o_full[gi], uint32_t(kp >> 1) & 1, s_abort)) {
-                    *s_abort = 1;
-                    raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
-                }
+            auto fold_prev = [&](int kp) {
+                if (!*s_abort && !mbar_wait_bounded(&o_full[gi], uint32_t(kp >> 1) & 1, s_abort)) give_up();
                 tc_fence_after();
                 uint32_t r[32];
                 tc_ld8(obuf, *reinterpret_cast<uint32_t(*)[8]>(&r[0]));
@@ -592,8 +601,6 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 }
                 tc_wait_ld();
                 tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&o_free[gi]);
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) {
                     float v;
@@ -612,20 +619,16 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             const int c0 = u.t0 / UM_CHUNK, c1 = (u.t1 + UM_CHUNK - 1) / UM_CHUNK;
             for (int c = c0; c < c1; ++c, ++k) {
                 const int cur_stage = stage;
-                const uint32_t cur_phase = phase;
-                if (++stage == STAGES) stage = 0, phase ^= 1u;
+                if (++stage == STAGES) stage = 0;
                 if (int(k & 1) != gi) continue;
                 const uint32_t use = uint32_t(k >> 1);
-                // The stage's full barrier makes the producer's metadata and the TMA bytes visible here
-                // (the fp16 path writes zeros into dead V rows, which must land after the TMA bytes).
-                const UStageMeta& md = meta[cur_stage];
+                // The stage's full barrier makes the producer's flags, scales and the TMA bytes visible
+                // here (the fp16 path writes zeros into dead V rows, which must land after the TMA bytes).
                 bool ok = true;
-                if (!*s_abort) ok = mbar_wait_bounded(&full[cur_stage], cur_phase, s_abort);
+                if (!*s_abort)
+                    ok = mbar_wait_bounded(&full[k % (2 * STAGES)], uint32_t(k / (2 * STAGES)) & 1, s_abort);
                 if (ok && !*s_abort) ok = mbar_wait_bounded(&s_full[gi], use & 1, s_abort);
-                if (!ok) {
-                    *s_abort = 1;
-                    raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
-                }
+                if (!ok) give_up();
                 tc_fence_after();
                 const int tok = c * UM_CHUNK + my_lane;
                 const bool valid = tok >= u.t0 && tok < u.t1;
@@ -637,12 +640,18 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     tc_ld8(sa + 16, *reinterpret_cast<uint32_t(*)[8]>(&r[16]));
                     tc_ld8(sa + 24, *reinterpret_cast<uint32_t(*)[8]>(&r[24]));
                 }
+                // this token's page scales (int8), read while the tensor-memory loads are in flight
+                float ks = 1.f, vs = 0.f;
+                if constexpr (KVT == 2) {
+                    const int slot = min(max((tok >> lp) - pg0, 0), pg_hi);
+                    ks = ks_b[slot];
+                    vs = valid ? vs_b[slot] : 0.f;
+                }
                 tc_wait_ld();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&s_free[gi]);
                 // scores (log2 units) of this token for each head
-                const float ks = KVT == 2 ? md.ks[my_lane >> 3] : 1.f;
                 float sc[QGP];
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) {
@@ -655,37 +664,40 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     }
                     sc[g] = (valid && g < u.nh) ? v * qscale[g] * ks : NEG_BIG;
                 }
-                bad |= md.bad;
-                // chunk max per head: warp, then across the group's four warps
-                float mc[QGP];
+                bad |= stage_bad[cur_stage];
+                // chunk max per head (and int8: the largest V scale): warp, then the group's four warps
+                constexpr int NR = KVT == 2 ? QGP + 1 : QGP;
+                float mc[NR];
 #pragma unroll
-                for (int g = 0; g < QGP; ++g) {
-                    float a = sc[g];
+                for (int g = 0; g < NR; ++g) {
+                    float a = g < QGP ? sc[g] : vs;
 #pragma unroll
                     for (int off = 16; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
                     mc[g] = a;
                 }
-                float* rb = gred + 32 * (1 + int(use & 1));  // two alternating reduction slots
+                float* rb = gred + 32 + 40 * int(use & 1);  // two alternating reduction slots
                 if (lane == 0) {
 #pragma unroll
-                    for (int g = 0; g < QGP; ++g) rb[sw * 8 + g] = mc[g];
+                    for (int g = 0; g < NR; ++g) rb[sw * 10 + g] = mc[g];
                 }
                 named_barrier(gbar, UM_SOFT);
                 float pr[QGP];
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) {
-                    const float cm = fmaxf(fmaxf(rb[g], rb[8 + g]), fmaxf(rb[16 + g], rb[24 + g]));
+                    const float cm = fmaxf(fmaxf(rb[g], rb[10 + g]), fmaxf(rb[20 + g], rb[30 + g]));
                     const float mn = fmaxf(m[g], cm);
                     lsum[g] *= exp2f(m[g] - mn);
                     m[g] = mn;
                     pr[g] = sc[g] > 0.5f * NEG_BIG ? exp2f(sc[g] - mn) : 0.f;
                     lsum[g] += pr[g];
                 }
+                float vscale_cur = 0.f;
+                if constexpr (KVT == 2)
+                    vscale_cur = fmaxf(fmaxf(rb[QGP], rb[10 + QGP]), fmaxf(rb[20 + QGP], rb[30 + QGP]));
                 // The group's Phat buffer was last read by the PV product of its previous chunk: fold that
                 // chunk's O first (this also waits for that product), then overwrite.
                 if (have_prev) fold_prev(k_own);
                 uint8_t* pbuf = smem + C::P_OFF + gi * C::PBUF;
-                float vscale_cur = 0.f;
                 if constexpr (KVT == 1) {
                     const int col = (my_lane % 64) * 2, sb = my_lane / 64;
 #pragma unroll
@@ -695,9 +707,9 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                         *reinterpret_cast<__half*>(pbuf + sb * (C::NMAX * 128) + swz_off(g, col)) = hi;
                         *reinterpret_cast<__half*>(pbuf + sb * (C::NMAX * 128) + swz_off(QGP + g, col)) = lo;
                     }
-                    // fp16 V rows past the partition end may hold stale data or dead pool slots:
-                    // zero this token's V row so 0 * NaN cannot reach O.
-                    if (!valid && tok >= u.t1) {
+                    // fp16 V rows outside the partition may hold stale data or dead pool slots, or were
+                    // never loaded: zero this token's V row so 0 * NaN cannot reach O.
+                    if (!valid) {
                         uint8_t* vrow = smem + cur_stage * C::STAGE + NSUB * TILE;
 #pragma unroll
                         for (int sb2 = 0; sb2 < NSUB; ++sb2)
@@ -708,8 +720,6 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 } else {
                     // probability * v_scale / (largest v_scale of the chunk) as an unsigned integer below
                     // 2^30 whose four bytes are the four limbs
-                    vscale_cur = md.vsmax;
-                    const float vs = md.vs[my_lane >> 3];
                     const float f = vscale_cur > 0.f ? vs / vscale_cur * 1073741824.f : 0.f;  // 2^30
 #pragma unroll
                     for (int g = 0; g < QGP; ++g) {
@@ -728,6 +738,10 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 have_prev = true;
                 k_own = k;
             }
+            if (KVT == 2) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&pt_free[qb]);  // the unit's scales are no longer read
+            }
             if (have_prev) fold_prev(k_own);
             // ---- unit epilogue: group sums across its 128 tokens, then the two groups merge
             float L[QGP];
@@ -740,11 +754,12 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             }
             if (lane == 0) {
 #pragma unroll
-                for (int g = 0; g < QGP; ++g) gred[96 + sw * 8 + g] = L[g];
+                for (int g = 0; g < QGP; ++g) gred[112 + sw * 8 + g] = L[g];
             }
             const int grp_bad = named_barrier_or(gbar, UM_SOFT, bad);
 #pragma unroll
-            for (int g = 0; g < QGP; ++g) L[g] = (gred[96 + g] + gred[104 + g]) + (gred[112 + g] + gred[120 + g]);
+            for (int g = 0; g < QGP; ++g)
+                L[g] = (gred[112 + g] + gred[120 + g]) + (gred[128 + g] + gred[136 + g]);
             float* xo = xbuf;                  // [QGP][128] group 1's O rows
             float* xml = xbuf + QGP * UM_D;    // [QGP] m, [QGP] L, [1] bad
             if (gi == 1) {
@@ -812,8 +827,7 @@ cudaError_t launch_one(const DecodeParams& p, const CUtensorMap& tk, const CUten
     const long long upper = (long long)p.B * p.nhg * p.max_parts;
     const long long grid = std::min<long long>(upper, (long long)li.num_sms);
     if (grid <= 0) return cudaSuccess;
-    decode_umma_kernel<KVT, QGP><<<(unsigned)grid, UM_THREADS, C::SMEM, li.stream>>>(tk, tv, p);
-    return cudaGetLastError();
+    return kvb_launch_pdl(decode_umma_kernel<KVT, QGP>, (unsigned)grid, UM_THREADS, C::SMEM, li.stream, tk, tv, p);
 }
 
 template <int KVT>
@@ -826,10 +840,12 @@ cudaError_t launch_kvt(const DecodeParams& p, const CUtensorMap& tk, const CUten
 
 }  // namespace
 
-bool kvb_umma_supported(int kv_type, int D, int page, int qg) {
+bool kvb_umma_supported(int kv_type, int D, int page, int qg, int part_tokens) {
     if (kv_type != 1 && kv_type != 2) return false;
     if (D != 128) return false;
     if (!(page == 8 || page == 16 || page == 32 || page == 64 || page == 128 || page == 256)) return false;
+    // a partition's pages must fit the page table (part_tokens 0: the automatic size, <= 4096)
+    if (part_tokens > 0 && part_tokens / page + 2 > UM_PT) return false;
     return qg >= 1 && qg <= 8;
 }
 

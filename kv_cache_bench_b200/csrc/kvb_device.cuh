@@ -140,6 +140,14 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
+// Programmatic dependent launch. The decode kernels are launched with programmatic stream
+// serialization, so a launch can start (and run its shared-memory setup) while the kernel before it
+// in the stream finishes. Every thread calls pdl_wait() before its first global memory access: it
+// returns once the previous grid has completed and its writes are visible. pdl_trigger() lets the
+// next launch in the stream start as SMs free up; that launch waits for this grid the same way.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void prefetch_l2(const void* ptr) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
 }

@@ -78,6 +78,24 @@ struct LaunchInfo {
     cudaStream_t stream;
 };
 
+// Launches `kernel` with programmatic stream serialization (the kernels call pdl_wait() before
+// touching global memory, so they may start while the previous kernel in the stream finishes).
+template <typename... KArgs, typename... Args>
+cudaError_t kvb_launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
+                           Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 // CUDA-core kernel: every storage type, page size, head dim and group size.
 cudaError_t kvb_launch_decode_simt(const DecodeParams& p, int kv_type, int D, const LaunchInfo& li);
 
@@ -87,9 +105,9 @@ bool kvb_mma_supported(int kv_type, int D, int page, int qg);
 cudaError_t kvb_launch_decode_mma(const DecodeParams& p, int kv_type, int D, const void* tmap_k,
                                   const void* tmap_v, const LaunchInfo& li);
 
-// tcgen05 kernel: fp16/int8, head dim 128, page 8/16/32/64/128/256, qg <= 8; tensor maps with boxes of
-// (128 bytes) x min(page, 128) rows.
-bool kvb_umma_supported(int kv_type, int D, int page, int qg);
+// tcgen05 kernel: fp16/int8, head dim 128, page 8/16/32/64/128/256, qg <= 8, partitions of at most
+// about 526 pages (part_tokens 0: automatic); tensor maps with boxes of (128 bytes) x min(page, 128) rows.
+bool kvb_umma_supported(int kv_type, int D, int page, int qg, int part_tokens);
 cudaError_t kvb_launch_decode_umma(const DecodeParams& p, int kv_type, int D, const void* tmap_k,
                                    const void* tmap_v, const LaunchInfo& li);
 
