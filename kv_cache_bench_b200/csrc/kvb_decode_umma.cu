@@ -46,7 +46,7 @@ constexpr int UM_SOFT = 128;          // threads of one softmax group
 constexpr int UM_D = 128;             // head dim
 constexpr int TILE = UM_CHUNK * 128;  // bytes of one [128 rows][128 B] swizzled tile
 constexpr int UM_PT = 528;            // page-table entries: pages of one partition, at most
-constexpr int UM_GRED = 160;          // reduction floats per softmax group
+constexpr int UM_GRED = 176;          // reduction floats per softmax group
 
 // ---- tcgen05 wrappers -----------------------------------------------------------------------------
 
@@ -124,6 +124,29 @@ __device__ __forceinline__ uint32_t swz_off(int row, int col) {
     return row * 128 + ((((col >> 4) ^ row) & 7) << 4) + (col & 15);
 }
 
+// Exact float of an integer |x| < 2^22 with two full-rate instructions (1.5 * 2^23 has a unit ulp)
+// instead of a conversion. The int32 limb products of one chunk stay below 2^22: 128 terms of at
+// most 128 * 128 (QK^T: int8 K times signed q limbs) or 128 * 255 (PV: int8 V times probability
+// bytes).
+__device__ __forceinline__ float small_int_to_float(int x) {
+    return __int_as_float(x + 0x4B400000) - 12582912.0f;
+}
+
+// Four int32 limb products (high first) recombined: ((r0 * 256 + r1) * 256 + r2) * 256 + r3.
+__device__ __forceinline__ float limbs_to_float(uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+    return ((small_int_to_float(int(r0)) * 256.f + small_int_to_float(int(r1))) * 256.f +
+            small_int_to_float(int(r2))) * 256.f + small_int_to_float(int(r3));
+}
+
+__device__ __forceinline__ float max4(float4 v) { return fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)); }
+
+// Largest value among the 32 lanes of the warp (redux.sync on floats, sm_100a).
+__device__ __forceinline__ float warp_max(float v) {
+    float r;
+    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+    return r;
+}
+
 // Splits a non-negative or signed integer |x| < 2^30 into four signed 8-bit limbs, high first.
 __device__ __forceinline__ void limbs4(int x, int8_t (&l)[4]) {
 #pragma unroll
@@ -139,7 +162,7 @@ template <int KVT>
 struct UCfg {
     static constexpr int NSUB = KVT == 1 ? 2 : 1;             // 128-byte column slices of a row
     static constexpr int STAGE = 2 * NSUB * TILE;              // K tiles, then V tiles
-    static constexpr int STAGES = KVT == 1 ? 3 : 5;
+    static constexpr int STAGES = KVT == 1 ? 3 : 6;
     static constexpr int NMAX = KVT == 1 ? 16 : 32;            // MMA N (rows of Qhat / Phat)
     static constexpr int QBUF = NMAX * 128 * NSUB;             // one Qhat^T buffer ([N][128 B] per slice)
     static constexpr int PBUF = NMAX * 128 * NSUB;             // one Phat^T buffer
@@ -157,10 +180,8 @@ struct UCfg {
     static constexpr size_t PT_BYTES = sizeof(int) * UM_PT * (KVT == 2 ? 5 : 1);
     static constexpr size_t PREFIX_OFF = WIN_OFF + PT_BYTES;
     static constexpr size_t SCRATCH_OFF = kvb_align_up(PREFIX_OFF + sizeof(int) * (KVB_PREFIX_MAX + 1), 16);
-    static constexpr size_t SCRATCH_FLOATS = 1024;             // final merge weights, prefix scan
-    static constexpr size_t XBUF_OFF = SCRATCH_OFF + SCRATCH_FLOATS * sizeof(float);
-    static constexpr size_t XBUF_FLOATS = 8 * 128 + 2 * 8 + 4;  // group 1's O rows, max, sums, bad flag
-    static constexpr size_t MISC_OFF = kvb_align_up(XBUF_OFF + XBUF_FLOATS * sizeof(float), 64);
+    static constexpr size_t SCRATCH_FLOATS = 512;              // final merge weights, prefix scan
+    static constexpr size_t MISC_OFF = kvb_align_up(SCRATCH_OFF + SCRATCH_FLOATS * sizeof(float), 64);
     static constexpr size_t SMEM = MISC_OFF + 64 + 1024;
 };
 
@@ -170,6 +191,7 @@ static_assert(UCfg<1>::MISC_OFF % 64 == 0 && UCfg<2>::MISC_OFF % 64 == 0, "align
 static_assert(UCfg<1>::Q_OFF % 1024 == 0 && UCfg<1>::P_OFF % 1024 == 0 && UCfg<2>::P_OFF % 1024 == 0,
               "swizzled operands need 1024-byte alignment");
 static_assert(UCfg<2>::SCRATCH_FLOATS >= UM_THREADS, "prefix scan scratch");
+static_assert(UCfg<1>::PBUF >= 8 * 128 * 4 && UCfg<2>::PBUF >= 8 * 128 * 4, "group 1's O rows fit its Phat buffer");
 
 template <int KVT, int QGP>  // QGP: query heads per group, padded to 1, 2, 4 or 8
 __global__ void __launch_bounds__(UM_THREADS, 1)
@@ -205,7 +227,6 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     float* pt_vs = pt_ks + 2 * UM_PT;                         // int8 only: [2][UM_PT]
     int* s_prefix = reinterpret_cast<int*>(smem + C::PREFIX_OFF);
     float* scratch = reinterpret_cast<float*>(smem + C::SCRATCH_OFF);
-    float* xbuf = reinterpret_cast<float*>(smem + C::XBUF_OFF);
     volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::MISC_OFF);
     int* s_flag = reinterpret_cast<int*>(smem + C::MISC_OFF + 8);
     uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF + 16);
@@ -498,7 +519,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         // this warp's tensor-memory lane quarter is fixed by warp % 4
         const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;
         const int my_lane = (warp & 3) * 32 + lane;  // token in S^T, head dim in O^T
-        // [0,32) q absmax; [32,112) chunk max x2 ([warp][10]: 8 heads, V scale); [112,144) sums
+        // [0,32) q absmax; [32,112) chunk max x2 ([value][warp]: 8 heads, V scale); [112,144) sums;
+        // group 1: [144,161) state handed to group 0 at the unit's end
         float* gred = red + gi * UM_GRED;
         UnitCursor cur{&p, prefix, (long long)blockIdx.x, total};
         Unit u;
@@ -523,19 +545,15 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) {
                     x[g] = g < u.nh ? __ldg(p.q + ((size_t)u.b * p.H + u.h0 + g) * UM_D + d) * p.q_scale : 0.f;
-                    float a = fabsf(x[g]);
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-                    amax[g] = a;
+                    amax[g] = warp_max(fabsf(x[g]));
                 }
                 if (lane == 0) {
 #pragma unroll
-                    for (int g = 0; g < QGP; ++g) gred[sw * 8 + g] = amax[g];
+                    for (int g = 0; g < QGP; ++g) gred[g * 4 + sw] = amax[g];
                 }
                 named_barrier(gbar, UM_SOFT);
 #pragma unroll
-                for (int g = 0; g < QGP; ++g)
-                    amax[g] = fmaxf(fmaxf(gred[g], gred[8 + g]), fmaxf(gred[16 + g], gred[24 + g]));
+                for (int g = 0; g < QGP; ++g) amax[g] = max4(reinterpret_cast<const float4*>(gred)[g]);
                 uint8_t* qbuf = smem + C::Q_OFF + qb * C::QBUF;
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) {
@@ -601,18 +619,24 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 }
                 tc_wait_ld();
                 tc_fence_before();
+                bool moved = false;  // the max moved since the previous chunk (group-uniform)
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) moved |= m_prev[g] != m[g];
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) {
                     float v;
                     if constexpr (KVT == 1) {
                         v = __uint_as_float(r[g]) + __uint_as_float(r[QGP + g]);
                     } else {
-                        v = (((float(int(r[4 * g])) * 256.f + float(int(r[4 * g + 1]))) * 256.f +
-                              float(int(r[4 * g + 2]))) * 256.f + float(int(r[4 * g + 3]))) *
+                        v = limbs_to_float(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]) *
                             (vscale_prev * 9.313225746154785e-10f);  // 2^-30
                     }
                     // o and the previous chunk are both relative to m_prev; move them to the current max
-                    o[g] = (o[g] + v) * exp2f(m_prev[g] - m[g]);
+                    o[g] += v;
+                }
+                if (moved) {
+#pragma unroll
+                    for (int g = 0; g < QGP; ++g) o[g] *= exp2f(m_prev[g] - m[g]);
                 }
             };
 
@@ -659,8 +683,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     if constexpr (KVT == 1) {
                         v = __uint_as_float(r[g]) + __uint_as_float(r[QGP + g]);
                     } else {
-                        v = ((float(int(r[4 * g])) * 256.f + float(int(r[4 * g + 1]))) * 256.f +
-                             float(int(r[4 * g + 2]))) * 256.f + float(int(r[4 * g + 3]));
+                        v = limbs_to_float(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]);
                     }
                     sc[g] = (valid && g < u.nh) ? v * qscale[g] * ks : NEG_BIG;
                 }
@@ -669,31 +692,32 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 constexpr int NR = KVT == 2 ? QGP + 1 : QGP;
                 float mc[NR];
 #pragma unroll
-                for (int g = 0; g < NR; ++g) {
-                    float a = g < QGP ? sc[g] : vs;
-#pragma unroll
-                    for (int off = 16; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
-                    mc[g] = a;
-                }
-                float* rb = gred + 32 + 40 * int(use & 1);  // two alternating reduction slots
+                for (int g = 0; g < NR; ++g) mc[g] = warp_max(g < QGP ? sc[g] : vs);
+                float* rb = gred + 32 + 40 * int(use & 1);  // two alternating reduction slots, [value][warp]
                 if (lane == 0) {
 #pragma unroll
-                    for (int g = 0; g < NR; ++g) rb[sw * 10 + g] = mc[g];
+                    for (int g = 0; g < NR; ++g) rb[g * 4 + sw] = mc[g];
                 }
                 named_barrier(gbar, UM_SOFT);
-                float pr[QGP];
+                float pr[QGP], mn[QGP];
+                bool moved = false;  // a running max changed (group-uniform: one branch, no divergence)
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) {
-                    const float cm = fmaxf(fmaxf(rb[g], rb[10 + g]), fmaxf(rb[20 + g], rb[30 + g]));
-                    const float mn = fmaxf(m[g], cm);
-                    lsum[g] *= exp2f(m[g] - mn);
-                    m[g] = mn;
-                    pr[g] = sc[g] > 0.5f * NEG_BIG ? exp2f(sc[g] - mn) : 0.f;
+                    mn[g] = fmaxf(m[g], max4(reinterpret_cast<const float4*>(rb)[g]));
+                    moved |= mn[g] != m[g];
+                }
+                if (moved) {
+#pragma unroll
+                    for (int g = 0; g < QGP; ++g) lsum[g] *= exp2f(m[g] - mn[g]);
+                }
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) {
+                    m[g] = mn[g];
+                    pr[g] = sc[g] > 0.5f * NEG_BIG ? exp2f(sc[g] - mn[g]) : 0.f;
                     lsum[g] += pr[g];
                 }
                 float vscale_cur = 0.f;
-                if constexpr (KVT == 2)
-                    vscale_cur = fmaxf(fmaxf(rb[QGP], rb[10 + QGP]), fmaxf(rb[20 + QGP], rb[30 + QGP]));
+                if constexpr (KVT == 2) vscale_cur = max4(reinterpret_cast<const float4*>(rb)[QGP]);
                 // The group's Phat buffer was last read by the PV product of its previous chunk: fold that
                 // chunk's O first (this also waits for that product), then overwrite.
                 if (have_prev) fold_prev(k_own);
@@ -754,14 +778,18 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             }
             if (lane == 0) {
 #pragma unroll
-                for (int g = 0; g < QGP; ++g) gred[112 + sw * 8 + g] = L[g];
+                for (int g = 0; g < QGP; ++g) gred[112 + g * 4 + sw] = L[g];
             }
             const int grp_bad = named_barrier_or(gbar, UM_SOFT, bad);
 #pragma unroll
-            for (int g = 0; g < QGP; ++g)
-                L[g] = (gred[112 + g] + gred[120 + g]) + (gred[128 + g] + gred[136 + g]);
-            float* xo = xbuf;                  // [QGP][128] group 1's O rows
-            float* xml = xbuf + QGP * UM_D;    // [QGP] m, [QGP] L, [1] bad
+            for (int g = 0; g < QGP; ++g) {
+                const float4 l4 = reinterpret_cast<const float4*>(gred + 112)[g];
+                L[g] = (l4.x + l4.y) + (l4.z + l4.w);
+            }
+            // Group 1 hands its state over in its own Phat buffer (its last PV product is done: the
+            // fold above waited for it) and in the spare end of its reduction floats.
+            float* xo = reinterpret_cast<float*>(smem + C::P_OFF + C::PBUF);  // [QGP][128] O rows
+            float* xml = red + UM_GRED + 144;                               // [QGP] m, [QGP] L, [1] bad
             if (gi == 1) {
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) xo[g * UM_D + my_lane] = o[g];
