@@ -170,6 +170,26 @@ int kvb_paged_workspace_bytes(const kvb_paged_args* args, size_t* bytes);
  * the buffers. Calls that share one workspace must not overlap on the device. */
 int kvb_paged_decode_async(const kvb_paged_args* args, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Bytes of the library-owned workspace of kvb_paged_decode_static (16 MiB per device). */
+#define KVB_STATIC_WORKSPACE_BYTES (16u << 20)
+
+/* kvb_paged_decode_async without a caller workspace: the step's split-K partials, arrival counters
+ * and error word live in a 16 MiB array of the library's own device memory, so the call allocates
+ * nothing (no cudaMalloc, cudaFree or allocator of any library). No counterpart in the reference,
+ * whose run_paged owns its buffers. For callers that cannot allocate device memory on their call
+ * path: a plain C or FFI caller without a device allocator, or a latency-critical loop where an
+ * allocation (which can synchronize the device) is not allowed.
+ * Limits: a call whose workspace (kvb_paged_workspace_bytes: about batch x heads x partitions x
+ * head_dim x 4 bytes) exceeds KVB_STATIC_WORKSPACE_BYTES is refused with KVB_ERR_INVALID and
+ * launches nothing. Every call on a device uses the same array: calls that overlap on the device
+ * (different streams without ordering, or several host threads) race on it, so serialize them.
+ * The array starts zeroed at module load, which is what its error word and split-K counters need;
+ * every completed call leaves the counters ready for the next. Bad lengths or block ids give NaN
+ * outputs as in kvb_paged_decode_async (the error word itself is not exposed here).
+ * The first call on each device looks up the array's address and sets kernel attributes: make it
+ * outside any stream capture. */
+int kvb_paged_decode_static(const kvb_paged_args* args, void* stream);
+
 /* Reads and clears the error flag of a workspace (synchronizes `stream`). *flag = 0: no bad
  * length or block id since the last read. Bits: 1 bad length, 2 bad block id, 4 a bounded device
  * wait gave up, 8 a split-K arrival counter counted past its partition count (two launches sharing

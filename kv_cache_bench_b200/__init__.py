@@ -107,6 +107,7 @@ _c_ws_bytes = _sig("kvb_paged_workspace_bytes", ctypes.c_int, ctypes.POINTER(_CP
                    ctypes.POINTER(ctypes.c_size_t))
 _c_decode_async = _sig("kvb_paged_decode_async", ctypes.c_int, ctypes.POINTER(_CPagedArgs), ctypes.c_void_p,
                        ctypes.c_size_t, ctypes.c_void_p)
+_c_decode_static = _sig("kvb_paged_decode_static", ctypes.c_int, ctypes.POINTER(_CPagedArgs), ctypes.c_void_p)
 _c_error_flag = _sig("kvb_paged_error_flag", ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                      ctypes.POINTER(ctypes.c_int))
 
@@ -344,6 +345,14 @@ def paged_part_tokens(c: _CPagedArgs) -> int:
 def paged_decode_async(c: _CPagedArgs, workspace: int, workspace_bytes: int, stream: int = 0) -> None:
     _check(_c_decode_async(ctypes.byref(c), workspace or None, int(workspace_bytes), stream or None),
            "paged_decode_async")
+
+
+def paged_decode_static(c: _CPagedArgs, stream: int = 0) -> None:
+    """kvb_paged_decode_static: one decode step with the library-owned workspace (no allocation)."""
+    _check(_c_decode_static(ctypes.byref(c), stream or None), "paged_decode_static")
+
+
+STATIC_WORKSPACE_BYTES = 16 << 20
 
 
 def paged_error_flag(workspace: int, stream: int = 0) -> int:

@@ -473,6 +473,48 @@ int kvb_paged_decode_async(const kvb_paged_args* a, void* workspace, size_t work
     return launch_paged(a, workspace, static_cast<cudaStream_t>(stream));
 }
 
+// ---- library-owned workspace ---------------------------------------------------------------------
+
+// The workspace of kvb_paged_decode_static: device memory of the library's own module (zero at module
+// load), so the call path allocates nothing. One per device; calls on a device share it.
+static __device__ __align__(256) unsigned char g_static_workspace[KVB_STATIC_WORKSPACE_BYTES];
+
+// Device address of g_static_workspace on the current device, looked up once per device (with that
+// device current) and cached.
+int static_workspace(void** out) {
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static void* addr[kMaxDevices] = {};
+    int dev = 0;
+    KVB_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(KVB_ERR_DEVICE, "device ordinal out of range for the static workspace");
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_workspace);
+        if (e != cudaSuccess || !p)
+            return fail(KVB_ERR_DEVICE, std::string("static workspace address: ") + cudaGetErrorString(e));
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return KVB_OK;
+}
+
+int kvb_paged_decode_static(const kvb_paged_args* a, void* stream) {
+    if (int rc = check_static(a)) return rc;
+    size_t need = 0;
+    if (int rc = kvb_paged_workspace_bytes(a, &need)) return rc;
+    if (need > KVB_STATIC_WORKSPACE_BYTES)
+        return fail(KVB_ERR_INVALID, "this call needs a " + std::to_string(need) +
+                                         "-byte workspace (batch x heads x partitions x head_dim floats and more); "
+                                         "the static workspace holds " +
+                                         std::to_string((size_t)KVB_STATIC_WORKSPACE_BYTES) +
+                                         " bytes: use kvb_paged_decode_async with a workspace of that size");
+    void* ws = nullptr;
+    if (int rc = static_workspace(&ws)) return rc;
+    return launch_paged(a, ws, static_cast<cudaStream_t>(stream));
+}
+
 int kvb_paged_error_flag(void* workspace, void* stream, int* flag) {
     if (!workspace || !flag) return fail(KVB_ERR_INVALID, "null workspace or flag");
     unsigned h = 0;
