@@ -248,27 +248,31 @@ class Shard:
 # ---------------------------------------------------------------------------------------------------
 # CPU baseline (the reference's own implementation, or the oracle port when it was not built)
 
-def cpu_baseline(w, steps: int, budget_tokens: int):
-    """Times the reference's CPU step on a bounded sample of the workload: whole sequences, in order,
-    until `budget_tokens` (at least one sequence). Returns the cpu_baseline object."""
-    lens = []
+def sample_lens(w, budget_tokens: int):
+    """The first sequences of the workload, in order, up to `budget_tokens` tokens; the last one taken
+    may be cut to a prefix of its context (a shorter step of the same shape)."""
+    lens, left = [], max(1, int(budget_tokens))
     for l in w["lens"]:
-        if lens and sum(lens) + l > budget_tokens:
+        if left <= 0:
             break
-        lens.append(l)
+        lens.append(min(l, left))
+        left -= lens[-1]
+    return lens
+
+
+def time_cpu_reference(w, lens, steps: int):
+    """ms per step and bytes per step (Workload::min_bytes, src/workload.hpp:69-74) of the reference's
+    CPU implementation on `lens`: oracle/_ref/kvb_ref_cpu (the reference's attention_reference with
+    all host threads), else the C restatement in oracle/."""
     exe = os.path.join(ROOT, "oracle", "_ref", "kvb_ref_cpu")
     threads = os.cpu_count() or 1
-    sample = (f"{len(lens)} of {len(w['lens'])} sequences ({sum(lens)} tokens, "
-              f"{100.0 * sum(lens) / sum(w['lens']):.1f}% of the step), {steps} timed steps after 1 warm-up")
     if os.path.exists(exe):
         cmd = [exe, f"--heads={w['H']}", f"--kv-heads={w['Hkv']}", f"--dim={w['D']}", f"--type={w['kv']}",
                f"--page={w['page']}", f"--lens={','.join(map(str, lens))}", f"--steps={steps}",
                f"--seed={w['seed']}", f"--threads={threads}"]
         r = json.loads(subprocess.run(cmd, check=True, capture_output=True, text=True).stdout.strip().splitlines()[-1])
-        gbps = r["min_bytes"] / (r["ms_per_step"] * 1e-3) / 1e9
-        return {"value": round(gbps, 4), "unit": "GB/s", "cores": r["threads"], "kind": "reference",
-                "ms_per_step": round(r["ms_per_step"], 3), "sample": sample,
-                "impl": "reference attention_reference (fp64, src/reference.cpp:65-100), oracle/_ref/kvb_ref_cpu"}
+        return r["ms_per_step"], float(r["min_bytes"]), r["threads"], "reference", \
+            "reference attention_reference (fp64, src/reference.cpp:65-100), oracle/_ref/kvb_ref_cpu"
     import oracle
     kvt = {"f32": oracle.F32, "f16": oracle.F16, "i8": oracle.I8}[w["kv"]]
     case = oracle.make_case(num_heads=w["H"], num_kv_heads=w["Hkv"], head_dim=w["D"], lens=lens, kv_type=kvt,
@@ -278,27 +282,55 @@ def cpu_baseline(w, steps: int, budget_tokens: int):
     for _ in range(steps):
         case.reference(threads)
     ms = (time.perf_counter() - t0) / steps * 1e3
-    return {"value": round(case.min_bytes() / (ms * 1e-3) / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-            "ms_per_step": round(ms, 3), "sample": sample, "impl": "oracle/kvb_oracle.c (C restatement)"}
+    return ms, case.min_bytes(), threads, "port", "oracle/kvb_oracle.c (C restatement)"
 
 
-def cpu_budget(w):
-    return {1: 1 << 30, 2: 1 << 30, 3: 1 << 30, 4: 65536, 5: 140000}[w["cfg"]]
+def cpu_sample(w, step_seconds: float):
+    """Token budget of one CPU step that takes about `step_seconds` (calibrated on a short sample)."""
+    probe = sample_lens(w, 4096)
+    ms, _, _, _, _ = time_cpu_reference(w, probe, 1)
+    tokens_per_s = sum(probe) / max(ms * 1e-3, 1e-6)
+    return max(128, int(tokens_per_s * step_seconds))
+
+
+def cpu_baseline(w, seconds: float = 12.0):
+    """The reference's CPU step timed on a bounded sample of the workload (about `seconds` of CPU
+    work): the whole step when it takes under a quarter of that, else a token-bounded prefix."""
+    total = sum(w["lens"])
+    budget = min(total, cpu_sample(w, seconds / 4))
+    lens = sample_lens(w, budget)
+    ms1, _, _, _, _ = time_cpu_reference(w, lens, 1)
+    steps = int(max(2, min(1000, seconds / max(ms1 * 1e-3, 1e-6))))
+    ms, nbytes, threads, kind, impl = time_cpu_reference(w, lens, steps)
+    sample = (f"{len(lens)} of {len(w['lens'])} sequences, {sum(lens)} of {total} tokens "
+              f"({100.0 * sum(lens) / total:.1f}% of the step), {steps} timed steps after 1 warm-up")
+    return {"value": round(nbytes / (ms * 1e-3) / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": kind,
+            "ms_per_step": round(ms, 3), "sample": sample, "impl": impl}
 
 
 def run_reference_arm(args, w):
+    """`--impl reference`: the reference's own CPU implementation of the step, on rank 0 only, each of
+    the W + K steps a bounded sample of the workload so that the run ends within about a minute."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    cb = cpu_baseline(w, max(args.steps, 1), cpu_budget(w))
+    steps = max(args.steps, 1)
+    total = sum(w["lens"])
+    budget = min(total, cpu_sample(w, 60.0 / (steps + max(args.warmup, 1))))
+    lens = sample_lens(w, budget)
+    ms, nbytes, threads, kind, impl = time_cpu_reference(w, lens, steps)
+    value = round(nbytes / (ms * 1e-3) / 1e9, 4)
+    sample = (f"{len(lens)} of {len(w['lens'])} sequences, {sum(lens)} of {total} tokens "
+              f"({100.0 * sum(lens) / total:.1f}% of the step) per step, {steps} timed steps after 1 warm-up")
+    cb = {"value": value, "unit": "GB/s", "cores": threads, "kind": kind, "ms_per_step": round(ms, 3),
+          "sample": sample, "impl": impl}
     line = {
-        "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "GB/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_step"], "higher_is_better": True,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
         "scaling": "weak" if w["shard"] == "replica" else "strong", "vs_baseline": None, "dtype": w["kv"],
         "data": "synthetic: the reference's own seeded Workload generator", "config": config_obj(w, None, world),
-        "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
-                                    "d2h_bytes_per_step": 0},
+        "cpu_baseline": cb, "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -487,7 +519,7 @@ def main():
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            cb = cpu_baseline(w, 2, cpu_budget(w))
+            cb = cpu_baseline(w)
         except Exception as ex:  # noqa: BLE001
             cb = {"value": None, "error": str(ex)[:200]}
 
