@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
             merge_slots_and_store<D>(p, u, epi_o, epi_ml, NCW, g0, min(KVB_EPI_HEADS, u.nh - g0), o_scale, tid,
                                      NCW * 32);
         }
-        finish_partition<D>(p, u, tid, NCW * 32, 1, s_flag, epi_o, NCW * KVB_EPI_HEADS * D);
+        finish_partition<D>(p, u, tid, NCW * 32, 1, s_flag);
         named_barrier(1, NCW * 32);
     }
 }

@@ -235,7 +235,7 @@ __global__ void __launch_bounds__(SIMT_THREADS) decode_simt_kernel(const DecodeP
             merge_slots_and_store<D>(p, u, s_slot_o, s_slot_ml, SIMT_SLOTS, g0, min(KVB_EPI_HEADS, u.nh - g0),
                                      o_scale, tid, SIMT_THREADS);
         }
-        finish_partition<D>(p, u, tid, SIMT_THREADS, 1, &s_flag, s_slot_o, SIMT_SLOTS * KVB_EPI_HEADS * D);
+        finish_partition<D>(p, u, tid, SIMT_THREADS, 1, &s_flag);
         __syncthreads();
     }
 }

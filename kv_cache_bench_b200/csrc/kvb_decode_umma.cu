@@ -5,17 +5,19 @@
 // tokens, then a weighted merge of the partitions. Shapes: head dim 128, fp16 or int8 pools, page
 // size 8, 16, 32, 64, 128 or 256, up to 8 query heads per KV-head group.
 //
-// One CTA per SM, warp-specialized (11 warps):
-//   warp 0      TMA producer: reads the unit's block ids (and int8 scales) once into a shared-memory
+// One CTA per SM, warp-specialized (12 warps in three warpgroups; the control warpgroup hands
+// registers to the two softmax warpgroups with setmaxnreg):
+//   warps 0-7   two softmax groups of 4 warps (below).
+//   warp 8      TMA producer: reads the unit's block ids (and int8 scales) once into a shared-memory
 //               page table, then for each 128-token chunk issues 2-D tile loads of the K and V rows
 //               of every page in the chunk (128-byte swizzle) into a ring of shared-memory stages.
-//   warps 1, 10 MMA issuers (one thread each), for the even and the odd chunks of the running chunk
+//   warps 9, 10 MMA issuers (one thread each), for the even and the odd chunks of the running chunk
 //               index:
 //                 S^T[128 tokens x N] = K[128 x 128] . Qhat^T[128 x N]      (tensor memory)
 //                 O^T[128 dims x N]   = V^T[128 x 128 tokens] . Phat^T       (tensor memory)
 //               reading K (K-major) and V (MN-major, the transposed view of the same TMA tile)
 //               straight from the stage. tcgen05.commit releases the stage and signals the softmax.
-//   warps 2-9   two softmax groups of 4 warps (128 threads, one per tensor-memory lane), group g for
+//   warps 0-7   two softmax groups of 4 warps (128 threads, one per tensor-memory lane), group g for
 //               the chunks of parity g: thread t reads token t's scores, the four warps agree on the
 //               chunk max per head, write Phat^T to shared memory, and after the PV product thread d
 //               folds O^T row d into registers. The groups merge once per unit.
@@ -40,8 +42,14 @@ namespace {
 using namespace kvb_dev;
 
 constexpr int UM_CHUNK = 128;         // tokens per stage = MMA M for QK^T
-constexpr int UM_WARPS = 11;          // producer, MMA (even chunks), 8 softmax, MMA (odd chunks)
+constexpr int UM_WARPS = 12;          // 8 softmax, producer, MMA (even chunks), MMA (odd chunks), TMEM owner
 constexpr int UM_THREADS = UM_WARPS * 32;
+constexpr int UM_PRODUCER = 8, UM_MMA0 = 9, UM_MMA1 = 10, UM_TMEM_WARP = 11;
+// Registers per thread after the split (the launch gives every thread 168: 65536 / 384, rounded
+// down to 8). The control warpgroup keeps 72, the softmax warpgroups get 216; the shares add up to at
+// most the launch's total, or setmaxnreg.inc would wait forever.
+constexpr int UM_REGS_LAUNCH = 168, UM_REGS_CTRL = 72, UM_REGS_SOFT = 216;
+static_assert(2 * 128 * UM_REGS_SOFT + 128 * UM_REGS_CTRL <= UM_THREADS * UM_REGS_LAUNCH, "register split");
 constexpr int UM_SOFT = 128;          // threads of one softmax group
 constexpr int UM_D = 128;             // head dim
 constexpr int TILE = UM_CHUNK * 128;  // bytes of one [128 rows][128 B] swizzled tile
@@ -88,6 +96,12 @@ __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t
             : "memory");
     }
 }
+
+// Warpgroup register split (all four warps of a warpgroup execute the same one).
+template <int N>
+__device__ __forceinline__ void reg_alloc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N>
+__device__ __forceinline__ void reg_dealloc() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
 
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
@@ -179,8 +193,9 @@ struct UCfg {
     // page table: block ids [UM_PT]; int8: scales [2 buffers][UM_PT] for K and for V
     static constexpr size_t PT_BYTES = sizeof(int) * UM_PT * (KVT == 2 ? 5 : 1);
     static constexpr size_t PREFIX_OFF = WIN_OFF + PT_BYTES;
-    static constexpr size_t SCRATCH_OFF = kvb_align_up(PREFIX_OFF + sizeof(int) * (KVB_PREFIX_MAX + 1), 16);
-    static constexpr size_t SCRATCH_FLOATS = 512;              // final merge weights, prefix scan
+    static constexpr size_t LENS_OFF = PREFIX_OFF + sizeof(int) * (KVB_PREFIX_MAX + 1);
+    static constexpr size_t SCRATCH_OFF = kvb_align_up(LENS_OFF + sizeof(int) * KVB_PREFIX_MAX, 16);
+    static constexpr size_t SCRATCH_FLOATS = 512;              // prefix scan
     static constexpr size_t MISC_OFF = kvb_align_up(SCRATCH_OFF + SCRATCH_FLOATS * sizeof(float), 64);
     static constexpr size_t SMEM = MISC_OFF + 64 + 1024;
 };
@@ -226,6 +241,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     float* pt_ks = reinterpret_cast<float*>(pt_blk + UM_PT);  // int8 only: [2][UM_PT]
     float* pt_vs = pt_ks + 2 * UM_PT;                         // int8 only: [2][UM_PT]
     int* s_prefix = reinterpret_cast<int*>(smem + C::PREFIX_OFF);
+    int* s_lens = reinterpret_cast<int*>(smem + C::LENS_OFF);
     float* scratch = reinterpret_cast<float*>(smem + C::SCRATCH_OFF);
     volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::MISC_OFF);
     int* s_flag = reinterpret_cast<int*>(smem + C::MISC_OFF + 8);
@@ -264,7 +280,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         *s_abort = 0;
         fence_mbarrier_init();
     }
-    if (warp == 1) {
+    if (warp == UM_TMEM_WARP) {
         tc_alloc(s_tmem, 128);
         tc_relinquish();
     }
@@ -281,7 +297,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     pdl_trigger();
     const int* prefix = nullptr;
     if (p.B <= KVB_PREFIX_MAX) {
-        build_unit_prefix(p, s_prefix, reinterpret_cast<int*>(scratch), tid, UM_THREADS, 1);
+        build_unit_prefix(p, s_prefix, reinterpret_cast<int*>(scratch), tid, UM_THREADS, 1, s_lens);
         prefix = s_prefix;
     }
     const long long total = unit_total(p, prefix);
@@ -293,10 +309,11 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
     };
 
-    if (warp == 0) {
+    if (warp >= 8) reg_dealloc<UM_REGS_CTRL>();  // the split happens in each role's own code
+    if (warp == UM_PRODUCER) {
         // ------------------------------------------------------------------ TMA producer
         const uint64_t policy = l2_evict_first_policy();
-        UnitCursor cur{&p, prefix, (long long)blockIdx.x, total};
+        UnitCursor cur{&p, prefix, (long long)blockIdx.x, total, prefix ? s_lens : nullptr};
         Unit u;
         int stage = 0;
         uint32_t phase = 0;
@@ -389,16 +406,16 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             }
             ++unit_no;
         }
-    } else if (warp == 1 || warp == UM_WARPS - 1) {
+    } else if (warp == UM_MMA0 || warp == UM_MMA1) {
         // ------------------------------------------------------------------ MMA issuers
-        // Warp 1 issues the products of the even chunks (running index), warp 10 those of the odd
+        // Warp 9 issues the products of the even chunks (running index), warp 10 those of the odd
         // ones, each into its own S^T and O^T buffers. One thread per warp polls: each pass issues the
         // oldest pending O^T product if its Phat is written (that releases the stage to the producer),
         // and the next S^T product if its stage is loaded and the previous S^T of this parity was read
         // (so the softmax finds S^T_k ready when it finishes chunk k-2). Neither waits behind the other.
         // QK for int8: A = K (signed), B = q limbs (signed). PV: A = V (signed), B = probability
         // bytes (unsigned).
-        const int par = warp == 1 ? 0 : 1;
+        const int par = warp == UM_MMA0 ? 0 : 1;
         if (lane == 0) {
             const uint32_t idesc_qk =
                 KVT == 1 ? instr_desc(1, 0, 0, 0, 0, N, 128) : instr_desc(2, 1, 1, 0, 0, N, 128);
@@ -407,7 +424,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             constexpr int KQK = KVT == 1 ? 16 : 32;  // contraction elements per instruction
             const uint32_t s_tm = tmem + 32 * par, o_tm = tmem + 64 + 32 * par;
             const uint32_t pb = sbase + uint32_t(C::P_OFF) + par * C::PBUF;
-            UnitCursor cur{&p, prefix, (long long)blockIdx.x, total};
+            UnitCursor cur{&p, prefix, (long long)blockIdx.x, total, prefix ? s_lens : nullptr};
             Unit u;
             bool have_unit = false, units_done = false, need_q = false;
             int unit_no = -1, qb = 0;
@@ -507,13 +524,14 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 }
             }
         }
-    } else {
+    } else if (warp < 8) {
         // ------------------------------------------------------------------ softmax / accumulation
+        reg_alloc<UM_REGS_SOFT>();
         // Two warpgroups take alternate chunks: group gi handles the chunks whose running index k has
         // k & 1 == gi, with its own tensor-memory S/O buffers and Phat buffer, and its own running
         // (max, sum, O). The groups merge once per unit.
-        const int gi = (warp - 2) >> 2;
-        const int gt = tid - 64 - gi * UM_SOFT;  // 0..127 within the group
+        const int gi = warp >> 2;
+        const int gt = tid - gi * UM_SOFT;  // 0..127 within the group
         const int sw = gt >> 5;                  // warp within the group
         const uint32_t gbar = 2 + gi;            // named barrier of the group
         // this warp's tensor-memory lane quarter is fixed by warp % 4
@@ -522,7 +540,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         // [0,32) q absmax; [32,112) chunk max x2 ([value][warp]: 8 heads, V scale); [112,144) sums;
         // group 1: [144,161) state handed to group 0 at the unit's end
         float* gred = red + gi * UM_GRED;
-        UnitCursor cur{&p, prefix, (long long)blockIdx.x, total};
+        UnitCursor cur{&p, prefix, (long long)blockIdx.x, total, prefix ? s_lens : nullptr};
         Unit u;
         int stage = 0;
         int k = 0;  // running chunk index
@@ -828,9 +846,9 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                         if (d == 0) p.part_ml[slot] = make_float2(m[g], any_bad ? nanv : L[g]);
                     }
                 }
-                finish_partition<UM_D>(p, u, gt, UM_SOFT, gbar, s_flag, scratch, int(C::SCRATCH_FLOATS));
-                named_barrier(gbar, UM_SOFT);
             }
+            // both groups: count the partition in; the last partition's CTA merges them all
+            finish_partition<UM_D, 12>(p, u, tid, 2 * UM_SOFT, 4, s_flag);
             ++unit_no;
         }
     }
@@ -839,7 +857,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tc_dealloc(tmem, 128);
+    if (warp == UM_TMEM_WARP) tc_dealloc(tmem, 128);
 }
 
 template <int KVT, int QGP>

@@ -266,6 +266,7 @@ struct UnitCursor {
     const DecodeParams* p;
     const int* prefix;  // nullptr: dense enumeration
     long long next, total;
+    const int* lens = nullptr;  // sequence lengths cached in shared memory (prefix mode), or nullptr
 
     __device__ __forceinline__ bool advance(Unit& u) {
         const DecodeParams& P = *p;
@@ -281,7 +282,7 @@ struct UnitCursor {
                     else hi = mid - 1;
                 }
                 const int b = lo;
-                const int len = __ldg(P.seq_lens + b);
+                const int len = lens ? lens[b] : __ldg(P.seq_lens + b);
                 bool bad;
                 const int per = max(1, seq_partitions(P, len, &bad));
                 const int local = int(idx - prefix[b]);
@@ -303,18 +304,21 @@ struct UnitCursor {
     }
 };
 
-// Fills prefix[0..B] with the running count of units per sequence (nhg * max(1, partitions)).
-// Called by `nthreads` threads (a multiple of 32, at most 1024) that then synchronize on barrier
-// `bar_id`; `scratch` holds nthreads ints of shared memory.
+// Fills prefix[0..B] with the running count of units per sequence (nhg * max(1, partitions)), and
+// lens_out[0..B) with the lengths when it is not null. Called by `nthreads` threads (a multiple of
+// 32, at most 1024) that then synchronize on barrier `bar_id`; `scratch` holds nthreads ints of
+// shared memory.
 __device__ __forceinline__ void build_unit_prefix(const DecodeParams& p, int* prefix, int* scratch, int tid,
-                                                  int nthreads, uint32_t bar_id) {
+                                                  int nthreads, uint32_t bar_id, int* lens_out = nullptr) {
     // Each thread counts a contiguous slice, then warp 0 scans the slice totals.
     const int per = (p.B + nthreads - 1) / nthreads;
     const int s0 = min(p.B, tid * per), s1 = min(p.B, s0 + per);
     int sum = 0;
     for (int b = s0; b < s1; ++b) {
         bool bad;
-        sum += p.nhg * max(1, seq_partitions(p, __ldg(p.seq_lens + b), &bad));
+        const int len = __ldg(p.seq_lens + b);
+        if (lens_out) lens_out[b] = len;
+        sum += p.nhg * max(1, seq_partitions(p, len, &bad));
         prefix[b + 1] = sum;  // slice-local inclusive sums for now
     }
     scratch[tid] = sum;
@@ -398,20 +402,36 @@ __device__ __forceinline__ void merge_slots_and_store(const DecodeParams& p, con
 // launch << 32) and counts itself again, so only the first use after a layout change pays for a
 // compare-and-swap. An arrival past the partition count (two launches sharing one workspace at the
 // same time, or an aborted launch) raises KVB_DEVERR_STATE; the flag reader then resets the counters.
-template <int D>
+//
+// The merge (src/kernels.metal:124-147): out = sum_i L_i 2^(m_i - M) o_i / sum_i L_i 2^(m_i - M)
+// over the stored normalized partials o_i with their (m_i, L_i). `nthreads` threads split the
+// (head, 4-dim slice) pairs; when there are fewer pairs than threads, SPLIT consecutive lanes share a
+// pair and take every SPLIT-th partition, so more loads are in flight at once. Each lane keeps an
+// online (M, S, A) over batches of BATCH partitions and the lanes of a pair combine with shuffles.
+//
+// Threads: `nthreads` consecutive threads (a multiple of 32) starting at tid 0, barrier `bar_id`.
+// Atomic add with release (this CTA's earlier stores, ordered before it by a barrier, are visible
+// to whoever observes the add) and acquire (later loads see what the other adders released).
+__device__ __forceinline__ unsigned long long atom_add_acq_rel(unsigned long long* ptr, unsigned long long v) {
+    unsigned long long old;
+    asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(ptr), "l"(v) : "memory");
+    return old;
+}
+
+template <int D, int BATCH = 8>
 __device__ __forceinline__ void finish_partition(const DecodeParams& p, const Unit& u, int tid, int nthreads,
-                                                 uint32_t bar_id, int* s_flag, float* scratch, int scratch_floats) {
+                                                 uint32_t bar_id, int* s_flag) {
     if (u.nparts <= 1) return;
-    __threadfence();
-    named_barrier(bar_id, nthreads);
+    named_barrier(bar_id, nthreads);  // every thread's partial stores come before the arrival below
     if (tid == 0) {
         unsigned long long* ctr = p.counters + (size_t)u.b * p.nhg + u.hg;
-        const unsigned long long old = atomicAdd(ctr, 1ull);
+        const unsigned long long old = atom_add_acq_rel(ctr, 1ull);
         const unsigned epoch = unsigned(old >> 32);
         unsigned arrived;
         if (epoch == p.launch || epoch == KVB_CTR_CLEAN) {
             arrived = unsigned(old) + 1u;
         } else {
+            __threadfence();
             unsigned long long seen = old + 1ull;
             for (;;) {
                 const unsigned long long cur = atomicCAS(ctr, seen, (unsigned long long)p.launch << 32);
@@ -419,7 +439,7 @@ __device__ __forceinline__ void finish_partition(const DecodeParams& p, const Un
                 if (cur == seen || e == p.launch || e == KVB_CTR_CLEAN) break;
                 seen = cur;
             }
-            arrived = unsigned(atomicAdd(ctr, 1ull)) + 1u;
+            arrived = unsigned(atom_add_acq_rel(ctr, 1ull)) + 1u;
         }
         const int last = arrived == unsigned(u.nparts);
         if (arrived > unsigned(u.nparts)) raise_error(p.error_flag, KVB_DEVERR_STATE);
@@ -428,68 +448,69 @@ __device__ __forceinline__ void finish_partition(const DecodeParams& p, const Un
     }
     named_barrier(bar_id, nthreads);
     if (!*s_flag) return;
-    __threadfence();
-    const int np = u.nparts, warps = nthreads >> 5, lane = tid & 31;
-    if (u.nh * (np + 1) <= scratch_floats) {
-        // Weights w_i = L_i * 2^(M_i - max M) per head, one warp per head (all partitions of a head
-        // load in parallel across lanes), then out[d] = sum_i w_i o_i[d] / sum_i w_i with independent
-        // 16-byte loads of the partials.
-        float* w = scratch;               // [nh][np]
-        float* wsum = scratch + u.nh * np;  // [nh]
-        for (int g = tid >> 5; g < u.nh; g += warps) {
-            const size_t base = ((size_t)u.b * p.H + u.h0 + g) * p.max_parts;
-            float M = NEG_BIG;
-            for (int i = lane; i < np; i += 32) M = fmaxf(M, __ldcg(&p.part_ml[base + i].x));
+
+    constexpr int D4 = D / 4;
+    const int np = u.nparts, nh = u.nh;
+    const int pairs = nh * D4;
+    int split = 1;
+    while (split < 32 && split * 2 * pairs <= nthreads) split *= 2;
+    const int s = tid % split;
+    for (int base = 0; base < pairs * split; base += nthreads) {  // the same trip count in every lane
+        const int idx = base + tid;
+        const bool active = idx < pairs * split;
+        const int pair = active ? idx / split : 0;
+        const int g = pair / D4, d4 = pair % D4, h = u.h0 + g;
+        const size_t row = ((size_t)u.b * p.H + h) * p.max_parts;
+        const float4* po = reinterpret_cast<const float4*>(p.part_o + row * D) + d4;
+        float M = NEG_BIG, S = 0.f;
+        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i0 = active ? s : np; i0 < np; i0 += BATCH * split) {
+            float2 ml[BATCH];
+            float4 ov[BATCH];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-            float L = 0.f;
-            for (int i = lane; i < np; i += 32) {
-                const float2 ml = __ldcg(&p.part_ml[base + i]);
-                const float wi = ml.y * exp2f(ml.x - M);
-                w[g * np + i] = wi;
-                L += wi;
+            for (int j = 0; j < BATCH; ++j) {
+                const int i = i0 + j * split;
+                if (i < np) {
+                    ml[j] = __ldcg(&p.part_ml[row + i]);
+                    ov[j] = __ldcg(po + (size_t)i * D4);
+                } else {
+                    ml[j] = make_float2(NEG_BIG, 0.f);
+                    ov[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
             }
+            float Mb = M;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-            if (lane == 0) wsum[g] = L;
-        }
-        named_barrier(bar_id, nthreads);
-        for (int idx = tid; idx < u.nh * (D / 4); idx += nthreads) {
-            const int g = idx / (D / 4), d4 = idx % (D / 4), h = u.h0 + g;
-            const float4* po = reinterpret_cast<const float4*>(p.part_o + ((size_t)u.b * p.H + h) * p.max_parts * D) + d4;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-            for (int i = 0; i < np; ++i) {
-                const float4 oi = __ldcg(po + (size_t)i * (D / 4));
-                const float wi = w[g * np + i];
-                acc.x = fmaf(wi, oi.x, acc.x);
-                acc.y = fmaf(wi, oi.y, acc.y);
-                acc.z = fmaf(wi, oi.z, acc.z);
-                acc.w = fmaf(wi, oi.w, acc.w);
+            for (int j = 0; j < BATCH; ++j) Mb = fmaxf(Mb, ml[j].x);
+            const float sc = exp2f(M - Mb);
+            S *= sc;
+            A.x *= sc, A.y *= sc, A.z *= sc, A.w *= sc;
+#pragma unroll
+            for (int j = 0; j < BATCH; ++j) {
+                const float w = ml[j].y * exp2f(ml[j].x - Mb);
+                S += w;
+                A.x = fmaf(w, ov[j].x, A.x);
+                A.y = fmaf(w, ov[j].y, A.y);
+                A.z = fmaf(w, ov[j].z, A.z);
+                A.w = fmaf(w, ov[j].w, A.w);
             }
-            const float inv = 1.f / wsum[g];
-            reinterpret_cast<float4*>(p.out + ((size_t)u.b * p.H + h) * D)[d4] =
-                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+            M = Mb;
         }
-        named_barrier(bar_id, nthreads);  // the scratch is free again
-        return;
-    }
-    // Many partitions: one pass of online merging per output element.
-    for (int idx = tid; idx < u.nh * D; idx += nthreads) {
-        const int g = idx / D, d = idx % D, h = u.h0 + g;
-        const size_t base = ((size_t)u.b * p.H + h) * p.max_parts;
-        float M = NEG_BIG, L = 0.f, o = 0.f;
-#pragma unroll 8
-        for (int i = 0; i < np; ++i) {
-            const float2 ml = __ldcg(&p.part_ml[base + i]);
-            const float oi = __ldcg(&p.part_o[(base + i) * D + d]);
-            const float Mn = fmaxf(M, ml.x);
-            const float a = exp2f(M - Mn), c = ml.y * exp2f(ml.x - Mn);
-            L = L * a + c;
-            o = o * a + c * oi;
+        // combine the `split` lanes of this pair (consecutive lanes)
+        for (int off = 1; off < split; off <<= 1) {
+            const float M2 = __shfl_xor_sync(0xffffffffu, M, off);
+            const float S2 = __shfl_xor_sync(0xffffffffu, S, off);
+            const float ax = __shfl_xor_sync(0xffffffffu, A.x, off), ay = __shfl_xor_sync(0xffffffffu, A.y, off);
+            const float az = __shfl_xor_sync(0xffffffffu, A.z, off), aw = __shfl_xor_sync(0xffffffffu, A.w, off);
+            const float Mn = fmaxf(M, M2), c1 = exp2f(M - Mn), c2 = exp2f(M2 - Mn);
+            S = S * c1 + S2 * c2;
+            A = make_float4(A.x * c1 + ax * c2, A.y * c1 + ay * c2, A.z * c1 + az * c2, A.w * c1 + aw * c2);
             M = Mn;
         }
-        p.out[((size_t)u.b * p.H + h) * D + d] = o / L;
+        if (active && s == 0) {
+            const float inv = 1.f / S;
+            reinterpret_cast<float4*>(p.out + ((size_t)u.b * p.H + h) * D)[d4] =
+                make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv);
+        }
     }
 }
 
