@@ -63,6 +63,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every step from the host")
     ap.add_argument("--ramp-s", type=float, default=1.0, help="untimed load before warm-up (clock ramp)")
+    ap.add_argument("--op", choices=["decode", "quantize", "scatter"], default="decode",
+                    help="decode step (default) or the page write path in front of it (one GPU)")
     return ap.parse_args()
 
 
@@ -366,11 +368,72 @@ def peak_hbm():
 
 # ---------------------------------------------------------------------------------------------------
 
+def run_write_path(args, w):
+    """`--op quantize|scatter`: the page write path (kvb_quantize_paged_i8 / kvb_scatter_paged) on the
+    workload's contiguous cache, one GPU; GB/s of live bytes read and written per launch."""
+    import torch
+
+    import kv_cache_bench_b200 as kvb
+    quantize = args.op == "quantize"
+    kv = "i8" if quantize else (w["kv"] if w["kv"] in ("f32", "f16") else "f16")
+    device = torch.device("cuda", 0)
+    lens = list(w["lens"])
+    B, Hkv, D, page = len(lens), w["Hkv"], w["D"], w["page"]
+    max_len = max(lens)
+    src_dt = torch.float32 if kv in ("i8", "f32") else torch.float16
+    if B * Hkv * max_len * D * (4 if src_dt == torch.float32 else 2) > (40 << 30):
+        raise SystemExit("the contiguous cache of this config does not fit the write-path bench")
+    rng = np.random.default_rng(w["seed"])
+    table, num_blocks = build_layout(lens, page, w.get("pool_slack", 1.0), w.get("pool_blocks"), rng)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(w["seed"])
+    contig = torch.empty((B, Hkv, max_len, D), dtype=src_dt, device=device).uniform_(-1, 1, generator=gen)
+    pool = torch.zeros((num_blocks, Hkv, page, D), dtype=torch.int8 if quantize else src_dt, device=device)
+    scales = torch.zeros((num_blocks, Hkv), device=device)
+    tb = torch.from_numpy(table).to(device)
+    ln = torch.tensor(lens, dtype=torch.int32, device=device)
+    a = kvb.page_write_args(B, Hkv, D, kvb.KvType[kv], page, table.shape[1], max_len, contig=contig.data_ptr(),
+                            block_table=tb.data_ptr(), seq_lens=ln.data_ptr(), pool=pool.data_ptr(),
+                            num_blocks=num_blocks, scales=scales.data_ptr())
+    fn = kvb.quantize_paged_i8 if quantize else kvb.scatter_paged
+    stream = torch.cuda.Stream(device)
+    for _ in range(max(args.warmup, 3)):
+        fn(a, stream.cuda_stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream.synchronize()
+    with torch.cuda.stream(stream):
+        e0.record()
+    for _ in range(args.steps):
+        fn(a, stream.cuda_stream)
+    with torch.cuda.stream(stream):
+        e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    live = float(sum(lens)) * Hkv * D
+    in_b = live * contig.element_size()
+    out_b = live * pool.element_size() + (float(sum((l + page - 1) // page for l in lens)) * Hkv * 4 if quantize else 0)
+    gbs = (in_b + out_b) / (ms * 1e-3) / 1e9
+    peak, peak_kind = peak_hbm()
+    print(json.dumps({
+        "metric": f"page write path ({'int8 quantize' if quantize else 'scatter'}) GB/s", "op": args.op,
+        "value": round(gbs, 2), "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 6), "higher_is_better": True, "dtype": kv,
+        "data": "synthetic: U(-1,1) contiguous cache generated on the device",
+        "config": dict(config_obj(w, None, 1), source_bytes=in_b, pool_bytes=out_b,
+                       l2=f"contiguous input {in_b / 1e6:.0f} MB vs L2 {torch.cuda.get_device_properties(device).L2_cache_size / 1e6:.0f} MB"),
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "peak_kind": peak_kind},
+        "gpu_launches": args.steps}), flush=True)
+
+
 def main():
     args = parse_args()
     w = workload(args.config, args.dtype)
     if args.impl == "reference":
         run_reference_arm(args, w)
+        return
+    if args.op != "decode":
+        run_write_path(args, w)
         return
     import torch
     import torch.distributed as dist

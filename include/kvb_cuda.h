@@ -170,6 +170,33 @@ int kvb_paged_workspace_bytes(const kvb_paged_args* args, size_t* bytes);
  * the buffers. Calls that share one workspace must not overlap on the device. */
 int kvb_paged_decode_async(const kvb_paged_args* args, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- page write path (the step before decode) --------------------------------------------- */
+
+/* A contiguous cache written into the paged pool through the block table. Device pointers,
+ * stream-ordered, nothing read on the host. */
+typedef struct {
+    kvb_shape shape;          /* batch, num_kv_heads, head_dim (a multiple of 8); num_heads unused */
+    int kv_type;              /* pool type: KVB_F32 / KVB_F16 (scatter) or KVB_I8 (quantize) */
+    int page_size, max_blocks, max_len;
+    const void* contig;       /* [batch][num_kv_heads][max_len][head_dim]; fp32 for KVB_I8, else the pool type */
+    const int* block_table;   /* [batch][max_blocks] */
+    const int* seq_lens;      /* [batch] */
+    void* pool;               /* [num_blocks][num_kv_heads][page_size][head_dim] */
+    float* scales;            /* KVB_I8: [num_blocks][num_kv_heads] */
+    long long num_blocks;
+    unsigned int* error_word; /* optional device word: bit 1 bad length, bit 2 bad block id (pages skipped) */
+} kvb_page_write_args;
+
+/* src/reference.cpp:32-51 quantize_to_paged_i8 on the device: per (sequence, logical page, KV
+ * head), scale = max|x| / 127 over the page's live tokens (fp32), q = clamp(nearbyint(x / scale),
+ * -127, 127), 0 for a zero page; bit-identical to the reference for finite inputs. Slots past the
+ * last token are not written. contig and pool 16-byte aligned. */
+int kvb_quantize_paged_i8(const kvb_page_write_args* args, void* stream);
+
+/* src/reference.hpp:60-68 scatter_to_paged on the device: the live tokens of an fp32 or fp16
+ * contiguous cache copied into the pool of the same type. */
+int kvb_scatter_paged(const kvb_page_write_args* args, void* stream);
+
 /* Bytes of the library-owned workspace of kvb_paged_decode_static (16 MiB per device). */
 #define KVB_STATIC_WORKSPACE_BYTES (16u << 20)
 

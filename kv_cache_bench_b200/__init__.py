@@ -73,6 +73,13 @@ class _CPagedArgs(ctypes.Structure):
                 ("num_blocks", ctypes.c_int64), ("kernel", ctypes.c_int)]
 
 
+class _CPageWriteArgs(ctypes.Structure):
+    _fields_ = [("shape", _CShape), ("kv_type", ctypes.c_int), ("page_size", ctypes.c_int),
+                ("max_blocks", ctypes.c_int), ("max_len", ctypes.c_int), ("contig", ctypes.c_void_p),
+                ("block_table", ctypes.c_void_p), ("seq_lens", ctypes.c_void_p), ("pool", ctypes.c_void_p),
+                ("scales", ctypes.c_void_p), ("num_blocks", ctypes.c_int64), ("error_word", ctypes.c_void_p)]
+
+
 class _CNaiveArgs(ctypes.Structure):
     _fields_ = [("shape", _CShape), ("kv_type", ctypes.c_int), ("max_len", ctypes.c_int),
                 ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
@@ -107,6 +114,8 @@ _c_ws_bytes = _sig("kvb_paged_workspace_bytes", ctypes.c_int, ctypes.POINTER(_CP
                    ctypes.POINTER(ctypes.c_size_t))
 _c_decode_async = _sig("kvb_paged_decode_async", ctypes.c_int, ctypes.POINTER(_CPagedArgs), ctypes.c_void_p,
                        ctypes.c_size_t, ctypes.c_void_p)
+_c_quantize = _sig("kvb_quantize_paged_i8", ctypes.c_int, ctypes.POINTER(_CPageWriteArgs), ctypes.c_void_p)
+_c_scatter = _sig("kvb_scatter_paged", ctypes.c_int, ctypes.POINTER(_CPageWriteArgs), ctypes.c_void_p)
 _c_decode_static = _sig("kvb_paged_decode_static", ctypes.c_int, ctypes.POINTER(_CPagedArgs), ctypes.c_void_p)
 _c_error_flag = _sig("kvb_paged_error_flag", ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                      ctypes.POINTER(ctypes.c_int))
@@ -353,6 +362,27 @@ def paged_decode_static(c: _CPagedArgs, stream: int = 0) -> None:
 
 
 STATIC_WORKSPACE_BYTES = 16 << 20
+
+
+# ---- page write path (src/reference.cpp:32-51, src/reference.hpp:60-68) ----------------------------
+
+def page_write_args(batch: int, num_kv_heads: int, head_dim: int, kv_type: KvType, page_size: int, max_blocks: int,
+                    max_len: int, *, contig: int, block_table: int, seq_lens: int, pool: int, num_blocks: int,
+                    scales: int = 0, error_word: int = 0) -> _CPageWriteArgs:
+    """kvb_page_write_args over raw device pointers (ints)."""
+    return _CPageWriteArgs(_CShape(batch, num_kv_heads, num_kv_heads, head_dim), int(kv_type), page_size, max_blocks,
+                           max_len, contig or None, block_table or None, seq_lens or None, pool or None,
+                           scales or None, int(num_blocks), error_word or None)
+
+
+def quantize_paged_i8(a: _CPageWriteArgs, stream: int = 0) -> None:
+    """kvb_quantize_paged_i8: the reference's per-(page, KV head) absmax/127 quantizer on the device."""
+    _check(_c_quantize(ctypes.byref(a), stream or None), "quantize_paged_i8")
+
+
+def scatter_paged(a: _CPageWriteArgs, stream: int = 0) -> None:
+    """kvb_scatter_paged: the reference's scatter_to_paged on the device (fp32 / fp16)."""
+    _check(_c_scatter(ctypes.byref(a), stream or None), "scatter_paged")
 
 
 def paged_error_flag(workspace: int, stream: int = 0) -> int:

@@ -473,6 +473,47 @@ int kvb_paged_decode_async(const kvb_paged_args* a, void* workspace, size_t work
     return launch_paged(a, workspace, static_cast<cudaStream_t>(stream));
 }
 
+// ---- page write path -------------------------------------------------------------------------------
+
+int page_write(const kvb_page_write_args* a, bool quantize, void* stream) {
+    if (!a) return fail(KVB_ERR_INVALID, "null arguments");
+    const kvb_shape& s = a->shape;
+    if (quantize ? a->kv_type != KVB_I8 : (a->kv_type != KVB_F32 && a->kv_type != KVB_F16))
+        return fail(KVB_ERR_INVALID, quantize ? "quantize writes an int8 pool" : "scatter takes f32 or f16");
+    if (s.batch < 0 || s.batch > 65535) return fail(KVB_ERR_INVALID, "batch must be in [0, 65535]");
+    if (s.num_kv_heads < 1 || s.num_kv_heads > 65535) return fail(KVB_ERR_INVALID, "num_kv_heads must be in [1, 65535]");
+    if (s.head_dim < 8 || s.head_dim % 8) return fail(KVB_ERR_INVALID, "head_dim must be a positive multiple of 8");
+    if (a->page_size <= 0) return fail(KVB_ERR_INVALID, "page_size must be > 0");
+    if (a->max_blocks < 0 || a->max_len < 0) return fail(KVB_ERR_INVALID, "max_blocks and max_len must be >= 0");
+    if (a->num_blocks <= 0) return fail(KVB_ERR_INVALID, "num_blocks must be > 0");
+    if (s.batch == 0 || a->max_blocks == 0) return KVB_OK;
+    if (!a->contig || !a->block_table || !a->seq_lens || !a->pool || (quantize && !a->scales))
+        return fail(KVB_ERR_INVALID, "null device pointer");
+    if (!aligned16(a->contig) || !aligned16(a->pool)) return fail(KVB_ERR_INVALID, "contig and pool must be 16-byte aligned");
+    PageWriteParams p;
+    p.src = a->contig;
+    p.dst = a->pool;
+    p.scales = a->scales;
+    p.block_table = a->block_table;
+    p.seq_lens = a->seq_lens;
+    p.error_flag = a->error_word;
+    p.B = s.batch;
+    p.Hkv = s.num_kv_heads;
+    p.D = s.head_dim;
+    p.page = a->page_size;
+    p.max_blocks = a->max_blocks;
+    p.max_len = a->max_len;
+    p.elem = (int)elem_size(a->kv_type);
+    p.num_blocks = a->num_blocks;
+    const cudaError_t e = kvb_launch_page_write(p, quantize, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(KVB_ERR_DEVICE, std::string("page write launch: ") + cudaGetErrorString(e));
+    return KVB_OK;
+}
+
+int kvb_quantize_paged_i8(const kvb_page_write_args* args, void* stream) { return page_write(args, true, stream); }
+
+int kvb_scatter_paged(const kvb_page_write_args* args, void* stream) { return page_write(args, false, stream); }
+
 // ---- library-owned workspace ---------------------------------------------------------------------
 
 // The workspace of kvb_paged_decode_static: device memory of the library's own module (zero at module

@@ -55,6 +55,19 @@ struct DecodeParams {
     unsigned launch;   // launch id (high bit set): tells this launch's counter values from stale ones
 };
 
+// The page write path (kvb_pages.cu): a contiguous cache into the paged pool.
+struct PageWriteParams {
+    const void* src;         // [B][Hkv][max_len][D]: fp32 (quantize) or the pool's type (scatter)
+    void* dst;               // pool [num_blocks][Hkv][page][D]
+    float* scales;           // quantize: [num_blocks][Hkv]
+    const int* block_table;  // [B][max_blocks]
+    const int* seq_lens;     // [B]
+    unsigned* error_flag;    // optional: KVB_DEVERR_LENGTH / KVB_DEVERR_BLOCK bits
+    int B, Hkv, D, page, max_blocks, max_len, elem;
+    long long num_blocks;
+};
+cudaError_t kvb_launch_page_write(const PageWriteParams& p, bool quantize, cudaStream_t stream);
+
 // Workspace layout (offsets in bytes), shared by the size query and the launcher.
 struct WorkspaceLayout {
     size_t flag_off, counters_off, ml_off, o_off, total;

@@ -102,6 +102,22 @@ def quantize_i8(contig, table, lens, *, num_blocks, page):
     return pool, scales
 
 
+def scatter_paged(contig, table, lens, *, num_blocks, page, fill=0):
+    """The live tokens of a contiguous cache [B][Hkv][max_len][D] copied into a pool
+    [num_blocks][Hkv][page][D] through the block table (src/reference.hpp:60-68 scatter_to_paged);
+    slots holding no live token keep `fill`."""
+    contig = np.ascontiguousarray(contig)
+    B, Hkv, max_len, D = contig.shape
+    table = _c(table, np.int32).reshape(B, -1)
+    pool = np.full((num_blocks, Hkv, page, D), fill, contig.dtype)
+    for b in range(B):
+        L = int(lens[b])
+        for i in range((L + page - 1) // page):
+            t0, t1 = i * page, min(L, (i + 1) * page)
+            pool[table[b, i], :, : t1 - t0] = contig[b, :, t0:t1]
+    return pool
+
+
 def dequantize_i8(pool, scales, table, lens, *, max_len):
     pool = _c(pool, np.int8)
     num_blocks, Hkv, page, D = pool.shape

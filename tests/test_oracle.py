@@ -40,6 +40,24 @@ def test_oracle_contiguous_matches_reference_bitwise(golden):
         assert np.array_equal(out.view(np.uint32), c["ref"].view(np.uint32)), c["name"]
 
 
+def test_oracle_scatter_matches_reference(golden):
+    """The fp16 pools the reference's scatter_to_paged wrote (src/reference.hpp:60-68) from its
+    contiguous cache (the fp16 rounding of k32 / v32) equal oracle.scatter_paged on every live slot."""
+    n = 0
+    for c in golden:
+        if c.get("kv_type") != oracle.F16 or "k32" not in c or "page_size" not in c:
+            continue
+        for src, pool_key in (("k32", "k"), ("v32", "v")):
+            pool = oracle.scatter_paged(c[src].astype(np.float16), c["block_table"], c["seq_lens"],
+                                        num_blocks=c["num_blocks"], page=c["page_size"])
+            for b, L in enumerate(c["seq_lens"]):
+                for t in range(L):
+                    blk, r = c["block_table"][b, t // c["page_size"]], t % c["page_size"]
+                    assert np.array_equal(pool[blk, :, r].view(np.uint16), c[pool_key][blk, :, r].view(np.uint16))
+        n += 1
+    assert n >= 4
+
+
 def test_oracle_quantizer_matches_reference(golden):
     n = 0
     for c in golden:
