@@ -33,22 +33,46 @@ def _load() -> ctypes.CDLL:
     return ctypes.CDLL(path)
 
 
-_lib = _load()
 _P = ctypes.c_void_p
-_lib.kvb_oracle_paged_attention.argtypes = [ctypes.c_int] * 7 + [_P] * 8 + [ctypes.c_int]
-_lib.kvb_oracle_paged_attention.restype = None
-_lib.kvb_oracle_contig_attention.argtypes = [ctypes.c_int] * 6 + [_P] * 5 + [ctypes.c_int]
-_lib.kvb_oracle_contig_attention.restype = None
-_lib.kvb_oracle_quantize_i8.argtypes = [ctypes.c_int] * 6 + [_P] * 5
-_lib.kvb_oracle_quantize_i8.restype = None
-_lib.kvb_oracle_dequantize_i8.argtypes = [ctypes.c_int] * 6 + [_P] * 5
-_lib.kvb_oracle_dequantize_i8.restype = None
-_lib.kvb_oracle_fp16_bound.argtypes = [ctypes.c_int] * 5 + [_P] * 4
-_lib.kvb_oracle_fp16_bound.restype = ctypes.c_double
-_lib.kvb_oracle_i8_bound.argtypes = [ctypes.c_int] * 6 + [_P] * 5
-_lib.kvb_oracle_i8_bound.restype = ctypes.c_double
-_lib.kvb_oracle_max_abs_diff.argtypes = [_P, _P, ctypes.c_size_t]
-_lib.kvb_oracle_max_abs_diff.restype = ctypes.c_double
+
+
+def _declare(lib: ctypes.CDLL) -> ctypes.CDLL:
+    lib.kvb_oracle_paged_attention.argtypes = [ctypes.c_int] * 7 + [_P] * 8 + [ctypes.c_int]
+    lib.kvb_oracle_paged_attention.restype = None
+    lib.kvb_oracle_contig_attention.argtypes = [ctypes.c_int] * 6 + [_P] * 5 + [ctypes.c_int]
+    lib.kvb_oracle_contig_attention.restype = None
+    lib.kvb_oracle_quantize_i8.argtypes = [ctypes.c_int] * 6 + [_P] * 5
+    lib.kvb_oracle_quantize_i8.restype = None
+    lib.kvb_oracle_dequantize_i8.argtypes = [ctypes.c_int] * 6 + [_P] * 5
+    lib.kvb_oracle_dequantize_i8.restype = None
+    lib.kvb_oracle_fp16_bound.argtypes = [ctypes.c_int] * 5 + [_P] * 4
+    lib.kvb_oracle_fp16_bound.restype = ctypes.c_double
+    lib.kvb_oracle_i8_bound.argtypes = [ctypes.c_int] * 6 + [_P] * 5
+    lib.kvb_oracle_i8_bound.restype = ctypes.c_double
+    lib.kvb_oracle_max_abs_diff.argtypes = [_P, _P, ctypes.c_size_t]
+    lib.kvb_oracle_max_abs_diff.restype = ctypes.c_double
+    return lib
+
+
+_lib = _declare(_load())
+
+
+class use_library:
+    """Context manager: the functions of this module call the oracle built at `path` instead (the
+    mutation tests load deliberately broken builds of kvb_oracle.c this way)."""
+
+    def __init__(self, path: str):
+        self.lib = _declare(ctypes.CDLL(path))
+
+    def __enter__(self):
+        global _lib
+        self.saved, _lib = _lib, self.lib
+        return self
+
+    def __exit__(self, *exc):
+        global _lib
+        _lib = self.saved
+        return False
 
 
 def _p(a: Optional[np.ndarray]):
