@@ -623,41 +623,62 @@ def main():
 
 
 def measure_e2e(torch, dist, s, dec, part, kernel, stream, args, world, barrier, job_bytes, w, gather):
-    """The same metric through the public API with host buffers: per step, H2D of q, lengths and block
-    table from pinned memory, the decode call, the output all-gather when sharded, D2H of the
-    (global) output."""
-    pin = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t.cpu())  # noqa: E731
-    hq, hl, ht = pin(s.q), pin(s.seq_lens), pin(s.table)
+    """The same metric through the public C ABI with host buffers: per step, one host->device copy
+    of the step's inputs (q, sequence lengths, block table, packed in one pinned staging buffer),
+    kvb_paged_decode_async reading them where they landed, the output all-gather when sharded, and
+    the device->host copy of the (global) output. The KV pool is device-resident state (written when a
+    page is written), rotated over the same copies as the device timing."""
+    import kv_cache_bench_b200 as kvb
+
+    def align(n):
+        return (n + 255) // 256 * 256
+
+    q_b, l_b, t_b = s.q.numel() * 4, s.seq_lens.numel() * 4, s.table.numel() * 4
+    off_l = align(q_b)
+    off_t = off_l + align(l_b)
+    total = off_t + t_b
+    host = torch.empty(total, dtype=torch.uint8, pin_memory=True)
+    host[:q_b].copy_(s.q.cpu().view(-1).view(torch.uint8))
+    host[off_l:off_l + l_b].copy_(s.seq_lens.cpu().view(-1).view(torch.uint8))
+    host[off_t:off_t + t_b].copy_(s.table.cpu().view(-1).view(torch.uint8))
+    stage = torch.empty(total, dtype=torch.uint8, device=s.q.device)
+    q = stage[:q_b].view(torch.float32).view(s.q.shape)
+    lens = stage[off_l:off_l + l_b].view(torch.int32)
+    table = stage[off_t:off_t + t_b].view(torch.int32).view(s.table.shape)
     result = gather()
     torch.cuda.synchronize()
     hout = torch.empty(result.shape, dtype=result.dtype, pin_memory=True)
-    k, v, ks, vs = s.pools[0]
-    h2d = hq.numel() * 4 + hl.numel() * 4 + ht.numel() * 4
-    d2h = hout.numel() * 4
+    cargs = [dec.args(q, k, v, table, lens, s.max_len, out=s.out, k_scale=ks, v_scale=vs, part_tokens=part,
+                      kernel=kernel) for (k, v, ks, vs) in s.pools]
+    need = max(kvb.paged_workspace_bytes(c) for c in cargs)
+    if need > dec.workspace.numel():
+        dec.workspace = torch.zeros(need, dtype=torch.uint8, device=s.q.device)
+    ws, wsn = dec.workspace.data_ptr(), dec.workspace.numel()
+    h2d = total
+    d2h = hout.numel() * hout.element_size()
     n = min(max(args.steps, 1), 2000)
+    raw = stream.cuda_stream
 
-    def one(pool_upload=None):
+    def one(i, pool_upload=None):
         with torch.cuda.stream(stream):
-            s.q.copy_(hq, non_blocking=True)
-            s.seq_lens.copy_(hl, non_blocking=True)
-            s.table.copy_(ht, non_blocking=True)
+            stage.copy_(host, non_blocking=True)
             if pool_upload is not None:
+                k, v, _, _ = s.pools[i % len(s.pools)]
                 k.copy_(pool_upload[0], non_blocking=True)
                 v.copy_(pool_upload[1], non_blocking=True)
-            dec(s.q, k, v, s.table, s.seq_lens, s.max_len, k_scale=ks, v_scale=vs, part_tokens=part, kernel=kernel,
-                out=s.out, stream=stream)
+            kvb.paged_decode_async(cargs[i % len(cargs)], ws, wsn, raw)
             hout.copy_(gather(), non_blocking=True)
 
     def timed(count, pool_upload=None):
-        for _ in range(3):
-            one(pool_upload)
+        for i in range(3):
+            one(i, pool_upload)
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             e0.record()
-        for _ in range(count):
-            one(pool_upload)
+        for i in range(count):
+            one(i, pool_upload)
         with torch.cuda.stream(stream):
             e1.record()
         barrier()
@@ -669,10 +690,12 @@ def measure_e2e(torch, dist, s, dec, part, kernel, stream, args, world, barrier,
     ms = timed(n)
     e2e = {"value": round(job_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 6),
            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": n,
-           "api": "PagedDecoder -> kvb_paged_decode_async (C ABI), host launch per step"}
+           "api": "kvb_paged_decode_async (C ABI), host launch per step, one packed input copy per step"}
     e2e_pool = None
     if w["shard"] == "replica" or world == 1:
-        hk, hv = pin(k), pin(v)
+        k0, v0, _, _ = s.pools[0]
+        pin = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t.cpu())  # noqa: E731
+        hk, hv = pin(k0), pin(v0)
         m = min(n, 20)
         ms2 = timed(m, (hk, hv))
         e2e_pool = {"value": round(job_bytes / (ms2 * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms2, 6),
