@@ -176,7 +176,7 @@ template <int KVT>
 struct UCfg {
     static constexpr int NSUB = KVT == 1 ? 2 : 1;             // 128-byte column slices of a row
     static constexpr int STAGE = 2 * NSUB * TILE;              // K tiles, then V tiles
-    static constexpr int STAGES = KVT == 1 ? 3 : 6;
+    static constexpr int STAGES = KVT == 1 ? 3 : 5;
     static constexpr int NMAX = KVT == 1 ? 16 : 32;            // MMA N (rows of Qhat / Phat)
     static constexpr int QBUF = NMAX * 128 * NSUB;             // one Qhat^T buffer ([N][128 B] per slice)
     static constexpr int PBUF = NMAX * 128 * NSUB;             // one Phat^T buffer
@@ -186,8 +186,8 @@ struct UCfg {
     static constexpr size_t BAD_OFF = P_OFF + 2 * PBUF;        // [STAGES] a block id of the chunk was refused
     static constexpr size_t BAR_OFF = kvb_align_up(BAD_OFF + STAGES * sizeof(int), 64);
     // full per (stage, chunk parity); empty per stage; q_full, q_free, s_full, s_free, p_full,
-    // o_full, pt_free x2
-    static constexpr int NBARS = 3 * STAGES + 2 * 7;
+    // o_full, pt_free x2; x_full, x_free
+    static constexpr int NBARS = 3 * STAGES + 2 * 7 + 2;
     static constexpr size_t RED_OFF = kvb_align_up(BAR_OFF + NBARS * sizeof(uint64_t), 16);
     static constexpr size_t WIN_OFF = RED_OFF + 2 * UM_GRED * sizeof(float);
     // page table: block ids [UM_PT]; int8: scales [2 buffers][UM_PT] for K and for V
@@ -196,8 +196,10 @@ struct UCfg {
     static constexpr size_t LENS_OFF = PREFIX_OFF + sizeof(int) * (KVB_PREFIX_MAX + 1);
     static constexpr size_t SCRATCH_OFF = kvb_align_up(LENS_OFF + sizeof(int) * KVB_PREFIX_MAX, 16);
     static constexpr size_t SCRATCH_FLOATS = 512;              // prefix scan
-    static constexpr size_t MISC_OFF = kvb_align_up(SCRATCH_OFF + SCRATCH_FLOATS * sizeof(float), 64);
-    static constexpr size_t SMEM = MISC_OFF + 64 + 1024;
+    static constexpr size_t XBUF_OFF = SCRATCH_OFF + SCRATCH_FLOATS * sizeof(float);
+    static constexpr size_t XBUF_FLOATS = 8 * 128 + 2 * 8 + 4;  // group 1's O rows, max, sums, bad flag
+    static constexpr size_t MISC_OFF = kvb_align_up(XBUF_OFF + XBUF_FLOATS * sizeof(float), 64);
+    static constexpr size_t SMEM = MISC_OFF + 256 + 1024;
 };
 
 static_assert(UCfg<1>::SMEM <= 227 * 1024 && UCfg<2>::SMEM <= 227 * 1024, "shared memory budget");
@@ -206,7 +208,6 @@ static_assert(UCfg<1>::MISC_OFF % 64 == 0 && UCfg<2>::MISC_OFF % 64 == 0, "align
 static_assert(UCfg<1>::Q_OFF % 1024 == 0 && UCfg<1>::P_OFF % 1024 == 0 && UCfg<2>::P_OFF % 1024 == 0,
               "swizzled operands need 1024-byte alignment");
 static_assert(UCfg<2>::SCRATCH_FLOATS >= UM_THREADS, "prefix scan scratch");
-static_assert(UCfg<1>::PBUF >= 8 * 128 * 4 && UCfg<2>::PBUF >= 8 * 128 * 4, "group 1's O rows fit its Phat buffer");
 
 template <int KVT, int QGP>  // QGP: query heads per group, padded to 1, 2, 4 or 8
 __global__ void __launch_bounds__(UM_THREADS, 1)
@@ -236,6 +237,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     uint64_t* p_full = q_full + 8;         // [2] Phat^T written, previous O^T folded (softmax -> MMA)
     uint64_t* o_full = q_full + 10;        // [2] O^T ready (MMA -> softmax)
     uint64_t* pt_free = q_full + 12;       // [2] int8 scale buffer read (softmax -> producer)
+    uint64_t* x_full = q_full + 14;        // group 1's unit state handed over (group 1 -> group 0)
+    uint64_t* x_free = q_full + 15;        // ... and read (group 0 -> group 1)
     float* red = reinterpret_cast<float*>(smem + C::RED_OFF);
     int* pt_blk = reinterpret_cast<int*>(smem + C::WIN_OFF);
     float* pt_ks = reinterpret_cast<float*>(pt_blk + UM_PT);  // int8 only: [2][UM_PT]
@@ -246,6 +249,9 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::MISC_OFF);
     int* s_flag = reinterpret_cast<int*>(smem + C::MISC_OFF + 8);
     uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF + 16);
+    volatile int* s_qprep = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 24);  // units with Qhat ready
+    float* s_qscale = reinterpret_cast<float*>(smem + C::MISC_OFF + 64);  // [unit % 4][8 heads]
+    float* xbuf = reinterpret_cast<float*>(smem + C::XBUF_OFF);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // The unit enumeration starts with the sequence lengths and the block table: have them on the
@@ -277,7 +283,10 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             mbar_init(&o_full[i], 1);
             mbar_init(&pt_free[i], 2 * UM_SOFT / 32);
         }
+        mbar_init(x_full, UM_SOFT / 32);
+        mbar_init(x_free, UM_SOFT / 32);
         *s_abort = 0;
+        *s_qprep = 0;
         fence_mbarrier_init();
     }
     if (warp == UM_TMEM_WARP) {
@@ -446,12 +455,17 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     const int k_base = k_end;
                     k_end = k_base + (u.t1 + UM_CHUNK - 1) / UM_CHUNK - u.t0 / UM_CHUNK;
                     qk = k_base + ((k_base & 1) != par ? 1 : 0);
-                    if (qk >= k_end) {
-                        tc_commit(&q_free[qb]);  // no chunk of this parity: release the Qhat buffer now
-                        continue;
-                    }
                     have_unit = true;
                     need_q = true;
+                }
+                // A unit with no chunk of this parity: release its Qhat buffer once it was written
+                // (not earlier, or this warp could count a later unit's release into an earlier phase).
+                if (have_unit && qk >= k_end) {
+                    if (mbar_test(&q_full[qb], (unit_no >> 1) & 1)) {
+                        tc_commit(&q_free[qb]);
+                        have_unit = false;
+                        progress = true;
+                    }
                 }
                 // ---- O^T = V^T Phat^T for the oldest pending chunk
                 if (pv_n > 0) {
@@ -477,7 +491,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     }
                 }
                 // ---- S^T = K Qhat^T for the next own chunk
-                if (have_unit && pv_n < 2) {
+                if (have_unit && qk < k_end && pv_n < 2) {
                     const int st = qk % STAGES;
                     const uint32_t use = uint32_t(qk >> 1);
                     const bool ready = (!need_q || mbar_test(&q_full[qb], (unit_no >> 1) & 1)) &&
@@ -529,7 +543,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         reg_alloc<UM_REGS_SOFT>();
         // Two warpgroups take alternate chunks: group gi handles the chunks whose running index k has
         // k & 1 == gi, with its own tensor-memory S/O buffers and Phat buffer, and its own running
-        // (max, sum, O). The groups merge once per unit.
+        // (max, sum, O). Group 1 hands its state to group 0 once per unit.
         const int gi = warp >> 2;
         const int gt = tid - gi * UM_SOFT;  // 0..127 within the group
         const int sw = gt >> 5;                  // warp within the group
@@ -537,77 +551,96 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         // this warp's tensor-memory lane quarter is fixed by warp % 4
         const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;
         const int my_lane = (warp & 3) * 32 + lane;  // token in S^T, head dim in O^T
-        // [0,32) q absmax; [32,112) chunk max x2 ([value][warp]: 8 heads, V scale); [112,144) sums;
-        // group 1: [144,161) state handed to group 0 at the unit's end
+        // [0,32) q absmax (group 0); [32,112) chunk max x2 ([value][warp]: 8 heads, V scale);
+        // [112,144) sums
         float* gred = red + gi * UM_GRED;
         UnitCursor cur{&p, prefix, (long long)blockIdx.x, total, prefix ? s_lens : nullptr};
         Unit u;
         int stage = 0;
         int k = 0;  // running chunk index
         int unit_no = 0;
+
+        // Group 1 writes Qhat^T and the per-head score factors of non-empty unit number `no` into
+        // buffer no & 1, one unit ahead of the one both groups process, so the MMA warps can start a
+        // unit while group 0 finishes the previous one: row (head g, part r) = fp16 half r of q, or
+        // int8 limb r.
+        UnitCursor ahead = cur;
+        Unit un;
+        auto next_nonempty = [&]() {
+            while (ahead.advance(un))
+                if (un.nparts != 0) return true;
+            return false;
+        };
+        auto prep_q = [&](const Unit& v, int no) {
+            const int b = no & 1;
+            if (no >= 2 && !*s_abort && !mbar_wait_bounded(&q_free[b], ((no - 2) >> 1) & 1, s_abort)) give_up();
+            const int d = my_lane;  // one head-dim element per thread
+            float x[QGP], amax[QGP];
+#pragma unroll
+            for (int g = 0; g < QGP; ++g) {
+                x[g] = g < v.nh ? __ldg(p.q + ((size_t)v.b * p.H + v.h0 + g) * UM_D + d) * p.q_scale : 0.f;
+                amax[g] = warp_max(fabsf(x[g]));
+            }
+            if (lane == 0) {
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) gred[g * 4 + sw] = amax[g];
+            }
+            named_barrier(gbar, UM_SOFT);
+#pragma unroll
+            for (int g = 0; g < QGP; ++g) amax[g] = max4(reinterpret_cast<const float4*>(gred)[g]);
+            uint8_t* qbuf = smem + C::Q_OFF + b * C::QBUF;
+#pragma unroll
+            for (int g = 0; g < QGP; ++g) {
+                int e = 0;
+                frexpf(amax[g], &e);
+                const bool live = amax[g] > 0.f && amax[g] < 3.0e38f;
+                // fp16: x * 2^(14 - e) in [-2^14, 2^14) as hi + lo halves; int8: the integer
+                // x * 2^(30 - e), |.| < 2^30, as four signed limbs
+                const float pre = live ? ldexpf(1.f, (KVT == 1 ? 14 : 30) - e) : 1.f;
+                if (gt == 0) s_qscale[(no & 3) * 8 + g] = 1.f / pre;
+                if constexpr (KVT == 1) {
+                    const float xs = x[g] * pre;
+                    const __half hi = __float2half_rn(xs);
+                    const __half lo = __float2half_rn(xs - __half2float(hi));
+                    const int col = (d % 64) * 2, sb = d / 64;
+                    *reinterpret_cast<__half*>(qbuf + sb * (C::NMAX * 128) + swz_off(g, col)) = hi;
+                    *reinterpret_cast<__half*>(qbuf + sb * (C::NMAX * 128) + swz_off(QGP + g, col)) = lo;
+                } else {
+                    int8_t l[4];
+                    limbs4(__float2int_rn(x[g] * pre), l);
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) *reinterpret_cast<int8_t*>(qbuf + swz_off(g * 4 + r, d)) = l[r];
+                }
+            }
+            fence_proxy_async_smem();  // generic writes of Qhat^T before the MMA reads them
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&q_full[b]);
+            if (gt == 0) {  // the score factors for group 0 (written by this thread above)
+                __threadfence_block();
+                *s_qprep = no + 1;
+            }
+        };
+        if (gi == 1 && next_nonempty()) prep_q(un, 0);
+        // Group 0's arrival on the split-K counter of its previous multi-partition unit: resolved one
+        // unit later (the atomic's round trip overlaps the next unit) and merged then if it was last.
+        Unit pend;
+        bool have_pend = false;
+        unsigned long long pend_old = 0;
+
         while (cur.advance(u)) {
             if (u.nparts == 0) {
                 if (gi == 0) store_tokenless_unit<UM_D>(p, u, gt, UM_SOFT);
                 continue;
             }
             const int qb = unit_no & 1;
-            // ---- Qhat^T for this unit (written by group 0): row (head g, part r) = fp16 half r of q,
-            // or int8 limb r. Both groups compute the per-head factors.
-            if (gi == 0 && unit_no >= 2) {
-                if (!*s_abort && !mbar_wait_bounded(&q_free[qb], ((unit_no - 2) >> 1) & 1, s_abort)) give_up();
-            }
+            if (gi == 1 && next_nonempty()) prep_q(un, unit_no + 1);
+            // this unit's score factors, written one unit ahead by group 1 (a counter, not a parity
+            // wait: group 1 can be two units ahead of group 0 here)
+            if (gi == 0 && !*s_abort && !wait_counter(s_qprep, unit_no + 1, s_abort)) give_up();
+            __threadfence_block();
             float qscale[QGP];  // per head: the factor that turns the combined MMA result into a log2 score
-            {
-                const int d = my_lane;  // one head-dim element per thread
-                float x[QGP], amax[QGP];
 #pragma unroll
-                for (int g = 0; g < QGP; ++g) {
-                    x[g] = g < u.nh ? __ldg(p.q + ((size_t)u.b * p.H + u.h0 + g) * UM_D + d) * p.q_scale : 0.f;
-                    amax[g] = warp_max(fabsf(x[g]));
-                }
-                if (lane == 0) {
-#pragma unroll
-                    for (int g = 0; g < QGP; ++g) gred[g * 4 + sw] = amax[g];
-                }
-                named_barrier(gbar, UM_SOFT);
-#pragma unroll
-                for (int g = 0; g < QGP; ++g) amax[g] = max4(reinterpret_cast<const float4*>(gred)[g]);
-                uint8_t* qbuf = smem + C::Q_OFF + qb * C::QBUF;
-#pragma unroll
-                for (int g = 0; g < QGP; ++g) {
-                    int e = 0;
-                    frexpf(amax[g], &e);
-                    const bool live = amax[g] > 0.f && amax[g] < 3.0e38f;
-                    if constexpr (KVT == 1) {
-                        // x * 2^(14 - e) in [-2^14, 2^14): hi + lo halves
-                        const float pre = live ? ldexpf(1.f, 14 - e) : 1.f;
-                        qscale[g] = 1.f / pre;
-                        if (gi == 0) {
-                            const float xs = x[g] * pre;
-                            const __half hi = __float2half_rn(xs);
-                            const __half lo = __float2half_rn(xs - __half2float(hi));
-                            const int col = (d % 64) * 2, sb = d / 64;
-                            *reinterpret_cast<__half*>(qbuf + sb * (C::NMAX * 128) + swz_off(g, col)) = hi;
-                            *reinterpret_cast<__half*>(qbuf + sb * (C::NMAX * 128) + swz_off(QGP + g, col)) = lo;
-                        }
-                    } else {
-                        // integer x * 2^(30 - e) with |.| < 2^30, as four signed limbs
-                        const float pre = live ? ldexpf(1.f, 30 - e) : 1.f;
-                        qscale[g] = 1.f / pre;
-                        if (gi == 0) {
-                            int8_t l[4];
-                            limbs4(__float2int_rn(x[g] * pre), l);
-#pragma unroll
-                            for (int r = 0; r < 4; ++r) *reinterpret_cast<int8_t*>(qbuf + swz_off(g * 4 + r, d)) = l[r];
-                        }
-                    }
-                }
-            }
-            if (gi == 0) {
-                fence_proxy_async_smem();  // generic writes of Qhat^T before the MMA reads them
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&q_full[qb]);
-            }
+            for (int g = 0; g < QGP; ++g) qscale[g] = s_qscale[(unit_no & 3) * 8 + g];
 
             // ---- chunks
             float m[QGP], lsum[QGP], o[QGP];  // running max (group-uniform), this thread's sum share, O row
@@ -804,11 +837,13 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 const float4 l4 = reinterpret_cast<const float4*>(gred + 112)[g];
                 L[g] = (l4.x + l4.y) + (l4.z + l4.w);
             }
-            // Group 1 hands its state over in its own Phat buffer (its last PV product is done: the
-            // fold above waited for it) and in the spare end of its reduction floats.
-            float* xo = reinterpret_cast<float*>(smem + C::P_OFF + C::PBUF);  // [QGP][128] O rows
-            float* xml = red + UM_GRED + 144;                               // [QGP] m, [QGP] L, [1] bad
+            // Group 1 hands its state over through xbuf and goes on with the next unit; group 0 merges it
+            // in, stores the unit's result and counts the partition in (x_full / x_free order the
+            // handover across units).
+            float* xo = xbuf;                  // [QGP][128] O rows
+            float* xml = xbuf + QGP * UM_D;    // [QGP] m, [QGP] L, [1] bad
             if (gi == 1) {
+                if (unit_no >= 1 && !*s_abort && !mbar_wait_bounded(x_free, (unit_no - 1) & 1, s_abort)) give_up();
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) xo[g * UM_D + my_lane] = o[g];
                 if (gt == 0) {
@@ -816,10 +851,10 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     for (int g = 0; g < QGP; ++g) xml[g] = m[g], xml[QGP + g] = L[g];
                     xml[2 * QGP] = grp_bad ? 1.f : 0.f;
                 }
-                named_barrier(4, 2 * UM_SOFT);  // group 1's state is written
-                named_barrier(4, 2 * UM_SOFT);  // group 0 has read it
+                named_barrier(gbar, UM_SOFT);  // the whole group's writes come before the arrivals
+                if (lane == 0) mbar_arrive(x_full);
             } else {
-                named_barrier(4, 2 * UM_SOFT);
+                if (!*s_abort && !mbar_wait_bounded(x_full, unit_no & 1, s_abort)) give_up();
                 const bool any_bad = grp_bad || xml[2 * QGP] != 0.f;
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) {
@@ -830,7 +865,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     L[g] = L[g] * w0 + l1 * w1;
                     m[g] = mm;
                 }
-                named_barrier(4, 2 * UM_SOFT);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(x_free);
                 const float nanv = __int_as_float(0x7fc00000);
                 const int d = my_lane;
 #pragma unroll
@@ -846,10 +882,26 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                         if (d == 0) p.part_ml[slot] = make_float2(m[g], any_bad ? nanv : L[g]);
                     }
                 }
+                // Count this partition in (the result is read one unit later) and merge the previous
+                // unit's partitions if its arrival was the last one.
+                named_barrier(gbar, UM_SOFT);  // the partial stores come before the arrival
+                if (gt == 0) {
+                    if (have_pend) *s_flag = resolve_arrival(p, pend, pend_old);
+                    if (u.nparts > 1) pend_old = arrive_partition(p, u);
+                }
+                if (have_pend) {
+                    named_barrier(gbar, UM_SOFT);
+                    if (*s_flag) merge_partitions<UM_D, 12>(p, pend, gt, UM_SOFT);
+                }
+                have_pend = u.nparts > 1;
+                pend = u;
             }
-            // both groups: count the partition in; the last partition's CTA merges them all
-            finish_partition<UM_D, 12>(p, u, tid, 2 * UM_SOFT, 4, s_flag);
             ++unit_no;
+        }
+        if (gi == 0 && have_pend) {  // the last unit's arrival
+            if (gt == 0) *s_flag = resolve_arrival(p, pend, pend_old);
+            named_barrier(gbar, UM_SOFT);
+            if (*s_flag) merge_partitions<UM_D, 12>(p, pend, gt, UM_SOFT);
         }
     }
 

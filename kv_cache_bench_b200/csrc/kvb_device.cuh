@@ -93,6 +93,20 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
 }
 
+// Waits until the shared-memory counter `*c` reaches `target` (another warp raises it), for at most
+// KVB_WAIT_LIMIT_NS (or until `*abort` is set). Returns false when it gave up.
+__device__ __forceinline__ bool wait_counter(volatile int* c, int target, volatile int* abort) {
+    if (*c >= target) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (*c >= target) return true;
+        if ((it & 255u) == 0) {
+            if (*abort) return false;
+            if (globaltimer_ns() - t0 > KVB_WAIT_LIMIT_NS) return false;
+        }
+    }
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -418,37 +432,54 @@ __device__ __forceinline__ unsigned long long atom_add_acq_rel(unsigned long lon
     return old;
 }
 
+// Counts partition u in: one atomic add on its (b, head group) counter, returning the old word.
+// Called by one thread after a barrier that orders the CTA's partial stores before it (release).
+__device__ __forceinline__ unsigned long long arrive_partition(const DecodeParams& p, const Unit& u) {
+    return atom_add_acq_rel(p.counters + (size_t)u.b * p.nhg + u.hg, 1ull);
+}
+
+// Whether the arrival that returned `old` was the last partition of u (then the counter is left
+// clean for the next launch). A stale epoch is claimed here; see above.
+__device__ __forceinline__ bool resolve_arrival(const DecodeParams& p, const Unit& u, unsigned long long old) {
+    unsigned long long* ctr = p.counters + (size_t)u.b * p.nhg + u.hg;
+    const unsigned epoch = unsigned(old >> 32);
+    unsigned arrived;
+    if (epoch == p.launch || epoch == KVB_CTR_CLEAN) {
+        arrived = unsigned(old) + 1u;
+    } else {
+        __threadfence();
+        unsigned long long seen = old + 1ull;
+        for (;;) {
+            const unsigned long long cur = atomicCAS(ctr, seen, (unsigned long long)p.launch << 32);
+            const unsigned e = unsigned(cur >> 32);
+            if (cur == seen || e == p.launch || e == KVB_CTR_CLEAN) break;
+            seen = cur;
+        }
+        arrived = unsigned(atom_add_acq_rel(ctr, 1ull)) + 1u;
+    }
+    const bool last = arrived == unsigned(u.nparts);
+    if (arrived > unsigned(u.nparts)) raise_error(p.error_flag, KVB_DEVERR_STATE);
+    if (last) atomicExch(ctr, (unsigned long long)KVB_CTR_CLEAN << 32);
+    return last;
+}
+
+template <int D, int BATCH = 8>
+__device__ __forceinline__ void merge_partitions(const DecodeParams& p, const Unit& u, int tid, int nthreads);
+
 template <int D, int BATCH = 8>
 __device__ __forceinline__ void finish_partition(const DecodeParams& p, const Unit& u, int tid, int nthreads,
                                                  uint32_t bar_id, int* s_flag) {
     if (u.nparts <= 1) return;
     named_barrier(bar_id, nthreads);  // every thread's partial stores come before the arrival below
-    if (tid == 0) {
-        unsigned long long* ctr = p.counters + (size_t)u.b * p.nhg + u.hg;
-        const unsigned long long old = atom_add_acq_rel(ctr, 1ull);
-        const unsigned epoch = unsigned(old >> 32);
-        unsigned arrived;
-        if (epoch == p.launch || epoch == KVB_CTR_CLEAN) {
-            arrived = unsigned(old) + 1u;
-        } else {
-            __threadfence();
-            unsigned long long seen = old + 1ull;
-            for (;;) {
-                const unsigned long long cur = atomicCAS(ctr, seen, (unsigned long long)p.launch << 32);
-                const unsigned e = unsigned(cur >> 32);
-                if (cur == seen || e == p.launch || e == KVB_CTR_CLEAN) break;
-                seen = cur;
-            }
-            arrived = unsigned(atom_add_acq_rel(ctr, 1ull)) + 1u;
-        }
-        const int last = arrived == unsigned(u.nparts);
-        if (arrived > unsigned(u.nparts)) raise_error(p.error_flag, KVB_DEVERR_STATE);
-        if (last) atomicExch(ctr, (unsigned long long)KVB_CTR_CLEAN << 32);
-        *s_flag = last;
-    }
+    if (tid == 0) *s_flag = resolve_arrival(p, u, arrive_partition(p, u));
     named_barrier(bar_id, nthreads);
-    if (!*s_flag) return;
+    if (*s_flag) merge_partitions<D, BATCH>(p, u, tid, nthreads);
+}
 
+// The merge of all partitions of u into `out` (the CTA of the last partition, every other
+// partition's stores visible through the acquiring arrival).
+template <int D, int BATCH>
+__device__ __forceinline__ void merge_partitions(const DecodeParams& p, const Unit& u, int tid, int nthreads) {
     constexpr int D4 = D / 4;
     const int np = u.nparts, nh = u.nh;
     const int pairs = nh * D4;
