@@ -1,0 +1,65 @@
+"""bench.py's host-side pieces on the CPU: the workloads (BASELINE.json's five configs), the
+algorithmic byte count (the reference's Workload::min_bytes, src/workload.hpp:69-74), the seeded
+layouts, the bounded CPU samples, and the reference arm's JSON line (it needs no GPU)."""
+import json
+import math
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+import bench  # noqa: E402
+
+
+def test_workloads_match_the_configs():
+    w1, w2, w3, w4, w5 = (bench.workload(c, None) for c in range(1, 6))
+    assert (w1["kv"], w1["lens"], w1["page"], w1["pool_blocks"]) == ("f32", [512], 16, 64)
+    assert (w2["kv"], w2["lens"], w2["page"], w2["pool_blocks"], w2["part"]) == ("f16", [4096], 32, 256, 512)
+    assert (w3["kv"], w3["lens"], w3["page"], w3["pool_blocks"]) == ("i8", [32768], 128, 512)
+    assert len(w4["lens"]) == 64 and 512 <= min(w4["lens"]) and max(w4["lens"]) <= 32768 and w4["page"] == 16
+    assert len(w5["lens"]) == 256 and 8192 <= min(w5["lens"]) and max(w5["lens"]) <= 131072
+    assert (w5["H"], w5["Hkv"], w5["page"]) == (64, 8, 64)
+    assert bench.workload(3, "f16")["kv"] == "f16"
+
+
+def test_min_bytes_is_the_references_count():
+    w = bench.workload(3, None)
+    assert bench.min_bytes(w, w["lens"], w["Hkv"], w["H"]) == 67_141_632
+    w = bench.workload(3, "f16")
+    assert bench.min_bytes(w, w["lens"], w["Hkv"], w["H"]) == 134_250_496
+    w = bench.workload(1, None)
+    assert bench.min_bytes(w, w["lens"], w["Hkv"], w["H"]) == 4_227_072
+    w = bench.workload(2, None)
+    assert bench.min_bytes(w, w["lens"], w["Hkv"], w["H"]) == 16_809_984
+
+
+def test_layout_gives_each_sequence_distinct_blocks():
+    rng = np.random.default_rng(4)
+    lens = [100, 0, 17, 64]
+    table, nb = bench.build_layout(lens, 16, 1.1, None, rng)
+    live = [b for i, l in enumerate(lens) for b in table[i, : math.ceil(l / 16)]]
+    assert len(set(live)) == len(live) and all(0 <= b < nb for b in live)
+    assert (table[1] == -1).all()
+
+
+def test_sample_lens_cuts_a_prefix():
+    w = dict(lens=[300, 200, 100])
+    assert bench.sample_lens(w, 10_000) == [300, 200, 100]
+    assert bench.sample_lens(w, 450) == [300, 150]
+    assert bench.sample_lens(w, 1) == [1]
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(ROOT, "oracle", "_ref", "kvb_ref_cpu")),
+                    reason="the reference's CPU timer was not built")
+def test_reference_arm_prints_the_contract_line():
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--config", "1",
+                          "--steps", "3", "--warmup", "1"], check=True, capture_output=True, text=True, timeout=300)
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["value"] > 0 and line["unit"] == "GB/s"
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+    assert line["cpu_baseline"]["kind"] == "reference" and line["cpu_baseline"]["cores"] >= 1
+    assert line["metric"] == bench.METRIC and line["higher_is_better"] is True
