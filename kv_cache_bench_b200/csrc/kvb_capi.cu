@@ -119,7 +119,7 @@ Geometry geometry(const kvb_paged_args* a, int num_sms) {
         // up to whole chunks of the kernel.
         const bool umma = g.kernel == KVB_KERNEL_UMMA;
         const long long chunk = umma ? 128 : KVB_CHUNK;
-        const long long part_max = umma ? 4096 : 2048;
+        const long long part_max = umma && a->page_size >= 16 ? 4096 : 2048;  // tcgen05: its page table
         const long long S = std::max<long long>(1, (long long)s.batch * g.nhg);
         const long long slots = (umma ? 1LL : 2LL) * std::max(1, num_sms);
         long long n = S < slots ? std::max<long long>(1, slots / S) : 1;

@@ -53,7 +53,8 @@ static_assert(2 * 128 * UM_REGS_SOFT + 128 * UM_REGS_CTRL <= UM_THREADS * UM_REG
 constexpr int UM_SOFT = 128;          // threads of one softmax group
 constexpr int UM_D = 128;             // head dim
 constexpr int TILE = UM_CHUNK * 128;  // bytes of one [128 rows][128 B] swizzled tile
-constexpr int UM_PT = 528;            // page-table entries: pages of one partition, at most
+constexpr int UM_PT = 264;            // page-table entries: pages of one partition, at most
+constexpr int UM_UCH = 64;            // chunks of one partition, at most (partitions <= 8064 tokens)
 constexpr int UM_GRED = 176;          // reduction floats per softmax group
 
 // ---- tcgen05 wrappers -----------------------------------------------------------------------------
@@ -176,7 +177,7 @@ template <int KVT>
 struct UCfg {
     static constexpr int NSUB = KVT == 1 ? 2 : 1;             // 128-byte column slices of a row
     static constexpr int STAGE = 2 * NSUB * TILE;              // K tiles, then V tiles
-    static constexpr int STAGES = KVT == 1 ? 3 : 5;
+    static constexpr int STAGES = KVT == 1 ? 3 : 6;
     static constexpr int NMAX = KVT == 1 ? 16 : 32;            // MMA N (rows of Qhat / Phat)
     static constexpr int QBUF = NMAX * 128 * NSUB;             // one Qhat^T buffer ([N][128 B] per slice)
     static constexpr int PBUF = NMAX * 128 * NSUB;             // one Phat^T buffer
@@ -184,10 +185,12 @@ struct UCfg {
     static constexpr size_t Q_OFF = RING;                      // 2 Qhat buffers (1024-aligned)
     static constexpr size_t P_OFF = Q_OFF + 2 * QBUF;          // 2 Phat buffers
     static constexpr size_t BAD_OFF = P_OFF + 2 * PBUF;        // [STAGES] a block id of the chunk was refused
-    static constexpr size_t BAR_OFF = kvb_align_up(BAD_OFF + STAGES * sizeof(int), 64);
+    // int8: largest V scale of every chunk of a unit, [2 units][UM_UCH chunks]
+    static constexpr size_t VSMAX_OFF = BAD_OFF + STAGES * sizeof(int);
+    static constexpr size_t BAR_OFF = kvb_align_up(VSMAX_OFF + (KVT == 2 ? 2 * UM_UCH : 0) * sizeof(float), 64);
     // full per (stage, chunk parity); empty per stage; q_full, q_free, s_full, s_free, p_full,
-    // o_full, pt_free x2; x_full, x_free
-    static constexpr int NBARS = 3 * STAGES + 2 * 7 + 2;
+    // o_full, pt_free x2
+    static constexpr int NBARS = 3 * STAGES + 2 * 7;
     static constexpr size_t RED_OFF = kvb_align_up(BAR_OFF + NBARS * sizeof(uint64_t), 16);
     static constexpr size_t WIN_OFF = RED_OFF + 2 * UM_GRED * sizeof(float);
     // page table: block ids [UM_PT]; int8: scales [2 buffers][UM_PT] for K and for V
@@ -196,10 +199,8 @@ struct UCfg {
     static constexpr size_t LENS_OFF = PREFIX_OFF + sizeof(int) * (KVB_PREFIX_MAX + 1);
     static constexpr size_t SCRATCH_OFF = kvb_align_up(LENS_OFF + sizeof(int) * KVB_PREFIX_MAX, 16);
     static constexpr size_t SCRATCH_FLOATS = 512;              // prefix scan
-    static constexpr size_t XBUF_OFF = SCRATCH_OFF + SCRATCH_FLOATS * sizeof(float);
-    static constexpr size_t XBUF_FLOATS = 8 * 128 + 2 * 8 + 4;  // group 1's O rows, max, sums, bad flag
-    static constexpr size_t MISC_OFF = kvb_align_up(XBUF_OFF + XBUF_FLOATS * sizeof(float), 64);
-    static constexpr size_t SMEM = MISC_OFF + 256 + 1024;
+    static constexpr size_t MISC_OFF = kvb_align_up(SCRATCH_OFF + SCRATCH_FLOATS * sizeof(float), 64);
+    static constexpr size_t SMEM = MISC_OFF + 64 + 1024;
 };
 
 static_assert(UCfg<1>::SMEM <= 227 * 1024 && UCfg<2>::SMEM <= 227 * 1024, "shared memory budget");
@@ -208,6 +209,7 @@ static_assert(UCfg<1>::MISC_OFF % 64 == 0 && UCfg<2>::MISC_OFF % 64 == 0, "align
 static_assert(UCfg<1>::Q_OFF % 1024 == 0 && UCfg<1>::P_OFF % 1024 == 0 && UCfg<2>::P_OFF % 1024 == 0,
               "swizzled operands need 1024-byte alignment");
 static_assert(UCfg<2>::SCRATCH_FLOATS >= UM_THREADS, "prefix scan scratch");
+static_assert(UCfg<1>::PBUF >= 8 * 128 * 4 && UCfg<2>::PBUF >= 8 * 128 * 4, "group 1's O rows fit its Phat buffer");
 
 template <int KVT, int QGP>  // QGP: query heads per group, padded to 1, 2, 4 or 8
 __global__ void __launch_bounds__(UM_THREADS, 1)
@@ -218,11 +220,17 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     constexpr int qgp = QGP;
     constexpr int RPH = KVT == 1 ? 2 : 4;  // rows of Qhat/Phat per head (halves or limbs)
     constexpr int N = RPH * qgp < 8 ? 8 : RPH * qgp;  // MMA N
+    // Probabilities are exp2(score - m) <= 2^kTau (lazy re-referencing). int8: p * v_scale / (largest
+    // v_scale of the chunk) * kPScale is an integer below 2^30; kPUnit = 1 / kPScale.
+    constexpr float kTau = KVT == 1 ? 8.f : 2.f;
+    constexpr float kPScale = 268435456.f;          // 2^28 = 2^(30 - kTau) for int8
+    constexpr float kPUnit = 3.7252902984619141e-09f;  // 2^-28
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
     int* stage_bad = reinterpret_cast<int*>(smem + C::BAD_OFF);
+    float* unit_vsmax = reinterpret_cast<float*>(smem + C::VSMAX_OFF);  // int8: [2][UM_UCH]
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
     // Chunk k (running index over the CTA's units) lives in stage k % STAGES and is announced on
     // full[k % (2 * STAGES)]: a stage alternates between even and odd chunks, whose consumers (MMA
@@ -237,8 +245,6 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     uint64_t* p_full = q_full + 8;         // [2] Phat^T written, previous O^T folded (softmax -> MMA)
     uint64_t* o_full = q_full + 10;        // [2] O^T ready (MMA -> softmax)
     uint64_t* pt_free = q_full + 12;       // [2] int8 scale buffer read (softmax -> producer)
-    uint64_t* x_full = q_full + 14;        // group 1's unit state handed over (group 1 -> group 0)
-    uint64_t* x_free = q_full + 15;        // ... and read (group 0 -> group 1)
     float* red = reinterpret_cast<float*>(smem + C::RED_OFF);
     int* pt_blk = reinterpret_cast<int*>(smem + C::WIN_OFF);
     float* pt_ks = reinterpret_cast<float*>(pt_blk + UM_PT);  // int8 only: [2][UM_PT]
@@ -249,9 +255,6 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::MISC_OFF);
     int* s_flag = reinterpret_cast<int*>(smem + C::MISC_OFF + 8);
     uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF + 16);
-    volatile int* s_qprep = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 24);  // units with Qhat ready
-    float* s_qscale = reinterpret_cast<float*>(smem + C::MISC_OFF + 64);  // [unit % 4][8 heads]
-    float* xbuf = reinterpret_cast<float*>(smem + C::XBUF_OFF);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // The unit enumeration starts with the sequence lengths and the block table: have them on the
@@ -283,10 +286,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             mbar_init(&o_full[i], 1);
             mbar_init(&pt_free[i], 2 * UM_SOFT / 32);
         }
-        mbar_init(x_full, UM_SOFT / 32);
-        mbar_init(x_free, UM_SOFT / 32);
         *s_abort = 0;
-        *s_qprep = 0;
         fence_mbarrier_init();
     }
     if (warp == UM_TMEM_WARP) {
@@ -405,6 +405,16 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                         const int b2 = pt_blk[i];
                         ks_b[i] = b2 >= 0 ? __ldg(p.k_scale + (size_t)b2 * p.Hkv + u.kvh) : 0.f;
                         vs_b[i] = b2 >= 0 ? __ldg(p.v_scale + (size_t)b2 * p.Hkv + u.kvh) : 0.f;
+                    }
+                    __syncwarp();
+                    // the largest V scale of each of the unit's chunks (an int8 probability scale bound)
+                    float* um = unit_vsmax + sb * UM_UCH;
+                    for (int j = lane; j < c1 - c0 && j < UM_UCH; j += 32) {
+                        const int a = max(((c0 + j) * UM_CHUNK) >> lp, pg0) - pg0;
+                        const int z = min((((c0 + j + 1) * UM_CHUNK - 1) >> lp), pg1) - pg0;
+                        float vmax = 0.f;
+                        for (int i = a; i <= z; ++i) vmax = fmaxf(vmax, vs_b[i]);
+                        um[j] = vmax;
                     }
                     __syncwarp();  // every lane's scale writes happen before the arrive
                     if (lane == 0) mbar_arrive(fb);
@@ -543,7 +553,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         reg_alloc<UM_REGS_SOFT>();
         // Two warpgroups take alternate chunks: group gi handles the chunks whose running index k has
         // k & 1 == gi, with its own tensor-memory S/O buffers and Phat buffer, and its own running
-        // (max, sum, O). Group 1 hands its state to group 0 once per unit.
+        // (max, sum, O). The groups merge once per unit.
         const int gi = warp >> 2;
         const int gt = tid - gi * UM_SOFT;  // 0..127 within the group
         const int sw = gt >> 5;                  // warp within the group
@@ -551,96 +561,77 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         // this warp's tensor-memory lane quarter is fixed by warp % 4
         const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;
         const int my_lane = (warp & 3) * 32 + lane;  // token in S^T, head dim in O^T
-        // [0,32) q absmax (group 0); [32,112) chunk max x2 ([value][warp]: 8 heads, V scale);
-        // [112,144) sums
+        // [0,32) q absmax; [32,112) chunk max x2 ([value][warp]: 8 heads, V scale); [112,144) sums;
+        // group 1: [144,161) state handed to group 0 at the unit's end
         float* gred = red + gi * UM_GRED;
         UnitCursor cur{&p, prefix, (long long)blockIdx.x, total, prefix ? s_lens : nullptr};
         Unit u;
         int stage = 0;
         int k = 0;  // running chunk index
         int unit_no = 0;
-
-        // Group 1 writes Qhat^T and the per-head score factors of non-empty unit number `no` into
-        // buffer no & 1, one unit ahead of the one both groups process, so the MMA warps can start a
-        // unit while group 0 finishes the previous one: row (head g, part r) = fp16 half r of q, or
-        // int8 limb r.
-        UnitCursor ahead = cur;
-        Unit un;
-        auto next_nonempty = [&]() {
-            while (ahead.advance(un))
-                if (un.nparts != 0) return true;
-            return false;
-        };
-        auto prep_q = [&](const Unit& v, int no) {
-            const int b = no & 1;
-            if (no >= 2 && !*s_abort && !mbar_wait_bounded(&q_free[b], ((no - 2) >> 1) & 1, s_abort)) give_up();
-            const int d = my_lane;  // one head-dim element per thread
-            float x[QGP], amax[QGP];
-#pragma unroll
-            for (int g = 0; g < QGP; ++g) {
-                x[g] = g < v.nh ? __ldg(p.q + ((size_t)v.b * p.H + v.h0 + g) * UM_D + d) * p.q_scale : 0.f;
-                amax[g] = warp_max(fabsf(x[g]));
-            }
-            if (lane == 0) {
-#pragma unroll
-                for (int g = 0; g < QGP; ++g) gred[g * 4 + sw] = amax[g];
-            }
-            named_barrier(gbar, UM_SOFT);
-#pragma unroll
-            for (int g = 0; g < QGP; ++g) amax[g] = max4(reinterpret_cast<const float4*>(gred)[g]);
-            uint8_t* qbuf = smem + C::Q_OFF + b * C::QBUF;
-#pragma unroll
-            for (int g = 0; g < QGP; ++g) {
-                int e = 0;
-                frexpf(amax[g], &e);
-                const bool live = amax[g] > 0.f && amax[g] < 3.0e38f;
-                // fp16: x * 2^(14 - e) in [-2^14, 2^14) as hi + lo halves; int8: the integer
-                // x * 2^(30 - e), |.| < 2^30, as four signed limbs
-                const float pre = live ? ldexpf(1.f, (KVT == 1 ? 14 : 30) - e) : 1.f;
-                if (gt == 0) s_qscale[(no & 3) * 8 + g] = 1.f / pre;
-                if constexpr (KVT == 1) {
-                    const float xs = x[g] * pre;
-                    const __half hi = __float2half_rn(xs);
-                    const __half lo = __float2half_rn(xs - __half2float(hi));
-                    const int col = (d % 64) * 2, sb = d / 64;
-                    *reinterpret_cast<__half*>(qbuf + sb * (C::NMAX * 128) + swz_off(g, col)) = hi;
-                    *reinterpret_cast<__half*>(qbuf + sb * (C::NMAX * 128) + swz_off(QGP + g, col)) = lo;
-                } else {
-                    int8_t l[4];
-                    limbs4(__float2int_rn(x[g] * pre), l);
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) *reinterpret_cast<int8_t*>(qbuf + swz_off(g * 4 + r, d)) = l[r];
-                }
-            }
-            fence_proxy_async_smem();  // generic writes of Qhat^T before the MMA reads them
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&q_full[b]);
-            if (gt == 0) {  // the score factors for group 0 (written by this thread above)
-                __threadfence_block();
-                *s_qprep = no + 1;
-            }
-        };
-        if (gi == 1 && next_nonempty()) prep_q(un, 0);
-        // Group 0's arrival on the split-K counter of its previous multi-partition unit: resolved one
-        // unit later (the atomic's round trip overlaps the next unit) and merged then if it was last.
-        Unit pend;
-        bool have_pend = false;
-        unsigned long long pend_old = 0;
-
         while (cur.advance(u)) {
             if (u.nparts == 0) {
                 if (gi == 0) store_tokenless_unit<UM_D>(p, u, gt, UM_SOFT);
                 continue;
             }
             const int qb = unit_no & 1;
-            if (gi == 1 && next_nonempty()) prep_q(un, unit_no + 1);
-            // this unit's score factors, written one unit ahead by group 1 (a counter, not a parity
-            // wait: group 1 can be two units ahead of group 0 here)
-            if (gi == 0 && !*s_abort && !wait_counter(s_qprep, unit_no + 1, s_abort)) give_up();
-            __threadfence_block();
+            // ---- Qhat^T for this unit (written by group 0): row (head g, part r) = fp16 half r of q,
+            // or int8 limb r. Both groups compute the per-head factors.
+            if (gi == 0 && unit_no >= 2) {
+                if (!*s_abort && !mbar_wait_bounded(&q_free[qb], ((unit_no - 2) >> 1) & 1, s_abort)) give_up();
+            }
             float qscale[QGP];  // per head: the factor that turns the combined MMA result into a log2 score
+            {
+                const int d = my_lane;  // one head-dim element per thread
+                float x[QGP], amax[QGP];
 #pragma unroll
-            for (int g = 0; g < QGP; ++g) qscale[g] = s_qscale[(unit_no & 3) * 8 + g];
+                for (int g = 0; g < QGP; ++g) {
+                    x[g] = g < u.nh ? __ldg(p.q + ((size_t)u.b * p.H + u.h0 + g) * UM_D + d) * p.q_scale : 0.f;
+                    amax[g] = warp_max(fabsf(x[g]));
+                }
+                if (lane == 0) {
+#pragma unroll
+                    for (int g = 0; g < QGP; ++g) gred[g * 4 + sw] = amax[g];
+                }
+                named_barrier(gbar, UM_SOFT);
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) amax[g] = max4(reinterpret_cast<const float4*>(gred)[g]);
+                uint8_t* qbuf = smem + C::Q_OFF + qb * C::QBUF;
+#pragma unroll
+                for (int g = 0; g < QGP; ++g) {
+                    int e = 0;
+                    frexpf(amax[g], &e);
+                    const bool live = amax[g] > 0.f && amax[g] < 3.0e38f;
+                    if constexpr (KVT == 1) {
+                        // x * 2^(14 - e) in [-2^14, 2^14): hi + lo halves
+                        const float pre = live ? ldexpf(1.f, 14 - e) : 1.f;
+                        qscale[g] = 1.f / pre;
+                        if (gi == 0) {
+                            const float xs = x[g] * pre;
+                            const __half hi = __float2half_rn(xs);
+                            const __half lo = __float2half_rn(xs - __half2float(hi));
+                            const int col = (d % 64) * 2, sb = d / 64;
+                            *reinterpret_cast<__half*>(qbuf + sb * (C::NMAX * 128) + swz_off(g, col)) = hi;
+                            *reinterpret_cast<__half*>(qbuf + sb * (C::NMAX * 128) + swz_off(QGP + g, col)) = lo;
+                        }
+                    } else {
+                        // integer x * 2^(30 - e) with |.| < 2^30, as four signed limbs
+                        const float pre = live ? ldexpf(1.f, 30 - e) : 1.f;
+                        qscale[g] = 1.f / pre;
+                        if (gi == 0) {
+                            int8_t l[4];
+                            limbs4(__float2int_rn(x[g] * pre), l);
+#pragma unroll
+                            for (int r = 0; r < 4; ++r) *reinterpret_cast<int8_t*>(qbuf + swz_off(g * 4 + r, d)) = l[r];
+                        }
+                    }
+                }
+            }
+            if (gi == 0) {
+                fence_proxy_async_smem();  // generic writes of Qhat^T before the MMA reads them
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&q_full[qb]);
+            }
 
             // ---- chunks
             float m[QGP], lsum[QGP], o[QGP];  // running max (group-uniform), this thread's sum share, O row
@@ -657,19 +648,25 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             const float* vs_b = pt_vs + qb * UM_PT;
 
             // Folds O^T of this group's previous chunk (running index kp; its PV product completes the
-            // buffer's (kp >> 1)-th use) into the registers.
-            auto fold_prev = [&](int kp) {
-                if (!*s_abort && !mbar_wait_bounded(&o_full[gi], uint32_t(kp >> 1) & 1, s_abort)) give_up();
-                tc_fence_after();
-                uint32_t r[32];
-                tc_ld8(obuf, *reinterpret_cast<uint32_t(*)[8]>(&r[0]));
-                if (N > 8) tc_ld8(obuf + 8, *reinterpret_cast<uint32_t(*)[8]>(&r[8]));
+            // buffer's (kp >> 1)-th use) into the registers: loaded here, or already in `ro`.
+            uint32_t ro[32];
+            auto load_o = [&]() {
+                tc_ld8(obuf, *reinterpret_cast<uint32_t(*)[8]>(&ro[0]));
+                if (N > 8) tc_ld8(obuf + 8, *reinterpret_cast<uint32_t(*)[8]>(&ro[8]));
                 if (N > 16) {
-                    tc_ld8(obuf + 16, *reinterpret_cast<uint32_t(*)[8]>(&r[16]));
-                    tc_ld8(obuf + 24, *reinterpret_cast<uint32_t(*)[8]>(&r[24]));
+                    tc_ld8(obuf + 16, *reinterpret_cast<uint32_t(*)[8]>(&ro[16]));
+                    tc_ld8(obuf + 24, *reinterpret_cast<uint32_t(*)[8]>(&ro[24]));
                 }
-                tc_wait_ld();
-                tc_fence_before();
+            };
+            auto fold_prev = [&](int kp, bool loaded) {
+                if (!loaded) {
+                    if (!*s_abort && !mbar_wait_bounded(&o_full[gi], uint32_t(kp >> 1) & 1, s_abort)) give_up();
+                    tc_fence_after();
+                    load_o();
+                    tc_wait_ld();
+                    tc_fence_before();
+                }
+                const uint32_t* r = ro;
                 bool moved = false;  // the max moved since the previous chunk (group-uniform)
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) moved |= m_prev[g] != m[g];
@@ -680,7 +677,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                         v = __uint_as_float(r[g]) + __uint_as_float(r[QGP + g]);
                     } else {
                         v = limbs_to_float(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]) *
-                            (vscale_prev * 9.313225746154785e-10f);  // 2^-30
+                            (vscale_prev * kPUnit);
                     }
                     // o and the previous chunk are both relative to m_prev; move them to the current max
                     o[g] += v;
@@ -716,6 +713,11 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     tc_ld8(sa + 24, *reinterpret_cast<uint32_t(*)[8]>(&r[24]));
                 }
                 // this token's page scales (int8), read while the tensor-memory loads are in flight
+                // the previous chunk's O^T too, when its PV product is already done (one load wait);
+                // not for int8 with 8 heads, whose S^T and O^T together would not fit the registers
+                constexpr bool kEarlyO = !(KVT == 2 && QGP == 8);
+                const bool early_o = kEarlyO && have_prev && mbar_test(&o_full[gi], uint32_t(k_own >> 1) & 1);
+                if (early_o) load_o();
                 float ks = 1.f, vs = 0.f;
                 if constexpr (KVT == 2) {
                     const int slot = min(max((tok >> lp) - pg0, 0), pg_hi);
@@ -739,39 +741,37 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     sc[g] = (valid && g < u.nh) ? v * qscale[g] * ks : NEG_BIG;
                 }
                 bad |= stage_bad[cur_stage];
-                // chunk max per head (and int8: the largest V scale): warp, then the group's four warps
-                constexpr int NR = KVT == 2 ? QGP + 1 : QGP;
-                float mc[NR];
+                // Lazy re-referencing: probabilities are taken relative to the group's running max m and
+                // may reach 2^kTau; only when a score passes m + kTau (one vote per chunk) does the group
+                // agree on the chunk max (warp, then its four warps) and move m.
+                int exceed = 0;
 #pragma unroll
-                for (int g = 0; g < NR; ++g) mc[g] = warp_max(g < QGP ? sc[g] : vs);
-                float* rb = gred + 32 + 40 * int(use & 1);  // two alternating reduction slots, [value][warp]
-                if (lane == 0) {
+                for (int g = 0; g < QGP; ++g) exceed |= sc[g] > m[g] + kTau;
+                if (named_barrier_or(gbar, UM_SOFT, exceed)) {
+                    float* rb = gred + 32 + 40 * int(use & 1);  // two alternating reduction slots, [head][warp]
 #pragma unroll
-                    for (int g = 0; g < NR; ++g) rb[g * 4 + sw] = mc[g];
+                    for (int g = 0; g < QGP; ++g) {
+                        const float mc = warp_max(sc[g]);
+                        if (lane == 0) rb[g * 4 + sw] = mc;
+                    }
+                    named_barrier(gbar, UM_SOFT);
+#pragma unroll
+                    for (int g = 0; g < QGP; ++g) {
+                        const float mn = fmaxf(m[g], max4(reinterpret_cast<const float4*>(rb)[g]));
+                        lsum[g] *= exp2f(m[g] - mn);
+                        m[g] = mn;
+                    }
                 }
-                named_barrier(gbar, UM_SOFT);
-                float pr[QGP], mn[QGP];
-                bool moved = false;  // a running max changed (group-uniform: one branch, no divergence)
+                float pr[QGP];
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) {
-                    mn[g] = fmaxf(m[g], max4(reinterpret_cast<const float4*>(rb)[g]));
-                    moved |= mn[g] != m[g];
-                }
-                if (moved) {
-#pragma unroll
-                    for (int g = 0; g < QGP; ++g) lsum[g] *= exp2f(m[g] - mn[g]);
-                }
-#pragma unroll
-                for (int g = 0; g < QGP; ++g) {
-                    m[g] = mn[g];
-                    pr[g] = sc[g] > 0.5f * NEG_BIG ? exp2f(sc[g] - mn[g]) : 0.f;
+                    pr[g] = sc[g] > 0.5f * NEG_BIG ? exp2f(sc[g] - m[g]) : 0.f;
                     lsum[g] += pr[g];
                 }
-                float vscale_cur = 0.f;
-                if constexpr (KVT == 2) vscale_cur = max4(reinterpret_cast<const float4*>(rb)[QGP]);
+                const float vscale_cur = KVT == 2 ? unit_vsmax[qb * UM_UCH + min(c - c0, UM_UCH - 1)] : 0.f;
                 // The group's Phat buffer was last read by the PV product of its previous chunk: fold that
                 // chunk's O first (this also waits for that product), then overwrite.
-                if (have_prev) fold_prev(k_own);
+                if (have_prev) fold_prev(k_own, early_o);
                 uint8_t* pbuf = smem + C::P_OFF + gi * C::PBUF;
                 if constexpr (KVT == 1) {
                     const int col = (my_lane % 64) * 2, sb = my_lane / 64;
@@ -795,7 +795,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 } else {
                     // probability * v_scale / (largest v_scale of the chunk) as an unsigned integer below
                     // 2^30 whose four bytes are the four limbs
-                    const float f = vscale_cur > 0.f ? vs / vscale_cur * 1073741824.f : 0.f;  // 2^30
+                    const float f = vscale_cur > 0.f ? vs / vscale_cur * kPScale : 0.f;
 #pragma unroll
                     for (int g = 0; g < QGP; ++g) {
                         const uint32_t xi = __float2uint_rn(pr[g] * f);
@@ -817,7 +817,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&pt_free[qb]);  // the unit's scales are no longer read
             }
-            if (have_prev) fold_prev(k_own);
+            if (have_prev) fold_prev(k_own, false);
             // ---- unit epilogue: group sums across its 128 tokens, then the two groups merge
             float L[QGP];
 #pragma unroll
@@ -837,13 +837,11 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 const float4 l4 = reinterpret_cast<const float4*>(gred + 112)[g];
                 L[g] = (l4.x + l4.y) + (l4.z + l4.w);
             }
-            // Group 1 hands its state over through xbuf and goes on with the next unit; group 0 merges it
-            // in, stores the unit's result and counts the partition in (x_full / x_free order the
-            // handover across units).
-            float* xo = xbuf;                  // [QGP][128] O rows
-            float* xml = xbuf + QGP * UM_D;    // [QGP] m, [QGP] L, [1] bad
+            // Group 1 hands its state over in its own Phat buffer (its last PV product is done: the
+            // fold above waited for it) and in the spare end of its reduction floats.
+            float* xo = reinterpret_cast<float*>(smem + C::P_OFF + C::PBUF);  // [QGP][128] O rows
+            float* xml = red + UM_GRED + 144;                               // [QGP] m, [QGP] L, [1] bad
             if (gi == 1) {
-                if (unit_no >= 1 && !*s_abort && !mbar_wait_bounded(x_free, (unit_no - 1) & 1, s_abort)) give_up();
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) xo[g * UM_D + my_lane] = o[g];
                 if (gt == 0) {
@@ -851,10 +849,10 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     for (int g = 0; g < QGP; ++g) xml[g] = m[g], xml[QGP + g] = L[g];
                     xml[2 * QGP] = grp_bad ? 1.f : 0.f;
                 }
-                named_barrier(gbar, UM_SOFT);  // the whole group's writes come before the arrivals
-                if (lane == 0) mbar_arrive(x_full);
+                named_barrier(4, 2 * UM_SOFT);  // group 1's state is written
+                named_barrier(4, 2 * UM_SOFT);  // group 0 has read it
             } else {
-                if (!*s_abort && !mbar_wait_bounded(x_full, unit_no & 1, s_abort)) give_up();
+                named_barrier(4, 2 * UM_SOFT);
                 const bool any_bad = grp_bad || xml[2 * QGP] != 0.f;
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) {
@@ -865,8 +863,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     L[g] = L[g] * w0 + l1 * w1;
                     m[g] = mm;
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(x_free);
+                named_barrier(4, 2 * UM_SOFT);
                 const float nanv = __int_as_float(0x7fc00000);
                 const int d = my_lane;
 #pragma unroll
@@ -882,26 +879,10 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                         if (d == 0) p.part_ml[slot] = make_float2(m[g], any_bad ? nanv : L[g]);
                     }
                 }
-                // Count this partition in (the result is read one unit later) and merge the previous
-                // unit's partitions if its arrival was the last one.
-                named_barrier(gbar, UM_SOFT);  // the partial stores come before the arrival
-                if (gt == 0) {
-                    if (have_pend) *s_flag = resolve_arrival(p, pend, pend_old);
-                    if (u.nparts > 1) pend_old = arrive_partition(p, u);
-                }
-                if (have_pend) {
-                    named_barrier(gbar, UM_SOFT);
-                    if (*s_flag) merge_partitions<UM_D, 12>(p, pend, gt, UM_SOFT);
-                }
-                have_pend = u.nparts > 1;
-                pend = u;
             }
+            // both groups: count the partition in; the last partition's CTA merges them all
+            finish_partition<UM_D, 12>(p, u, tid, 2 * UM_SOFT, 4, s_flag);
             ++unit_no;
-        }
-        if (gi == 0 && have_pend) {  // the last unit's arrival
-            if (gt == 0) *s_flag = resolve_arrival(p, pend, pend_old);
-            named_barrier(gbar, UM_SOFT);
-            if (*s_flag) merge_partitions<UM_D, 12>(p, pend, gt, UM_SOFT);
         }
     }
 
@@ -942,8 +923,9 @@ bool kvb_umma_supported(int kv_type, int D, int page, int qg, int part_tokens) {
     if (kv_type != 1 && kv_type != 2) return false;
     if (D != 128) return false;
     if (!(page == 8 || page == 16 || page == 32 || page == 64 || page == 128 || page == 256)) return false;
-    // a partition's pages must fit the page table (part_tokens 0: the automatic size, <= 4096)
-    if (part_tokens > 0 && part_tokens / page + 2 > UM_PT) return false;
+    // a partition's pages and chunks must fit the page table and the per-chunk V scale bounds
+    // (part_tokens 0: the automatic size, at most 4096 tokens, 2048 for 8-token pages)
+    if (part_tokens > 0 && (part_tokens / page + 2 > UM_PT || part_tokens > (UM_UCH - 1) * UM_CHUNK)) return false;
     return qg >= 1 && qg <= 8;
 }
 

@@ -119,7 +119,8 @@ cudaError_t kvb_launch_decode_mma(const DecodeParams& p, int kv_type, int D, con
                                   const void* tmap_v, const LaunchInfo& li);
 
 // tcgen05 kernel: fp16/int8, head dim 128, page 8/16/32/64/128/256, qg <= 8, partitions of at most
-// about 526 pages (part_tokens 0: automatic); tensor maps with boxes of (128 bytes) x min(page, 128) rows.
+// about 262 pages and 8064 tokens (part_tokens 0: automatic); tensor maps with boxes of (128 bytes) x
+// min(page, 128) rows.
 bool kvb_umma_supported(int kv_type, int D, int page, int qg, int part_tokens);
 cudaError_t kvb_launch_decode_umma(const DecodeParams& p, int kv_type, int D, const void* tmap_k,
                                    const void* tmap_v, const LaunchInfo& li);
