@@ -358,8 +358,11 @@ int read_clear_flag(void* ws, cudaStream_t s, unsigned* flag) {
     *flag = h[0];
     if (!h[0]) return KVB_OK;
     KVB_CUDA(cudaMemsetAsync(ws, 0, sizeof h[0], s));
-    if (h[0] & (KVB_DEVERR_TIMEOUT | KVB_DEVERR_STATE))
+    if (h[0] & (KVB_DEVERR_TIMEOUT | KVB_DEVERR_STATE)) {
+        // a launch that gave up may have left the split-K counters and the work counters (words 2, 3)
         KVB_CUDA(cudaMemsetAsync(static_cast<char*>(ws) + 256, 0, sizeof(unsigned long long) * (size_t)h[1], s));
+        KVB_CUDA(cudaMemsetAsync(static_cast<char*>(ws) + 8, 0, 2 * sizeof(unsigned), s));
+    }
     KVB_CUDA(cudaStreamSynchronize(s));
     return KVB_OK;
 }

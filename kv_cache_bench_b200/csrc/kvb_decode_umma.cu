@@ -44,18 +44,22 @@ using namespace kvb_dev;
 constexpr int UM_CHUNK = 128;         // tokens per stage = MMA M for QK^T
 constexpr int UM_WARPS = 12;          // 8 softmax, producer, MMA (even chunks), MMA (odd chunks), TMEM owner
 constexpr int UM_THREADS = UM_WARPS * 32;
-constexpr int UM_PRODUCER = 8, UM_MMA0 = 9, UM_MMA1 = 10, UM_TMEM_WARP = 11;
+constexpr int UM_PRODUCER = 8, UM_MMA0 = 9, UM_MMA1 = 10, UM_TMEM_WARP = 11;  // warp 11 also prepares Qhat
 // Registers per thread after the split (the launch gives every thread 168: 65536 / 384, rounded
-// down to 8). The control warpgroup keeps 72, the softmax warpgroups get 216; the shares add up to at
+// down to 8). The control warpgroup keeps 88, the softmax warpgroups get 208; the shares add up to at
 // most the launch's total, or setmaxnreg.inc would wait forever.
-constexpr int UM_REGS_LAUNCH = 168, UM_REGS_CTRL = 72, UM_REGS_SOFT = 216;
+constexpr int UM_REGS_LAUNCH = 168, UM_REGS_CTRL = 88, UM_REGS_SOFT = 208;
 static_assert(2 * 128 * UM_REGS_SOFT + 128 * UM_REGS_CTRL <= UM_THREADS * UM_REGS_LAUNCH, "register split");
 constexpr int UM_SOFT = 128;          // threads of one softmax group
 constexpr int UM_D = 128;             // head dim
 constexpr int TILE = UM_CHUNK * 128;  // bytes of one [128 rows][128 B] swizzled tile
 constexpr int UM_PT = 264;            // page-table entries: pages of one partition, at most
 constexpr int UM_UCH = 64;            // chunks of one partition, at most (partitions <= 8064 tokens)
-constexpr int UM_GRED = 176;          // reduction floats per softmax group
+constexpr int UM_GRED = 144;          // reduction floats per softmax group
+constexpr int UM_TMEM_COLS = 256;     // tensor-memory columns of the CTA
+constexpr int UM_XCOL = 128;          // first column of the groups' unit shares
+constexpr int UM_QBATCH = 4;          // query heads the Qhat warp loads at once
+constexpr int UM_RQ = 8;              // entries of the unit ring (producer -> MMA issuers, Qhat warp)
 
 // ---- tcgen05 wrappers -----------------------------------------------------------------------------
 
@@ -112,6 +116,12 @@ __device__ __forceinline__ void tc_ld8(uint32_t taddr, uint32_t (&r)[8]) {
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                  : "r"(taddr));
 }
+__device__ __forceinline__ void tc_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor: 128-byte swizzle, 1024-byte atoms (8 rows of 128 B).
 // lbo / sbo in bytes (leading: stride between 128-byte column groups of an MN-major operand;
@@ -162,17 +172,6 @@ __device__ __forceinline__ float warp_max(float v) {
     return r;
 }
 
-// Splits a non-negative or signed integer |x| < 2^30 into four signed 8-bit limbs, high first.
-__device__ __forceinline__ void limbs4(int x, int8_t (&l)[4]) {
-#pragma unroll
-    for (int i = 3; i > 0; --i) {
-        const int lo = ((x + 128) & 255) - 128;
-        l[i] = (int8_t)lo;
-        x = (x - lo) >> 8;
-    }
-    l[0] = (int8_t)x;
-}
-
 template <int KVT>
 struct UCfg {
     static constexpr int NSUB = KVT == 1 ? 2 : 1;             // 128-byte column slices of a row
@@ -189,8 +188,9 @@ struct UCfg {
     static constexpr size_t VSMAX_OFF = BAD_OFF + STAGES * sizeof(int);
     static constexpr size_t BAR_OFF = kvb_align_up(VSMAX_OFF + (KVT == 2 ? 2 * UM_UCH : 0) * sizeof(float), 64);
     // full per (stage, chunk parity); empty per stage; q_full, q_free, s_full, s_free, p_full,
-    // o_full, pt_free x2
-    static constexpr int NBARS = 3 * STAGES + 2 * 7;
+    // o_full, pt_free x2; r_full, r_empty x UM_RQ
+    // unit ring: full and empty per entry
+    static constexpr int NBARS = 3 * STAGES + 2 * 7 + 2 * UM_RQ;
     static constexpr size_t RED_OFF = kvb_align_up(BAR_OFF + NBARS * sizeof(uint64_t), 16);
     static constexpr size_t WIN_OFF = RED_OFF + 2 * UM_GRED * sizeof(float);
     // page table: block ids [UM_PT]; int8: scales [2 buffers][UM_PT] for K and for V
@@ -200,7 +200,16 @@ struct UCfg {
     static constexpr size_t SCRATCH_OFF = kvb_align_up(LENS_OFF + sizeof(int) * KVB_PREFIX_MAX, 16);
     static constexpr size_t SCRATCH_FLOATS = 512;              // prefix scan
     static constexpr size_t MISC_OFF = kvb_align_up(SCRATCH_OFF + SCRATCH_FLOATS * sizeof(float), 64);
-    static constexpr size_t SMEM = MISC_OFF + 64 + 1024;
+    // Two unit slots (a unit's slot is its index among the CTA's units with tokens, mod 2): the unit
+    // and its per-head score factors (written by the Qhat warp); per group, the m, L and refusal flag
+    // of the group's share of the unit; the count of groups done with the unit; per group, the split-K
+    // arrival flag.
+    static constexpr size_t SLOT_UNIT_OFF = MISC_OFF + 64;                    // [2] Unit (64 B each)
+    static constexpr size_t SLOT_QS_OFF = SLOT_UNIT_OFF + 2 * 64;             // [2][8] float
+    static constexpr size_t XML_OFF = SLOT_QS_OFF + 2 * 8 * sizeof(float);    // [2 slots][2 groups][24] float
+    static constexpr size_t XCNT_OFF = XML_OFF + 2 * 2 * 24 * sizeof(float);  // [2] int count, [2] int flags
+    static constexpr size_t RING_OFF = XCNT_OFF + 16;                         // [UM_RQ] unit indices
+    static constexpr size_t SMEM = RING_OFF + UM_RQ * sizeof(int) + 1024;
 };
 
 static_assert(UCfg<1>::SMEM <= 227 * 1024 && UCfg<2>::SMEM <= 227 * 1024, "shared memory budget");
@@ -209,7 +218,7 @@ static_assert(UCfg<1>::MISC_OFF % 64 == 0 && UCfg<2>::MISC_OFF % 64 == 0, "align
 static_assert(UCfg<1>::Q_OFF % 1024 == 0 && UCfg<1>::P_OFF % 1024 == 0 && UCfg<2>::P_OFF % 1024 == 0,
               "swizzled operands need 1024-byte alignment");
 static_assert(UCfg<2>::SCRATCH_FLOATS >= UM_THREADS, "prefix scan scratch");
-static_assert(UCfg<1>::PBUF >= 8 * 128 * 4 && UCfg<2>::PBUF >= 8 * 128 * 4, "group 1's O rows fit its Phat buffer");
+static_assert(sizeof(Unit) <= 64, "unit slot");
 
 template <int KVT, int QGP>  // QGP: query heads per group, padded to 1, 2, 4 or 8
 __global__ void __launch_bounds__(UM_THREADS, 1)
@@ -238,13 +247,16 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     // parity wait never matches a phase two uses old.
     uint64_t* full = bars;
     uint64_t* empty = bars + 2 * STAGES;
-    uint64_t* q_full = bars + 3 * STAGES;  // [2] Qhat^T written (softmax group 0 -> MMA)
-    uint64_t* q_free = q_full + 2;         // [2] the unit's QK^T products done (both MMA warps -> softmax)
+    uint64_t* q_full = bars + 3 * STAGES;  // [2] Qhat^T and the unit slot written (Qhat warp -> MMA, softmax)
+    uint64_t* q_free = q_full + 2;         // [2] the unit's QK^T products and both groups' shares done
     uint64_t* s_full = q_full + 4;         // [2] S^T ready (MMA -> softmax), one per chunk parity
     uint64_t* s_free = q_full + 6;         // [2] S^T read (softmax -> MMA)
     uint64_t* p_full = q_full + 8;         // [2] Phat^T written, previous O^T folded (softmax -> MMA)
     uint64_t* o_full = q_full + 10;        // [2] O^T ready (MMA -> softmax)
     uint64_t* pt_free = q_full + 12;       // [2] int8 scale buffer read (softmax -> producer)
+    uint64_t* r_full = q_full + 14;        // [UM_RQ] unit ring entry written (producer -> consumers)
+    uint64_t* r_empty = r_full + UM_RQ;    // [UM_RQ] unit ring entry read (MMA issuers, Qhat warp)
+    int* s_ring = reinterpret_cast<int*>(smem + C::RING_OFF);
     float* red = reinterpret_cast<float*>(smem + C::RED_OFF);
     int* pt_blk = reinterpret_cast<int*>(smem + C::WIN_OFF);
     float* pt_ks = reinterpret_cast<float*>(pt_blk + UM_PT);  // int8 only: [2][UM_PT]
@@ -253,8 +265,11 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     int* s_lens = reinterpret_cast<int*>(smem + C::LENS_OFF);
     float* scratch = reinterpret_cast<float*>(smem + C::SCRATCH_OFF);
     volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::MISC_OFF);
-    int* s_flag = reinterpret_cast<int*>(smem + C::MISC_OFF + 8);
     uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF + 16);
+    auto slot_unit = [&](int qb) { return reinterpret_cast<Unit*>(smem + C::SLOT_UNIT_OFF + 64 * qb); };
+    float* s_qs = reinterpret_cast<float*>(smem + C::SLOT_QS_OFF);  // [slot][8] score factors
+    float* s_xml = reinterpret_cast<float*>(smem + C::XML_OFF);     // [slot][group][24]: m, L, refused
+    int* s_xcnt = reinterpret_cast<int*>(smem + C::XCNT_OFF);       // [slot] groups done, [group] flag
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // The unit enumeration starts with the sequence lengths and the block table: have them on the
@@ -278,19 +293,24 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         for (int s = 0; s < 2 * STAGES; ++s) mbar_init(&full[s], 1);
         for (int s = 0; s < STAGES; ++s) mbar_init(&empty[s], 1);
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&q_full[i], UM_SOFT / 32);
-            mbar_init(&q_free[i], 2);
+            mbar_init(&q_full[i], 1);
+            mbar_init(&q_free[i], 2 + 2 * UM_SOFT / 32);
             mbar_init(&s_full[i], 1);
             mbar_init(&s_free[i], UM_SOFT / 32);
             mbar_init(&p_full[i], UM_SOFT / 32);
             mbar_init(&o_full[i], 1);
             mbar_init(&pt_free[i], 2 * UM_SOFT / 32);
         }
+        for (int i = 0; i < UM_RQ; ++i) {
+            mbar_init(&r_full[i], 1);
+            mbar_init(&r_empty[i], 3);
+        }
         *s_abort = 0;
+        s_xcnt[0] = s_xcnt[1] = 0;
         fence_mbarrier_init();
     }
     if (warp == UM_TMEM_WARP) {
-        tc_alloc(s_tmem, 128);
+        tc_alloc(s_tmem, UM_TMEM_COLS);
         tc_relinquish();
     }
     if (tid == 0) {
@@ -301,7 +321,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
-    // tensor-memory columns: S^T buffers at 0 and 32, O^T buffers at 64 and 96 (one per chunk parity)
+    // tensor-memory columns: S^T buffers at 0 and 32, O^T buffers at 64 and 96 (one per chunk parity),
+    // the groups' shares of a unit at UM_XCOL + 8 * (2 * slot + group)
     pdl_wait();
     pdl_trigger();
     const int* prefix = nullptr;
@@ -322,7 +343,28 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     if (warp == UM_PRODUCER) {
         // ------------------------------------------------------------------ TMA producer
         const uint64_t policy = l2_evict_first_policy();
-        UnitCursor cur{&p, prefix, (long long)blockIdx.x, total, prefix ? s_lens : nullptr};
+        // Units: first unit blockIdx.x; with more units than CTAs, the rest one at a time from the
+        // workspace's work counter, the next index requested while the current unit streams (so an
+        // SM that runs slow takes fewer). Every unit is published to the MMA issuers and the Qhat
+        // warp through the unit ring, in order; -1 ends it.
+        unsigned* wc = work_counters(p);
+        const bool dyn = total > (long long)gridDim.x;
+        unsigned nxt = 0;
+        if (dyn && lane == 0) nxt = atomicAdd(&wc[0], 1u);
+        int wpos = 0;
+        auto publish = [&](int v) {
+            const int e = wpos % UM_RQ;
+            if (lane == 0 && wpos >= UM_RQ && !*s_abort &&
+                !mbar_wait_bounded(&r_empty[e], ((wpos / UM_RQ) - 1) & 1, s_abort))
+                give_up();
+            __syncwarp();
+            if (lane == 0) {
+                s_ring[e] = v;
+                mbar_arrive(&r_full[e]);
+            }
+            ++wpos;
+        };
+        long long idx = blockIdx.x;
         Unit u;
         int stage = 0;
         uint32_t phase = 0;
@@ -331,100 +373,122 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         const uint32_t box_bytes = 2u * NSUB * uint32_t(box_rows) * 128u;
         int unit_no = 0;
         int kp = 0;  // running chunk index
-        while (cur.advance(u)) {
-            if (u.nparts == 0) continue;
-            const int* bt = p.block_table + (size_t)u.b * p.max_blocks;
-            const int pg0 = u.t0 >> lp, pg1 = (u.t1 - 1) >> lp;  // the unit's pages (pg1 - pg0 < UM_PT)
-            const int npg = min(pg1 - pg0 + 1, UM_PT);  // the host keeps partitions within UM_PT pages
-            const int sb = unit_no & 1;
-            // Block ids of the unit; refused ones (outside [0, num_blocks)) become -2.
-            __syncwarp();
-            for (int i = lane; i < npg; i += 32) {
-                int blk = __ldg(bt + pg0 + i);
-                if (blk < 0 || (long long)blk >= p.num_blocks) blk = -2;
-                pt_blk[i] = blk;
-            }
-            __syncwarp();
-            const int c0 = u.t0 / UM_CHUNK, c1 = (u.t1 + UM_CHUNK - 1) / UM_CHUNK;
-            for (int c = c0; c < c1; ++c) {
-                const int tok0 = c * UM_CHUNK;
-                if (lane == 0 && !*s_abort && !mbar_wait_bounded(&empty[stage], phase ^ 1u, s_abort)) give_up();
+        for (;;) {
+            const bool real = idx < total && unit_at(p, prefix, prefix ? s_lens : nullptr, idx, u);
+            // A unit is published once its first chunk's loads are on their way (a tokenless one at once).
+            if (real && u.nparts == 0) publish(int(idx));
+            if (real && u.nparts > 0) {
+                const int* bt = p.block_table + (size_t)u.b * p.max_blocks;
+                const int pg0 = u.t0 >> lp, pg1 = (u.t1 - 1) >> lp;  // the unit's pages (pg1 - pg0 < UM_PT)
+                const int npg = min(pg1 - pg0 + 1, UM_PT);  // the host keeps partitions within UM_PT pages
+                const int sb = unit_no & 1;
+                // Block ids of the unit; refused ones (outside [0, num_blocks)) become -2.
                 __syncwarp();
-                // lane j < nbox owns box j (one page, or 128 rows of a larger page)
-                int blk = -1;
-                bool mine = false, refused = false;
-                if (lane < nbox) {
-                    const int i = (tok0 + lane * box_rows) >> lp;
-                    if (i >= pg0 && i <= pg1) {
-                        blk = pt_blk[i - pg0];
-                        refused = blk < 0;
-                        mine = !refused;
-                    }
-                }
-                const unsigned owned = __ballot_sync(0xffffffffu, mine);
-                const bool bad = __any_sync(0xffffffffu, refused);
-                const uint32_t bytes = uint32_t(__popc(owned)) * box_bytes;
-                const bool abort_now = *s_abort;
-                // The unit's first int8 chunk also publishes the unit's scales, fetched after the tile
-                // loads are on their way: its stage completes on the bytes plus the arrival below.
-                const bool scales_due = KVT == 2 && c == c0;
-                uint64_t* fb = &full[kp % (2 * STAGES)];
-                if (lane == 0) {
-                    stage_bad[stage] = bad;
-                    if (bad) raise_error(p.error_flag, KVB_DEVERR_BLOCK);
-                    if (scales_due) {
-                        if (!abort_now && bytes) mbar_expect_tx(fb, bytes);
-                    } else if (abort_now || bytes == 0) {
-                        mbar_arrive(fb);
-                    } else {
-                        mbar_arrive_expect_tx(fb, bytes);
-                    }
+                for (int i = lane; i < npg; i += 32) {
+                    int blk = __ldg(bt + pg0 + i);
+                    if (blk < 0 || (long long)blk >= p.num_blocks) blk = -2;
+                    pt_blk[i] = blk;
                 }
                 __syncwarp();
-                if (mine && !abort_now) {
-                    const int tok = tok0 + lane * box_rows;
-                    const int y = (blk * p.Hkv + u.kvh) * p.page + (tok & (p.page - 1));
-                    uint8_t* st = smem + stage * C::STAGE;
+                const int c0 = u.t0 / UM_CHUNK, c1 = (u.t1 + UM_CHUNK - 1) / UM_CHUNK;
+                for (int c = c0; c < c1; ++c) {
+                    const int tok0 = c * UM_CHUNK;
+                    if (lane == 0 && !*s_abort && !mbar_wait_bounded(&empty[stage], phase ^ 1u, s_abort)) give_up();
+                    __syncwarp();
+                    // lane j < nbox owns box j (one page, or 128 rows of a larger page)
+                    int blk = -1;
+                    bool mine = false, refused = false;
+                    if (lane < nbox) {
+                        const int i = (tok0 + lane * box_rows) >> lp;
+                        if (i >= pg0 && i <= pg1) {
+                            blk = pt_blk[i - pg0];
+                            refused = blk < 0;
+                            mine = !refused;
+                        }
+                    }
+                    const unsigned owned = __ballot_sync(0xffffffffu, mine);
+                    const bool bad = __any_sync(0xffffffffu, refused);
+                    const uint32_t bytes = uint32_t(__popc(owned)) * box_bytes;
+                    const bool abort_now = *s_abort;
+                    // The unit's first int8 chunk also publishes the unit's scales, fetched after the tile
+                    // loads are on their way: its stage completes on the bytes plus the arrival below.
+                    const bool scales_due = KVT == 2 && c == c0;
+                    uint64_t* fb = &full[kp % (2 * STAGES)];
+                    if (lane == 0) {
+                        stage_bad[stage] = bad;
+                        if (bad) raise_error(p.error_flag, KVB_DEVERR_BLOCK);
+                        if (scales_due) {
+                            if (!abort_now && bytes) mbar_expect_tx(fb, bytes);
+                        } else if (abort_now || bytes == 0) {
+                            mbar_arrive(fb);
+                        } else {
+                            mbar_arrive_expect_tx(fb, bytes);
+                        }
+                    }
+                    __syncwarp();
+                    if (mine && !abort_now) {
+                        const int tok = tok0 + lane * box_rows;
+                        const int y = (blk * p.Hkv + u.kvh) * p.page + (tok & (p.page - 1));
+                        uint8_t* st = smem + stage * C::STAGE;
 #pragma unroll
-                    for (int s = 0; s < NSUB; ++s) {
-                        const int x = s * (KVT == 1 ? 64 : 128);
-                        const uint32_t off = s * TILE + lane * box_rows * 128;
-                        tma_load_2d(st + off, &tmk, fb, x, y, policy);
-                        tma_load_2d(st + NSUB * TILE + off, &tmv, fb, x, y, policy);
+                        for (int s = 0; s < NSUB; ++s) {
+                            const int x = s * (KVT == 1 ? 64 : 128);
+                            const uint32_t off = s * TILE + lane * box_rows * 128;
+                            tma_load_2d(st + off, &tmk, fb, x, y, policy);
+                            tma_load_2d(st + NSUB * TILE + off, &tmv, fb, x, y, policy);
+                        }
                     }
-                }
-                if (scales_due) {
-                    // the softmax warps are done with this scale buffer's previous unit
-                    if (lane == 0 && unit_no >= 2 && !*s_abort &&
-                        !mbar_wait_bounded(&pt_free[sb], ((unit_no - 2) >> 1) & 1, s_abort))
-                        give_up();
+                    if (c == c0) publish(int(idx));
+                    if (scales_due) {
+                        // the softmax warps are done with this scale buffer's previous unit
+                        if (lane == 0 && unit_no >= 2 && !*s_abort &&
+                            !mbar_wait_bounded(&pt_free[sb], ((unit_no - 2) >> 1) & 1, s_abort))
+                            give_up();
+                        __syncwarp();
+                        float* ks_b = pt_ks + sb * UM_PT;
+                        float* vs_b = pt_vs + sb * UM_PT;
+                        for (int i = lane; i < npg; i += 32) {
+                            const int b2 = pt_blk[i];
+                            ks_b[i] = b2 >= 0 ? __ldg(p.k_scale + (size_t)b2 * p.Hkv + u.kvh) : 0.f;
+                            vs_b[i] = b2 >= 0 ? __ldg(p.v_scale + (size_t)b2 * p.Hkv + u.kvh) : 0.f;
+                        }
+                        __syncwarp();
+                        // the largest V scale of each of the unit's chunks (an int8 probability scale bound)
+                        float* um = unit_vsmax + sb * UM_UCH;
+                        for (int j = lane; j < c1 - c0 && j < UM_UCH; j += 32) {
+                            const int a = max(((c0 + j) * UM_CHUNK) >> lp, pg0) - pg0;
+                            const int z = min((((c0 + j + 1) * UM_CHUNK - 1) >> lp), pg1) - pg0;
+                            float vmax = 0.f;
+                            for (int i = a; i <= z; ++i) vmax = fmaxf(vmax, vs_b[i]);
+                            um[j] = vmax;
+                        }
+                        __syncwarp();  // every lane's scale writes happen before the arrive
+                        if (lane == 0) mbar_arrive(fb);
+                    }
                     __syncwarp();
-                    float* ks_b = pt_ks + sb * UM_PT;
-                    float* vs_b = pt_vs + sb * UM_PT;
-                    for (int i = lane; i < npg; i += 32) {
-                        const int b2 = pt_blk[i];
-                        ks_b[i] = b2 >= 0 ? __ldg(p.k_scale + (size_t)b2 * p.Hkv + u.kvh) : 0.f;
-                        vs_b[i] = b2 >= 0 ? __ldg(p.v_scale + (size_t)b2 * p.Hkv + u.kvh) : 0.f;
-                    }
-                    __syncwarp();
-                    // the largest V scale of each of the unit's chunks (an int8 probability scale bound)
-                    float* um = unit_vsmax + sb * UM_UCH;
-                    for (int j = lane; j < c1 - c0 && j < UM_UCH; j += 32) {
-                        const int a = max(((c0 + j) * UM_CHUNK) >> lp, pg0) - pg0;
-                        const int z = min((((c0 + j + 1) * UM_CHUNK - 1) >> lp), pg1) - pg0;
-                        float vmax = 0.f;
-                        for (int i = a; i <= z; ++i) vmax = fmaxf(vmax, vs_b[i]);
-                        um[j] = vmax;
-                    }
-                    __syncwarp();  // every lane's scale writes happen before the arrive
-                    if (lane == 0) mbar_arrive(fb);
+                    ++kp;
+                    if (++stage == STAGES) stage = 0, phase ^= 1u;
                 }
-                __syncwarp();
-                ++kp;
-                if (++stage == STAGES) stage = 0, phase ^= 1u;
+                ++unit_no;
             }
-            ++unit_no;
+            // the next unit
+            if (!dyn) break;
+            long long nidx = 0;
+            if (lane == 0) {
+                nidx = (long long)gridDim.x + nxt;
+                if (nidx < total) {
+                    nxt = atomicAdd(&wc[0], 1u);
+                } else if (atomicAdd(&wc[1], 1u) == gridDim.x - 1) {
+                    // every CTA has found the units exhausted: leave the counters zero for the next launch
+                    atomicExch(&wc[0], 0u);
+                    atomicExch(&wc[1], 0u);
+                }
+            }
+            nidx = __shfl_sync(0xffffffffu, nidx, 0);
+            if (nidx >= total) break;
+            idx = nidx;
         }
+        publish(-1);
     } else if (warp == UM_MMA0 || warp == UM_MMA1) {
         // ------------------------------------------------------------------ MMA issuers
         // Warp 9 issues the products of the even chunks (running index), warp 10 those of the odd
@@ -443,8 +507,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             constexpr int KQK = KVT == 1 ? 16 : 32;  // contraction elements per instruction
             const uint32_t s_tm = tmem + 32 * par, o_tm = tmem + 64 + 32 * par;
             const uint32_t pb = sbase + uint32_t(C::P_OFF) + par * C::PBUF;
-            UnitCursor cur{&p, prefix, (long long)blockIdx.x, total, prefix ? s_lens : nullptr};
             Unit u;
+            int rpos = 0;  // next unit ring entry
             bool have_unit = false, units_done = false, need_q = false;
             int unit_no = -1, qb = 0;
             int qk = 0, k_end = 0;         // next own chunk for S^T; end of the current unit's chunks
@@ -455,11 +519,17 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             while (!*s_abort) {
                 bool progress = false;
                 while (!have_unit && !units_done) {
-                    if (!cur.advance(u)) {
+                    // the next unit from the ring, once published (units without tokens are skipped)
+                    const int e = rpos % UM_RQ;
+                    if (!mbar_test(&r_full[e], uint32_t(rpos / UM_RQ) & 1)) break;
+                    const int v = s_ring[e];
+                    mbar_arrive(&r_empty[e]);
+                    ++rpos;
+                    if (v < 0) {
                         units_done = true;
                         break;
                     }
-                    if (u.nparts == 0) continue;
+                    if (!unit_at(p, prefix, prefix ? s_lens : nullptr, v, u) || u.nparts == 0) continue;
                     ++unit_no;
                     qb = unit_no & 1;
                     const int k_base = k_end;
@@ -548,6 +618,132 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 }
             }
         }
+    } else if (warp == UM_TMEM_WARP) {
+        // ------------------------------------------------------------------ Qhat preparation
+        // Runs ahead of the softmax groups. For the n-th unit with tokens (slot n & 1) it waits until
+        // the slot's previous unit is done (its QK^T products and both groups' shares), writes Qhat^T
+        // (row (head g, part r) = fp16 half r of q, or int8 limb r) and the per-head factors that turn
+        // the combined MMA result into a log2 score, publishes the unit and arrives on q_full. A unit
+        // with nparts < 0 ends the groups' loop. Units without tokens get their outputs here.
+        Unit u;
+        const bool q16 = (reinterpret_cast<uintptr_t>(p.q) & 15) == 0;
+        int rpos = 0;  // next unit ring entry
+        auto ring_next = [&]() {  // the next published unit index, -1 at the end (every lane)
+            const int e = rpos % UM_RQ;
+            int v = -1;
+            if (lane == 0) {
+                if (!*s_abort && !mbar_wait_bounded(&r_full[e], uint32_t(rpos / UM_RQ) & 1, s_abort)) give_up();
+                if (!*s_abort) v = s_ring[e];
+                mbar_arrive(&r_empty[e]);
+            }
+            ++rpos;
+            return __shfl_sync(0xffffffffu, v, 0);
+        };
+        // The producer's first entry is unit blockIdx.x whenever that is a unit: it is taken without
+        // waiting for the ring (which is on the first unit's critical path), and its entry is
+        // consumed with the next one.
+        bool first = blockIdx.x < total && unit_at(p, prefix, prefix ? s_lens : nullptr, blockIdx.x, u);
+        bool first_entry = first;
+        for (int n = 0;; ++n) {
+            // the next unit with tokens; units without tokens get their outputs here
+            bool more = false;
+            for (;;) {
+                if (first) {
+                    first = false;
+                } else {
+                    if (first_entry) {
+                        first_entry = false;
+                        ring_next();
+                    }
+                    const int v = ring_next();
+                    if (v < 0 || !unit_at(p, prefix, prefix ? s_lens : nullptr, v, u)) break;
+                }
+                if (u.nparts > 0) {
+                    more = true;
+                    break;
+                }
+                store_tokenless_unit<UM_D>(p, u, lane, 32);
+            }
+            const int qb = n & 1;
+            if (n >= 2) {
+                if (lane == 0 && !*s_abort && !mbar_wait_bounded(&q_free[qb], ((n - 2) >> 1) & 1, s_abort))
+                    give_up();
+                __syncwarp();
+            }
+            if (!more) {
+                if (lane == 0) {
+                    slot_unit(qb)->nparts = -1;
+                    mbar_arrive(&q_full[qb]);
+                }
+                break;
+            }
+            uint8_t* qbuf = smem + C::Q_OFF + qb * C::QBUF;
+            const int d0 = 4 * lane;  // this lane's four head-dim elements
+            const float* qrow = p.q + ((size_t)u.b * p.H + u.h0) * UM_D + d0;
+            constexpr int QB = QGP < UM_QBATCH ? QGP : UM_QBATCH;
+#pragma unroll
+            for (int g0 = 0; g0 < QGP; g0 += QB) {
+                float4 xs[QB];
+#pragma unroll
+                for (int j = 0; j < QB; ++j) {
+                    const float* row = qrow + (g0 + j) * UM_D;
+                    xs[j] = g0 + j >= u.nh ? make_float4(0.f, 0.f, 0.f, 0.f)
+                            : q16          ? __ldg(reinterpret_cast<const float4*>(row))
+                                           : make_float4(__ldg(row), __ldg(row + 1), __ldg(row + 2), __ldg(row + 3));
+                }
+#pragma unroll
+                for (int j = 0; j < QB; ++j) {
+                    const int g = g0 + j;
+                    const float x[4] = {xs[j].x * p.q_scale, xs[j].y * p.q_scale, xs[j].z * p.q_scale,
+                                        xs[j].w * p.q_scale};
+                    const float amax = warp_max(fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3]))));
+                    int e = 0;
+                    frexpf(amax, &e);
+                    const bool live = amax > 0.f && amax < 3.0e38f;
+                    if constexpr (KVT == 1) {
+                        // x * 2^(14 - e) in [-2^14, 2^14): hi + lo halves
+                        const float pre = live ? ldexpf(1.f, 14 - e) : 1.f;
+                        if (lane == 0) s_qs[qb * 8 + g] = 1.f / pre;
+                        uint32_t hi[2], lo[2];
+#pragma unroll
+                        for (int t = 0; t < 2; ++t) {
+                            const float a = x[2 * t] * pre, b = x[2 * t + 1] * pre;
+                            const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+                            const __half la = __float2half_rn(a - __half2float(ha));
+                            const __half lb = __float2half_rn(b - __half2float(hb));
+                            hi[t] = uint32_t(__half_as_ushort(ha)) | uint32_t(__half_as_ushort(hb)) << 16;
+                            lo[t] = uint32_t(__half_as_ushort(la)) | uint32_t(__half_as_ushort(lb)) << 16;
+                        }
+                        const int col = (d0 % 64) * 2, sb = d0 / 64;
+                        *reinterpret_cast<uint2*>(qbuf + sb * (C::NMAX * 128) + swz_off(g, col)) = make_uint2(hi[0], hi[1]);
+                        *reinterpret_cast<uint2*>(qbuf + sb * (C::NMAX * 128) + swz_off(QGP + g, col)) =
+                            make_uint2(lo[0], lo[1]);
+                    } else {
+                        // integer x * 2^(30 - e) with |.| < 2^30, as four signed limbs
+                        const float pre = live ? ldexpf(1.f, 30 - e) : 1.f;
+                        if (lane == 0) s_qs[qb * 8 + g] = 1.f / pre;
+                        // Limbs of element i packed in w[i] (byte 3 = limb 0 .. byte 0 = limb 3): adding 128
+                        // to each of the three lower signed digits turns them into plain bytes (no
+                        // carries), so the digits are the bytes of x + 0x808080 with those three flipped
+                        // back by 0x80; the top byte is the signed top digit (|x| < 2^30).
+                        uint32_t w[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) w[i] = uint32_t(__float2int_rn(x[i] * pre) + 0x808080) ^ 0x808080u;
+                        // 4 x 4 byte transpose: row r gets limb r of the four elements, element i in byte i
+                        const uint32_t a01 = __byte_perm(w[0], w[1], 0x5140), b01 = __byte_perm(w[0], w[1], 0x7362);
+                        const uint32_t a23 = __byte_perm(w[2], w[3], 0x5140), b23 = __byte_perm(w[2], w[3], 0x7362);
+                        const uint32_t rows[4] = {__byte_perm(b01, b23, 0x7632), __byte_perm(b01, b23, 0x5410),
+                                                  __byte_perm(a01, a23, 0x7632), __byte_perm(a01, a23, 0x5410)};
+#pragma unroll
+                        for (int r = 0; r < 4; ++r) *reinterpret_cast<uint32_t*>(qbuf + swz_off(g * 4 + r, d0)) = rows[r];
+                    }
+                }
+            }
+            if (lane == 0) *slot_unit(qb) = u;
+            fence_proxy_async_smem();  // generic writes of Qhat^T before the MMA reads them
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&q_full[qb]);
+        }
     } else if (warp < 8) {
         // ------------------------------------------------------------------ softmax / accumulation
         reg_alloc<UM_REGS_SOFT>();
@@ -561,77 +757,20 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         // this warp's tensor-memory lane quarter is fixed by warp % 4
         const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;
         const int my_lane = (warp & 3) * 32 + lane;  // token in S^T, head dim in O^T
-        // [0,32) q absmax; [32,112) chunk max x2 ([value][warp]: 8 heads, V scale); [112,144) sums;
-        // group 1: [144,161) state handed to group 0 at the unit's end
+        // [32,112) chunk max x2 ([value][warp]: 8 heads, V scale); [112,144) sums
         float* gred = red + gi * UM_GRED;
-        UnitCursor cur{&p, prefix, (long long)blockIdx.x, total, prefix ? s_lens : nullptr};
-        Unit u;
         int stage = 0;
         int k = 0;  // running chunk index
-        int unit_no = 0;
-        while (cur.advance(u)) {
-            if (u.nparts == 0) {
-                if (gi == 0) store_tokenless_unit<UM_D>(p, u, gt, UM_SOFT);
-                continue;
-            }
+        for (int unit_no = 0;; ++unit_no) {
+            // ---- the unit and its score factors, from the slot the Qhat warp filled
             const int qb = unit_no & 1;
-            // ---- Qhat^T for this unit (written by group 0): row (head g, part r) = fp16 half r of q,
-            // or int8 limb r. Both groups compute the per-head factors.
-            if (gi == 0 && unit_no >= 2) {
-                if (!*s_abort && !mbar_wait_bounded(&q_free[qb], ((unit_no - 2) >> 1) & 1, s_abort)) give_up();
-            }
+            if (!*s_abort && !mbar_wait_bounded(&q_full[qb], (unit_no >> 1) & 1, s_abort)) give_up();
+            const Unit u = *slot_unit(qb);
+            // one decision for the whole group (after an abort the slot may never have been written)
+            if (named_barrier_or(gbar, UM_SOFT, *s_abort || u.nparts < 0)) break;
             float qscale[QGP];  // per head: the factor that turns the combined MMA result into a log2 score
-            {
-                const int d = my_lane;  // one head-dim element per thread
-                float x[QGP], amax[QGP];
 #pragma unroll
-                for (int g = 0; g < QGP; ++g) {
-                    x[g] = g < u.nh ? __ldg(p.q + ((size_t)u.b * p.H + u.h0 + g) * UM_D + d) * p.q_scale : 0.f;
-                    amax[g] = warp_max(fabsf(x[g]));
-                }
-                if (lane == 0) {
-#pragma unroll
-                    for (int g = 0; g < QGP; ++g) gred[g * 4 + sw] = amax[g];
-                }
-                named_barrier(gbar, UM_SOFT);
-#pragma unroll
-                for (int g = 0; g < QGP; ++g) amax[g] = max4(reinterpret_cast<const float4*>(gred)[g]);
-                uint8_t* qbuf = smem + C::Q_OFF + qb * C::QBUF;
-#pragma unroll
-                for (int g = 0; g < QGP; ++g) {
-                    int e = 0;
-                    frexpf(amax[g], &e);
-                    const bool live = amax[g] > 0.f && amax[g] < 3.0e38f;
-                    if constexpr (KVT == 1) {
-                        // x * 2^(14 - e) in [-2^14, 2^14): hi + lo halves
-                        const float pre = live ? ldexpf(1.f, 14 - e) : 1.f;
-                        qscale[g] = 1.f / pre;
-                        if (gi == 0) {
-                            const float xs = x[g] * pre;
-                            const __half hi = __float2half_rn(xs);
-                            const __half lo = __float2half_rn(xs - __half2float(hi));
-                            const int col = (d % 64) * 2, sb = d / 64;
-                            *reinterpret_cast<__half*>(qbuf + sb * (C::NMAX * 128) + swz_off(g, col)) = hi;
-                            *reinterpret_cast<__half*>(qbuf + sb * (C::NMAX * 128) + swz_off(QGP + g, col)) = lo;
-                        }
-                    } else {
-                        // integer x * 2^(30 - e) with |.| < 2^30, as four signed limbs
-                        const float pre = live ? ldexpf(1.f, 30 - e) : 1.f;
-                        qscale[g] = 1.f / pre;
-                        if (gi == 0) {
-                            int8_t l[4];
-                            limbs4(__float2int_rn(x[g] * pre), l);
-#pragma unroll
-                            for (int r = 0; r < 4; ++r) *reinterpret_cast<int8_t*>(qbuf + swz_off(g * 4 + r, d)) = l[r];
-                        }
-                    }
-                }
-            }
-            if (gi == 0) {
-                fence_proxy_async_smem();  // generic writes of Qhat^T before the MMA reads them
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&q_full[qb]);
-            }
+            for (int g = 0; g < QGP; ++g) qscale[g] = s_qs[qb * 8 + g];
 
             // ---- chunks
             float m[QGP], lsum[QGP], o[QGP];  // running max (group-uniform), this thread's sum share, O row
@@ -818,7 +957,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 if (lane == 0) mbar_arrive(&pt_free[qb]);  // the unit's scales are no longer read
             }
             if (have_prev) fold_prev(k_own, false);
-            // ---- unit epilogue: group sums across its 128 tokens, then the two groups merge
+            // ---- unit end: the group's sums over its 128 tokens
             float L[QGP];
 #pragma unroll
             for (int g = 0; g < QGP; ++g) {
@@ -837,33 +976,51 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 const float4 l4 = reinterpret_cast<const float4*>(gred + 112)[g];
                 L[g] = (l4.x + l4.y) + (l4.z + l4.w);
             }
-            // Group 1 hands its state over in its own Phat buffer (its last PV product is done: the
-            // fold above waited for it) and in the spare end of its reduction floats.
-            float* xo = reinterpret_cast<float*>(smem + C::P_OFF + C::PBUF);  // [QGP][128] O rows
-            float* xml = red + UM_GRED + 144;                               // [QGP] m, [QGP] L, [1] bad
-            if (gi == 1) {
+            // Each group leaves its share of the unit (O rows in tensor memory; m, L and the refusal
+            // flag in shared memory) and counts itself in. The second group to finish merges the two
+            // and stores the unit's result; the first goes on to its next unit without waiting.
+            {
+                uint32_t w[8];
 #pragma unroll
-                for (int g = 0; g < QGP; ++g) xo[g * UM_D + my_lane] = o[g];
-                if (gt == 0) {
+                for (int j = 0; j < 8; ++j) w[j] = j < QGP ? __float_as_uint(o[j]) : 0u;
+                tc_st8(tmem + lane_base + uint32_t(UM_XCOL + 8 * (2 * qb + gi)), w);
+            }
+            float* xml = s_xml + (2 * qb + gi) * 24;
+            if (gt == 0) {
 #pragma unroll
-                    for (int g = 0; g < QGP; ++g) xml[g] = m[g], xml[QGP + g] = L[g];
-                    xml[2 * QGP] = grp_bad ? 1.f : 0.f;
-                }
-                named_barrier(4, 2 * UM_SOFT);  // group 1's state is written
-                named_barrier(4, 2 * UM_SOFT);  // group 0 has read it
-            } else {
-                named_barrier(4, 2 * UM_SOFT);
-                const bool any_bad = grp_bad || xml[2 * QGP] != 0.f;
+                for (int g = 0; g < QGP; ++g) xml[g] = m[g], xml[8 + g] = L[g];
+                xml[16] = grp_bad ? 1.f : 0.f;
+            }
+            tc_wait_st();
+            tc_fence_before();
+            named_barrier(gbar, UM_SOFT);  // the group's share is written
+            if (gt == 0) {
+                __threadfence_block();
+                s_xcnt[2 + gi] = atomicAdd(&s_xcnt[qb], 1);
+                __threadfence_block();
+            }
+            named_barrier(gbar, UM_SOFT);
+            if (s_xcnt[2 + gi] == 1) {
+                tc_fence_after();
+                uint32_t w[8];
+                tc_ld8(tmem + lane_base + uint32_t(UM_XCOL + 8 * (2 * qb + (gi ^ 1))), w);
+                const float* yml = s_xml + (2 * qb + (gi ^ 1)) * 24;
+                const bool any_bad = grp_bad || yml[16] != 0.f;
+                tc_wait_ld();
+                // group 0's share first whichever group merges, so the result does not depend on timing
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) {
-                    const float m1 = xml[g], l1 = xml[QGP + g];
-                    const float mm = fmaxf(m[g], m1);
-                    const float w0 = exp2f(m[g] - mm), w1 = exp2f(m1 - mm);
-                    o[g] = o[g] * w0 + xo[g * UM_D + my_lane] * w1;
-                    L[g] = L[g] * w0 + l1 * w1;
+                    const float oy = __uint_as_float(w[g]), my = yml[g], ly = yml[8 + g];
+                    const float o0 = gi == 0 ? o[g] : oy, o1 = gi == 0 ? oy : o[g];
+                    const float m0 = gi == 0 ? m[g] : my, m1 = gi == 0 ? my : m[g];
+                    const float l0 = gi == 0 ? L[g] : ly, l1 = gi == 0 ? ly : L[g];
+                    const float mm = fmaxf(m0, m1);
+                    const float w0 = exp2f(m0 - mm), w1 = exp2f(m1 - mm);
+                    o[g] = o0 * w0 + o1 * w1;
+                    L[g] = l0 * w0 + l1 * w1;
                     m[g] = mm;
                 }
-                named_barrier(4, 2 * UM_SOFT);
+                if (gt == 0) s_xcnt[qb] = 0;  // both groups counted: the slot's next unit counts from zero
                 const float nanv = __int_as_float(0x7fc00000);
                 const int d = my_lane;
 #pragma unroll
@@ -879,10 +1036,13 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                         if (d == 0) p.part_ml[slot] = make_float2(m[g], any_bad ? nanv : L[g]);
                     }
                 }
+                // count the partition in; the last partition's CTA merges them all
+                finish_partition<UM_D, 20>(p, u, gt, UM_SOFT, gbar, &s_xcnt[2 + gi]);
             }
-            // both groups: count the partition in; the last partition's CTA merges them all
-            finish_partition<UM_D, 12>(p, u, tid, 2 * UM_SOFT, 4, s_flag);
-            ++unit_no;
+            // this warp is done with the unit's slot (its factors, both shares)
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&q_free[qb]);
         }
     }
 
@@ -890,7 +1050,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == UM_TMEM_WARP) tc_dealloc(tmem, 128);
+    if (warp == UM_TMEM_WARP) tc_dealloc(tmem, UM_TMEM_COLS);
 }
 
 template <int KVT, int QGP>

@@ -276,6 +276,38 @@ __device__ __forceinline__ Unit make_unit(const DecodeParams& p, int b, int hg, 
 // units are packed through a prefix sum over sequences kept in shared memory (`prefix`, B + 1
 // ints, filled by build_unit_prefix); otherwise every (b, hg, part < max_parts) slot is visited and
 // slots past a sequence's partitions are skipped.
+// The unit with index idx (0 <= idx < unit_total): false for a dense-mode slot past its sequence's
+// partitions, which is no unit at all. `prefix` and `lens` as in UnitCursor.
+__device__ __forceinline__ bool unit_at(const DecodeParams& P, const int* prefix, const int* lens, long long idx,
+                                        Unit& u) {
+    if (prefix) {
+        // largest b with prefix[b] <= idx
+        int lo = 0, hi = P.B - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (prefix[mid] <= idx) lo = mid;
+            else hi = mid - 1;
+        }
+        const int b = lo;
+        const int len = lens ? lens[b] : __ldg(P.seq_lens + b);
+        bool bad;
+        const int per = max(1, seq_partitions(P, len, &bad));
+        const int local = int(idx - prefix[b]);
+        u = make_unit(P, b, local / per, local % per, len);
+        return true;
+    }
+    const long long per_seq = (long long)P.nhg * P.max_parts;
+    const int b = int(idx / per_seq);
+    const int rem = int(idx % per_seq);
+    const int hg = rem / P.max_parts, part = rem % P.max_parts;
+    const int len = __ldg(P.seq_lens + b);
+    bool bad;
+    const int np = seq_partitions(P, len, &bad);
+    if (part >= max(1, np)) return false;
+    u = make_unit(P, b, hg, part, len);
+    return true;
+}
+
 struct UnitCursor {
     const DecodeParams* p;
     const int* prefix;  // nullptr: dense enumeration
@@ -283,36 +315,10 @@ struct UnitCursor {
     const int* lens = nullptr;  // sequence lengths cached in shared memory (prefix mode), or nullptr
 
     __device__ __forceinline__ bool advance(Unit& u) {
-        const DecodeParams& P = *p;
         while (next < total) {
             const long long idx = next;
             next += gridDim.x;
-            if (prefix) {
-                // largest b with prefix[b] <= idx
-                int lo = 0, hi = P.B - 1;
-                while (lo < hi) {
-                    const int mid = (lo + hi + 1) >> 1;
-                    if (prefix[mid] <= idx) lo = mid;
-                    else hi = mid - 1;
-                }
-                const int b = lo;
-                const int len = lens ? lens[b] : __ldg(P.seq_lens + b);
-                bool bad;
-                const int per = max(1, seq_partitions(P, len, &bad));
-                const int local = int(idx - prefix[b]);
-                u = make_unit(P, b, local / per, local % per, len);
-                return true;
-            }
-            const long long per_seq = (long long)P.nhg * P.max_parts;
-            const int b = int(idx / per_seq);
-            const int rem = int(idx % per_seq);
-            const int hg = rem / P.max_parts, part = rem % P.max_parts;
-            const int len = __ldg(P.seq_lens + b);
-            bool bad;
-            const int np = seq_partitions(P, len, &bad);
-            if (part >= max(1, np)) continue;
-            u = make_unit(P, b, hg, part, len);
-            return true;
+            if (unit_at(*p, prefix, lens, idx, u)) return true;
         }
         return false;
     }
@@ -360,6 +366,10 @@ __device__ __forceinline__ void build_unit_prefix(const DecodeParams& p, int* pr
 __device__ __forceinline__ long long unit_total(const DecodeParams& p, const int* prefix) {
     return prefix ? (long long)prefix[p.B] : (long long)p.B * p.nhg * p.max_parts;
 }
+
+// Workspace words 2 and 3: the units handed out beyond the first grid-wide round, and the CTAs that
+// found none left (kernels that take units dynamically; the last such CTA zeroes both).
+__device__ __forceinline__ unsigned* work_counters(const DecodeParams& p) { return p.error_flag + 2; }
 
 // Records in workspace word 1 how many arrival counters this launch uses (see KVB_DEVERR_STATE).
 __device__ __forceinline__ void note_counter_count(const DecodeParams& p) {

@@ -20,7 +20,9 @@
 // launch id nor a stored partial result takes).
 #define KVB_CTR_CLEAN 0x7fffffffu
 // Word 1 of the workspace holds the number of arrival counters the last launch used, so that the
-// flag reader can zero them after a TIMEOUT or STATE error (words 0 and 1 are the header).
+// flag reader can zero them after a TIMEOUT or STATE error. Words 2 and 3 count the units the
+// tcgen05 kernel handed out dynamically and the CTAs that found none left; a launch leaves both 0
+// (the flag reader zeroes them after a TIMEOUT or STATE error too). Words 0-3 are the header.
 
 // Sequences up to this batch size are enumerated through a prefix sum in shared memory.
 #define KVB_PREFIX_MAX 256
