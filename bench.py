@@ -472,8 +472,10 @@ def main():
 
     def c_args(i):
         k, v, ks, vs = s.pools[i]
+        # nothing in the step loop writes the lengths or the block table: the kernel may read them
+        # while the previous step finishes
         return dec.args(s.q, k, v, s.table, s.seq_lens, s.max_len, out=s.out, k_scale=ks, v_scale=vs,
-                        part_tokens=part, kernel=kernel)
+                        part_tokens=part, kernel=kernel, tables_ready=True)
 
     cargs = [c_args(i) for i in range(copies)]
     need = kvb.paged_workspace_bytes(cargs[0])
@@ -648,8 +650,9 @@ def measure_e2e(torch, dist, s, dec, part, kernel, stream, args, world, barrier,
     result = gather()
     torch.cuda.synchronize()
     hout = torch.empty(result.shape, dtype=result.dtype, pin_memory=True)
+    # the lengths and the table arrive by host copy each step (no kernel writes them)
     cargs = [dec.args(q, k, v, table, lens, s.max_len, out=s.out, k_scale=ks, v_scale=vs, part_tokens=part,
-                      kernel=kernel) for (k, v, ks, vs) in s.pools]
+                      kernel=kernel, tables_ready=True) for (k, v, ks, vs) in s.pools]
     need = max(kvb.paged_workspace_bytes(c) for c in cargs)
     if need > dec.workspace.numel():
         dec.workspace = torch.zeros(need, dtype=torch.uint8, device=s.q.device)

@@ -85,7 +85,16 @@ typedef struct kvb_paged_args {
     const float* v_scale;
     int64_t num_blocks;   /* physical blocks in the pools (> 0 when any sequence is non-empty) */
     int kernel;           /* KVB_KERNEL_* */
+    int flags;            /* KVB_FLAG_* (no counterpart in the reference); 0 for the default */
 } kvb_paged_args;
+
+/* kvb_paged_args.flags.
+ * KVB_FLAG_TABLES_READY: seq_lens and block_table are not written by the kernel launched right
+ *   before this call on the same stream (host copies, and kernels launched earlier, are fine). The
+ *   tensor-core kernel then reads them while that kernel finishes (programmatic dependent launch)
+ *   instead of after it; q, the pools, the scales and the workspace are still read after it. A
+ *   decode loop whose tables come from host copies, or that launches steps back to back, sets it. */
+#define KVB_FLAG_TABLES_READY 1
 
 /* src/metal_attn.hpp:71-80 (NaiveArgs): contiguous cache [B][Hkv][max_len][D], fp32 or fp16. */
 typedef struct kvb_naive_args {

@@ -145,6 +145,7 @@ int check_static(const kvb_paged_args* a) {
     if (s.num_heads % s.num_kv_heads != 0) return fail(KVB_ERR_INVALID, "H % Hkv != 0");
     if (a->max_blocks < 0) return fail(KVB_ERR_INVALID, "max_blocks < 0");
     if (a->kernel < KVB_KERNEL_AUTO || a->kernel > KVB_KERNEL_UMMA) return fail(KVB_ERR_INVALID, "unknown kernel");
+    if (a->flags & ~KVB_FLAG_TABLES_READY) return fail(KVB_ERR_INVALID, "unknown flags");
     if (s.batch > 0 && (!a->q || !a->out || !a->seq_lens)) return fail(KVB_ERR_INVALID, "null q, out or seq_lens");
     if (s.batch > 0 && a->max_len > 0) {
         if (!a->k || !a->v || !a->block_table) return fail(KVB_ERR_INVALID, "null k, v or block_table");
@@ -222,6 +223,7 @@ int launch_paged(const kvb_paged_args* a, void* ws, cudaStream_t stream) {
     p.num_blocks = a->num_blocks;
     p.q_scale = 1.4426950408889634f / std::sqrt(float(s.head_dim));
     p.launch = next_launch_id();
+    p.tables_ready = (a->flags & KVB_FLAG_TABLES_READY) != 0;
 
     if (g.kernel < 0)
         return fail(KVB_ERR_INVALID, "the requested tensor-core kernel does not support this shape, page size or dtype");
@@ -631,8 +633,12 @@ int kvb_run_paged(const kvb_paged_args* a, int steps, double* gpu_ms) {
     }
     cudaEvent_t e0, e1;
     if (int rc = begin_timed(S, &e0, &e1)) return rc;
+    // Nothing on the library's stream writes the lengths or the block table (uploads are host
+    // copies), so every step may read them while the previous one finishes.
+    kvb_paged_args ready = *a;
+    ready.flags |= KVB_FLAG_TABLES_READY;
     for (int i = 0; i < steps; ++i) {
-        if (int rc = launch_paged(a, S.ws, S.stream)) {
+        if (int rc = launch_paged(&ready, S.ws, S.stream)) {
             cudaEventDestroy(e0);
             cudaEventDestroy(e1);
             return rc;

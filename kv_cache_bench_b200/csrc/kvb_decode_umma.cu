@@ -323,16 +323,49 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     const uint32_t tmem = *s_tmem;
     // tensor-memory columns: S^T buffers at 0 and 32, O^T buffers at 64 and 96 (one per chunk parity),
     // the groups' shares of a unit at UM_XCOL + 8 * (2 * slot + group)
-    pdl_wait();
-    pdl_trigger();
+    // With tables_ready the lengths and the block table are not written by the kernel before this
+    // one, so the unit enumeration and the producer's first block ids are read while that kernel
+    // finishes; q, the pools, the scales and the workspace are read only after the wait.
+    const bool early = p.tables_ready != 0;
+    if (!early) {
+        pdl_wait();
+        pdl_trigger();
+    }
     const int* prefix = nullptr;
     if (p.B <= KVB_PREFIX_MAX) {
         build_unit_prefix(p, s_prefix, reinterpret_cast<int*>(scratch), tid, UM_THREADS, 1, s_lens);
         prefix = s_prefix;
     }
     const long long total = unit_total(p, prefix);
-    note_counter_count(p);
     const int lp = __ffs(p.page) - 1;  // pages are powers of two on this path
+    // Block ids of a unit's pages into the page table (producer warp); refused ones (outside
+    // [0, num_blocks)) become -2.
+    auto read_block_ids = [&](const Unit& uu) {
+        const int* bt = p.block_table + (size_t)uu.b * p.max_blocks;
+        const int pg0 = uu.t0 >> lp, pg1 = (uu.t1 - 1) >> lp;
+        const int npg = min(pg1 - pg0 + 1, UM_PT);  // the host keeps partitions within UM_PT pages
+        __syncwarp();
+        for (int i = lane; i < npg; i += 32) {
+            int blk = __ldg(bt + pg0 + i);
+            if (blk < 0 || (long long)blk >= p.num_blocks) blk = -2;
+            pt_blk[i] = blk;
+        }
+        __syncwarp();
+    };
+    bool ids_early = false;  // producer: the first unit's block ids are already in the page table
+    if (early) {
+        if (warp == UM_PRODUCER) {
+            Unit u0;
+            if ((long long)blockIdx.x < total && unit_at(p, prefix, prefix ? s_lens : nullptr, blockIdx.x, u0) &&
+                u0.nparts > 0) {
+                read_block_ids(u0);
+                ids_early = true;
+            }
+        }
+        pdl_wait();
+        pdl_trigger();
+    }
+    note_counter_count(p);
 
     auto give_up = [&]() {
         *s_abort = 1;
@@ -378,19 +411,12 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             // A unit is published once its first chunk's loads are on their way (a tokenless one at once).
             if (real && u.nparts == 0) publish(int(idx));
             if (real && u.nparts > 0) {
-                const int* bt = p.block_table + (size_t)u.b * p.max_blocks;
                 const int pg0 = u.t0 >> lp, pg1 = (u.t1 - 1) >> lp;  // the unit's pages (pg1 - pg0 < UM_PT)
-                const int npg = min(pg1 - pg0 + 1, UM_PT);  // the host keeps partitions within UM_PT pages
+                const int npg = min(pg1 - pg0 + 1, UM_PT);
                 const int sb = unit_no & 1;
-                // Block ids of the unit; refused ones (outside [0, num_blocks)) become -2.
-                __syncwarp();
-                for (int i = lane; i < npg; i += 32) {
-                    int blk = __ldg(bt + pg0 + i);
-                    if (blk < 0 || (long long)blk >= p.num_blocks) blk = -2;
-                    pt_blk[i] = blk;
-                }
-                __syncwarp();
-                const int c0 = u.t0 / UM_CHUNK, c1 = (u.t1 + UM_CHUNK - 1) / UM_CHUNK;
+                if (!(ids_early && unit_no == 0)) read_block_ids(u);
+                // a unit starting at an odd running index gets one empty chunk in front (see the softmax)
+                const int c0 = u.t0 / UM_CHUNK - (kp & 1), c1 = (u.t1 + UM_CHUNK - 1) / UM_CHUNK;
                 for (int c = c0; c < c1; ++c) {
                     const int tok0 = c * UM_CHUNK;
                     if (lane == 0 && !*s_abort && !mbar_wait_bounded(&empty[stage], phase ^ 1u, s_abort)) give_up();
@@ -533,7 +559,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     ++unit_no;
                     qb = unit_no & 1;
                     const int k_base = k_end;
-                    k_end = k_base + (u.t1 + UM_CHUNK - 1) / UM_CHUNK - u.t0 / UM_CHUNK;
+                    k_end = k_base + (u.t1 + UM_CHUNK - 1) / UM_CHUNK - u.t0 / UM_CHUNK + (k_base & 1);
                     qk = k_base + ((k_base & 1) != par ? 1 : 0);
                     have_unit = true;
                     need_q = true;
@@ -626,7 +652,6 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         // the combined MMA result into a log2 score, publishes the unit and arrives on q_full. A unit
         // with nparts < 0 ends the groups' loop. Units without tokens get their outputs here.
         Unit u;
-        const bool q16 = (reinterpret_cast<uintptr_t>(p.q) & 15) == 0;
         int rpos = 0;  // next unit ring entry
         auto ring_next = [&]() {  // the next published unit index, -1 at the end (every lane)
             const int e = rpos % UM_RQ;
@@ -687,9 +712,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
 #pragma unroll
                 for (int j = 0; j < QB; ++j) {
                     const float* row = qrow + (g0 + j) * UM_D;
-                    xs[j] = g0 + j >= u.nh ? make_float4(0.f, 0.f, 0.f, 0.f)
-                            : q16          ? __ldg(reinterpret_cast<const float4*>(row))
-                                           : make_float4(__ldg(row), __ldg(row + 1), __ldg(row + 2), __ldg(row + 3));
+                    // q is 16-byte aligned (the host checks it)
+                    xs[j] = g0 + j < u.nh ? __ldg(reinterpret_cast<const float4*>(row)) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
 #pragma unroll
                 for (int j = 0; j < QB; ++j) {
@@ -827,7 +851,12 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 }
             };
 
-            const int c0 = u.t0 / UM_CHUNK, c1 = (u.t1 + UM_CHUNK - 1) / UM_CHUNK;
+            // Group g takes the unit's chunks at running indices of parity g. A unit that would start at
+            // an odd index gets one empty chunk (no valid token: nothing loaded, probabilities 0) in
+            // front, so its first chunk goes to group 0 whatever ran before it on this CTA: which
+            // chunks each group sums, and so the rounding of the unit's result, depend on the unit
+            // alone, not on how units were handed out.
+            const int c0 = u.t0 / UM_CHUNK - (k & 1), c1 = (u.t1 + UM_CHUNK - 1) / UM_CHUNK;
             for (int c = c0; c < c1; ++c, ++k) {
                 const int cur_stage = stage;
                 if (++stage == STAGES) stage = 0;

@@ -78,3 +78,12 @@ def test_workspace_layout_is_monotone_in_partitions():
 def test_available_is_false_without_gpu_or_true_with():
     import torch
     assert kvb.metal_available() == torch.cuda.is_available()
+
+
+def test_flags_field_and_unknown_flags_refused():
+    c = kvb.device_args(kvb.Shape(1, 8, 2, 128), kvb.KvType.f16, 16, 4, 64, q=16, k=16, v=16, block_table=16,
+                        seq_lens=16, out=16, num_blocks=4, part_tokens=16, tables_ready=True)
+    assert c.flags == kvb.FLAG_TABLES_READY
+    c.flags = kvb.FLAG_TABLES_READY | 0x10
+    with pytest.raises(ValueError, match="unknown flags"):
+        kvb.paged_workspace_bytes(c)

@@ -63,6 +63,25 @@ def test_cuda_graph_replay():
     del g
 
 
+@pytest.mark.parametrize("kv_type", [oracle.F16, oracle.I8])
+def test_tables_ready_and_dynamic_units_are_bit_identical(kv_type):
+    """FLAG_TABLES_READY (lengths and block ids read while the previous kernel finishes) and the
+    dynamic hand-out of units (far more units than CTAs here) change no bit of the output, over
+    repeated launches on one workspace (the work counters must come back to zero each time)."""
+    lens = [8000, 0, 3, 5000, 129] * 8
+    case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=lens, kv_type=kv_type, page=64,
+                            seed=11)
+    d = _dev(case)
+    dec = PagedDecoder()
+    outs = [_call(dec, d, case.max_len, part_tokens=512, tables_ready=ready).clone()
+            for ready in (False, True, True, False, True)]
+    torch.cuda.synchronize()
+    assert oracle.max_abs_diff(outs[0].cpu().numpy(), case.reference()) <= TOL
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    assert dec.error_flag() == 0
+
+
 @pytest.mark.parametrize("kernel", [kvb.Kernel.simt, kvb.Kernel.mma, kvb.Kernel.umma])
 def test_device_refuses_bad_lengths_with_nan_and_flag(kernel):
     case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=[300, 200, 100], kv_type=oracle.F16,
