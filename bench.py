@@ -526,15 +526,19 @@ def main():
             graphs[n] = g
         return graphs[n]
 
+    # graphs of at least 64 steps (a whole number of pool rotations): consecutive launches inside a
+    # graph overlap through programmatic dependent launch, launches across two replays do not
+    per_graph = copies * max(1, math.ceil(64 / copies))
+
     def run_steps(n):
         if not use_graph:
             for i in range(n):
                 step(i)
             return
-        full, rem = divmod(n, copies)
+        full, rem = divmod(n, per_graph)
         with torch.cuda.stream(stream):
             for _ in range(full):
-                graph_of(copies).replay()
+                graph_of(per_graph).replay()
             if rem:
                 graph_of(rem).replay()
 
