@@ -509,7 +509,11 @@ int page_write(const kvb_page_write_args* a, bool quantize, void* stream) {
     p.max_blocks = a->max_blocks;
     p.max_len = a->max_len;
     p.elem = (int)elem_size(a->kv_type);
+    p.src_elem = quantize ? (int)sizeof(float) : p.elem;
     p.num_blocks = a->num_blocks;
+    DeviceFacts f;
+    if (int rc = device_facts(&f)) return rc;
+    p.num_sms = f.num_sms;
     const cudaError_t e = kvb_launch_page_write(p, quantize, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return fail(KVB_ERR_DEVICE, std::string("page write launch: ") + cudaGetErrorString(e));
     return KVB_OK;

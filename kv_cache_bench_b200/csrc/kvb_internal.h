@@ -66,7 +66,10 @@ struct PageWriteParams {
     const int* block_table;  // [B][max_blocks]
     const int* seq_lens;     // [B]
     unsigned* error_flag;    // optional: KVB_DEVERR_LENGTH / KVB_DEVERR_BLOCK bits
-    int B, Hkv, D, page, max_blocks, max_len, elem;
+    int B, Hkv, D, page, max_blocks, max_len;
+    int elem;      // bytes per pool element
+    int src_elem;  // bytes per source element (4: fp32 for the quantizer)
+    int num_sms;   // sizes the persistent grid
     long long num_blocks;
 };
 cudaError_t kvb_launch_page_write(const PageWriteParams& p, bool quantize, cudaStream_t stream);

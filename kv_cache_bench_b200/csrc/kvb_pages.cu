@@ -1,19 +1,23 @@
 // The page write path in front of decode: a contiguous cache [B][Hkv][max_len][D] written into the
 // paged pool [num_blocks][Hkv][page][D] through the block table.
 //
-//   quantize_pages_i8  src/reference.cpp:32-51 (quantize_to_paged_i8): per (sequence, logical page,
-//                      KV head) amax over the page's live tokens and all D, scale = amax / 127 (fp32),
-//                      q = clamp(nearbyint(x / scale), -127, 127) with an IEEE fp32 division and
-//                      round-half-to-even, 0 when the scale is 0; the scale goes to
-//                      scales[block * Hkv + kvh].
-//   scatter_pages      src/reference.hpp:60-68 (scatter_to_paged): the live tokens copied unchanged.
+//   quantize (int8)   src/reference.cpp:32-51 (quantize_to_paged_i8): per (sequence, logical page,
+//                     KV head) amax over the page's live tokens and all D, scale = amax / 127 (fp32),
+//                     q = clamp(nearbyint(x / scale), -127, 127) with an IEEE fp32 division and
+//                     round-half-to-even, 0 when the scale is 0; the scale goes to
+//                     scales[block * Hkv + kvh].
+//   scatter           src/reference.hpp:60-68 (scatter_to_paged): the live tokens copied unchanged.
 //
-// Slots past a sequence's last token are not written (as in the reference). One CTA per (page, KV
-// head, sequence): the page's live rows are one contiguous run in both layouts, read and written
-// with 16-byte vectors. The quantizer reads its run twice (amax, then quantize); the second pass
-// hits L1/L2, so HBM sees each input byte once. Bad lengths or block ids skip the page and raise the
-// same error bits as the decode kernels.
+// Slots past a sequence's last token are not written (as in the reference). A persistent grid walks
+// the runs (sequence, page slot, KV head): a live page's rows are one contiguous run in both layouts,
+// moved with 16-byte vectors, PW_UNROLL of them in flight per thread, by one warp (runs under 64 KB)
+// or one CTA (larger runs, so that enough bytes are in flight). Dead slots cost a shared-memory
+// length lookup. The quantizer reads its run twice (amax, then quantize);
+// the second pass hits L1/L2, so HBM sees each input byte once. Bad lengths or block ids skip the
+// page and raise the same error bits as the decode kernels.
 #include <cuda_fp16.h>
+
+#include <algorithm>
 
 #include "kvb_device.cuh"
 
@@ -21,93 +25,162 @@ namespace {
 
 using namespace kvb_dev;
 
-constexpr int PG_THREADS = 256;
+constexpr int PW_THREADS = 256;
+constexpr int PW_WARPS = PW_THREADS / 32;
+constexpr int PW_UNROLL = 8;          // 16-byte loads in flight per lane
+constexpr int PW_LENS_MAX = 8192;     // sequence lengths cached in shared memory up to this batch
 
-struct PageUnit {
-    bool live;
-    int t0, n;      // first token and live tokens of the page
-    long long blk;  // physical block
+struct Run {
+    const void* src;  // first source byte of the run
+    void* dst;        // first pool byte of the run
+    long long blk;    // physical block
+    int kvh;          // KV head
+    int n;            // live tokens of the page
 };
 
-__device__ __forceinline__ PageUnit page_unit(const PageWriteParams& p, int b, int i, unsigned* flag) {
-    PageUnit u{false, 0, 0, 0};
-    const int len = __ldg(p.seq_lens + b);
+// The run of (sequence b, page slot i, KV head kvh), or n = 0 for a dead or refused slot (refusals
+// raise their error bit).
+__device__ __forceinline__ Run run_of(const PageWriteParams& p, int b, int i, int kvh, const int* s_len, int lane) {
+    Run r{nullptr, nullptr, 0, 0, 0};
+    const int len = s_len ? s_len[b] : __ldg(p.seq_lens + b);
     if (len < 0 || len > p.max_len || (long long)len > (long long)p.max_blocks * p.page) {
-        if (i == 0 && threadIdx.x == 0 && flag) raise_error(flag, KVB_DEVERR_LENGTH);
-        return u;
+        if (i == 0 && kvh == 0 && lane == 0 && p.error_flag) raise_error(p.error_flag, KVB_DEVERR_LENGTH);
+        return r;
     }
-    u.t0 = i * p.page;
-    if (u.t0 >= len) return u;
-    u.n = min(len - u.t0, p.page);
+    const int t0 = i * p.page;
+    if (t0 >= len) return r;
     const int blk = __ldg(p.block_table + (size_t)b * p.max_blocks + i);
     if (blk < 0 || (long long)blk >= p.num_blocks) {
-        if (threadIdx.x == 0 && flag) raise_error(flag, KVB_DEVERR_BLOCK);
-        return u;
+        if (kvh == 0 && lane == 0 && p.error_flag) raise_error(p.error_flag, KVB_DEVERR_BLOCK);
+        return r;
     }
-    u.blk = blk;
-    u.live = true;
-    return u;
+    const size_t row = (size_t)p.D * p.src_elem;
+    r.src = static_cast<const char*>(p.src) + (((size_t)b * p.Hkv + kvh) * p.max_len + t0) * row;
+    r.dst = static_cast<char*>(p.dst) + ((size_t)blk * p.Hkv + kvh) * p.page * (size_t)p.D * p.elem;
+    r.blk = blk;
+    r.kvh = kvh;
+    r.n = min(len - t0, p.page);
+    return r;
 }
 
-__global__ void __launch_bounds__(PG_THREADS) quantize_pages_kernel(const PageWriteParams p) {
-    const int i = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-    const PageUnit u = page_unit(p, b, i, p.error_flag);
-    if (!u.live) return;
-    const float* src = static_cast<const float*>(p.src) + (((size_t)b * p.Hkv + kvh) * p.max_len + u.t0) * p.D;
-    int8_t* dst = static_cast<int8_t*>(p.dst) + ((size_t)u.blk * p.Hkv + kvh) * p.page * p.D;
-    const int n4 = u.n * p.D / 4;  // D is a multiple of 4
-    const float4* s4 = reinterpret_cast<const float4*>(src);
-
-    float amax = 0.f;
-    for (int j = threadIdx.x; j < n4; j += PG_THREADS) {
-        const float4 x = __ldg(s4 + j);
-        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+// TPR threads (a warp or the whole CTA) per run.
+template <bool QUANT, int TPR>
+__global__ void __launch_bounds__(PW_THREADS) page_write_kernel(const PageWriteParams p) {
+    constexpr int GROUPS = PW_THREADS / TPR;  // runs in flight per CTA
+    __shared__ float s_max[2][PW_WARPS];
+    extern __shared__ int s_len_raw[];
+    const int* s_len = nullptr;
+    if (p.B <= PW_LENS_MAX) {
+        for (int b = threadIdx.x; b < p.B; b += PW_THREADS) s_len_raw[b] = __ldg(p.seq_lens + b);
+        __syncthreads();
+        s_len = s_len_raw;
     }
-    __shared__ float s_max[PG_THREADS / 32];
-    float r;
-    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(amax));
-    if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = r;
-    __syncthreads();
-    amax = s_max[0];
+    const int lane = threadIdx.x & 31;
+    const int gl = threadIdx.x % TPR;  // thread within the run's group
+    // Task t = (b * max_blocks + i) * Hkv + kvh, one group per task, tasks t, t + stride, ...; the
+    // position is advanced in mixed radix (no division per task).
+    const long long t0 = (long long)blockIdx.x * GROUPS + threadIdx.x / TPR;
+    const long long stride = (long long)gridDim.x * GROUPS;
+    int parity = 0;  // alternates the CTA-wide reduction slots
+    int kvh = int(t0 % p.Hkv), i = int(t0 / p.Hkv % p.max_blocks);
+    long long b = t0 / p.Hkv / p.max_blocks;
+    const int dk = int(stride % p.Hkv), di = int(stride / p.Hkv % p.max_blocks);
+    const long long db = stride / p.Hkv / p.max_blocks;
+    for (; b < p.B; kvh += dk, i += di, b += db) {
+        if (kvh >= p.Hkv) kvh -= p.Hkv, ++i;
+        if (i >= p.max_blocks) i -= p.max_blocks, ++b;
+        if (b >= p.B) break;
+        const Run r = run_of(p, int(b), i, kvh, s_len, gl);
+        if (r.n == 0) continue;
+        if constexpr (!QUANT) {
+            const uint4* s16 = static_cast<const uint4*>(r.src);
+            uint4* d16 = static_cast<uint4*>(r.dst);
+            const int n16 = int((size_t)r.n * p.D * p.elem / 16);  // rows are a multiple of 16 bytes
+            for (int j0 = 0; j0 < n16; j0 += TPR * PW_UNROLL) {
+                uint4 v[PW_UNROLL];
 #pragma unroll
-    for (int w = 1; w < PG_THREADS / 32; ++w) amax = fmaxf(amax, s_max[w]);
-    const float scale = amax / 127.0f;
-    if (threadIdx.x == 0) p.scales[(size_t)u.blk * p.Hkv + kvh] = scale;
-
-    uint32_t* d4 = reinterpret_cast<uint32_t*>(dst);
-    for (int j = threadIdx.x; j < n4; j += PG_THREADS) {
-        const float4 x = __ldg(s4 + j);
-        uint32_t packed = 0;
-        if (scale > 0.f) {
-            const float v[4] = {x.x, x.y, x.z, x.w};
+                for (int u = 0; u < PW_UNROLL; ++u) {
+                    const int j = j0 + u * TPR + gl;
+                    if (j < n16) v[u] = __ldcs(s16 + j);
+                }
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float q = fminf(fmaxf(rintf(__fdiv_rn(v[e], scale)), -127.f), 127.f);
-                packed |= (uint32_t)(uint8_t)(int8_t)q << (8 * e);
+                for (int u = 0; u < PW_UNROLL; ++u) {
+                    const int j = j0 + u * TPR + gl;
+                    if (j < n16) d16[j] = v[u];
+                }
+            }
+        } else {
+            const float4* s4 = static_cast<const float4*>(r.src);
+            const int n4 = r.n * p.D / 4;  // D is a multiple of 4
+            float amax = 0.f;
+            for (int j0 = 0; j0 < n4; j0 += TPR * PW_UNROLL) {
+                float4 v[PW_UNROLL];
+#pragma unroll
+                for (int u = 0; u < PW_UNROLL; ++u) {
+                    const int j = j0 + u * TPR + gl;
+                    v[u] = j < n4 ? __ldg(s4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < PW_UNROLL; ++u)
+                    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w))));
+            }
+            float m;
+            asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(m) : "f"(amax));
+            if constexpr (TPR > 32) {
+                // the CTA's warps agree (two slot sets: a fast warp's next run cannot overwrite this one)
+                if (lane == 0) s_max[parity][threadIdx.x >> 5] = m;
+                __syncthreads();
+#pragma unroll
+                for (int w = 0; w < PW_WARPS; ++w) m = fmaxf(m, s_max[parity][w]);
+                parity ^= 1;
+            }
+            const float scale = m / 127.0f;
+            if (gl == 0) p.scales[(size_t)r.blk * p.Hkv + r.kvh] = scale;
+            uint32_t* d4 = static_cast<uint32_t*>(r.dst);
+            for (int j0 = 0; j0 < n4; j0 += TPR * PW_UNROLL) {
+                float4 v[PW_UNROLL];
+#pragma unroll
+                for (int u = 0; u < PW_UNROLL; ++u) {
+                    const int j = j0 + u * TPR + gl;
+                    v[u] = j < n4 ? __ldcs(s4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < PW_UNROLL; ++u) {
+                    const int j = j0 + u * TPR + gl;
+                    if (j >= n4) continue;
+                    uint32_t packed = 0;
+                    if (scale > 0.f) {
+                        const float x[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float q = fminf(fmaxf(rintf(__fdiv_rn(x[e], scale)), -127.f), 127.f);
+                            packed |= (uint32_t)(uint8_t)(int8_t)q << (8 * e);
+                        }
+                    }
+                    d4[j] = packed;
+                }
             }
         }
-        d4[j] = packed;
     }
-}
-
-__global__ void __launch_bounds__(PG_THREADS) scatter_pages_kernel(const PageWriteParams p) {
-    const int i = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-    const PageUnit u = page_unit(p, b, i, p.error_flag);
-    if (!u.live) return;
-    const size_t row = (size_t)p.D * p.elem;  // bytes per token row (a multiple of 16)
-    const uint4* s16 = reinterpret_cast<const uint4*>(static_cast<const char*>(p.src) +
-                                                      (((size_t)b * p.Hkv + kvh) * p.max_len + u.t0) * row);
-    uint4* d16 = reinterpret_cast<uint4*>(static_cast<char*>(p.dst) + ((size_t)u.blk * p.Hkv + kvh) * p.page * row);
-    const int n16 = int((size_t)u.n * row / 16);
-    for (int j = threadIdx.x; j < n16; j += PG_THREADS) d16[j] = __ldg(s16 + j);
 }
 
 }  // namespace
 
 cudaError_t kvb_launch_page_write(const PageWriteParams& p, bool quantize, cudaStream_t stream) {
     if (p.B == 0 || p.max_blocks == 0 || p.Hkv == 0) return cudaSuccess;
-    const dim3 grid((unsigned)p.max_blocks, (unsigned)p.Hkv, (unsigned)p.B);
-    if (quantize) quantize_pages_kernel<<<grid, PG_THREADS, 0, stream>>>(p);
-    else scatter_pages_kernel<<<grid, PG_THREADS, 0, stream>>>(p);
+    const long long runs = (long long)p.B * p.max_blocks * p.Hkv;
+    const size_t run_bytes = (size_t)p.page * p.D * p.src_elem;
+    const bool cta_runs = run_bytes >= (size_t(64) << 10);
+    const int groups = cta_runs ? 1 : PW_WARPS;
+    const long long ctas = (runs + groups - 1) / groups;
+    const unsigned grid = (unsigned)std::min<long long>(ctas, (long long)p.num_sms * (cta_runs ? 8 : 4));
+    const size_t smem = p.B <= PW_LENS_MAX ? sizeof(int) * (size_t)p.B : 0;
+    if (quantize) {
+        if (cta_runs) page_write_kernel<true, PW_THREADS><<<grid, PW_THREADS, smem, stream>>>(p);
+        else page_write_kernel<true, 32><<<grid, PW_THREADS, smem, stream>>>(p);
+    } else {
+        if (cta_runs) page_write_kernel<false, PW_THREADS><<<grid, PW_THREADS, smem, stream>>>(p);
+        else page_write_kernel<false, 32><<<grid, PW_THREADS, smem, stream>>>(p);
+    }
     return cudaGetLastError();
 }
