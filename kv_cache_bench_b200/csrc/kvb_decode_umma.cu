@@ -962,14 +962,19 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     }
                 } else {
                     // probability * v_scale / (largest v_scale of the chunk) as an unsigned integer below
-                    // 2^30 whose four bytes are the four limbs
+                    // 2^30 whose four bytes are the four limbs (byte 3 = limb 0). Four neighbouring
+                    // tokens exchange them so that lane c of each quad writes limb row c for all four
+                    // tokens as one 32-bit word.
                     const float f = vscale_cur > 0.f ? vs / vscale_cur * kPScale : 0.f;
+                    const int quad = lane & ~3, qc = lane & 3;
+                    const uint32_t sel = uint32_t(3 - qc) | (uint32_t(7 - qc) << 4);  // byte 3 - qc of a, of b
 #pragma unroll
                     for (int g = 0; g < QGP; ++g) {
                         const uint32_t xi = __float2uint_rn(pr[g] * f);
-#pragma unroll
-                        for (int r2 = 0; r2 < 4; ++r2)
-                            *(pbuf + swz_off(g * 4 + r2, my_lane)) = uint8_t(xi >> (24 - 8 * r2));
+                        const uint32_t v0 = __shfl_sync(0xffffffffu, xi, quad), v1 = __shfl_sync(0xffffffffu, xi, quad + 1);
+                        const uint32_t v2 = __shfl_sync(0xffffffffu, xi, quad + 2), v3 = __shfl_sync(0xffffffffu, xi, quad + 3);
+                        const uint32_t w = __byte_perm(__byte_perm(v0, v1, sel), __byte_perm(v2, v3, sel), 0x5410);
+                        *reinterpret_cast<uint32_t*>(pbuf + swz_off(g * 4 + qc, (my_lane & ~3))) = w;
                     }
                 }
                 fence_proxy_async_smem();

@@ -12,8 +12,8 @@
 // the runs (sequence, page slot, KV head): a live page's rows are one contiguous run in both layouts,
 // moved with 16-byte vectors, PW_UNROLL of them in flight per thread, by one warp (runs under 64 KB)
 // or one CTA (larger runs, so that enough bytes are in flight). Dead slots cost a shared-memory
-// length lookup. The quantizer reads its run twice (amax, then quantize);
-// the second pass hits L1/L2, so HBM sees each input byte once. Bad lengths or block ids skip the
+// length lookup. The quantizer keeps a run of up to 8 KB in registers; a larger one it reads twice
+// (amax, then quantize), the second pass from L1/L2, so HBM sees each input byte once. Bad lengths or block ids skip the
 // page and raise the same error bits as the decode kernels.
 #include <cuda_fp16.h>
 
@@ -29,6 +29,7 @@ constexpr int PW_THREADS = 256;
 constexpr int PW_WARPS = PW_THREADS / 32;
 constexpr int PW_UNROLL = 8;          // 16-byte loads in flight per lane
 constexpr int PW_LENS_MAX = 8192;     // sequence lengths cached in shared memory up to this batch
+constexpr int PW_REG_F4 = 16;         // quantizer runs of up to 32 x 16 float4 (8 KB) stay in registers
 
 struct Run {
     const void* src;  // first source byte of the run
@@ -61,6 +62,38 @@ __device__ __forceinline__ Run run_of(const PageWriteParams& p, int b, int i, in
     r.kvh = kvh;
     r.n = min(len - t0, p.page);
     return r;
+}
+
+// Four values quantized with `scale` (0 when the scale is 0), packed low byte first:
+// clamp(rint(x / scale), -127, 127) with the IEEE division of the reference. |x / scale| <= 127, so
+// t = x * fl(1 / scale) is within 2^-16 of the exact quotient and fl(x / scale) within 2^-17 of it.
+// When t is at least 2^-14 away from every half-integer, no rounding boundary lies between t and
+// fl(x / scale), and the integer nearest t is the reference's value; only the rare t near a
+// boundary takes the division. t + 1.5 * 2^23 rounds t to that integer (ties to even) and holds it
+// in its low mantissa bits: two full-rate additions instead of a round and a conversion.
+// `rcp` = 1 / scale, or 0 when that is not finite (then every value takes the division).
+__device__ __forceinline__ uint32_t quantize4(const float4 v, float scale, float rcp) {
+    constexpr float kMagic = 12582912.f;  // 1.5 * 2^23
+    uint32_t packed = 0;
+    if (scale > 0.f) {
+        const float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float t = __fmul_rn(x[e], rcp);
+            const float y = __fadd_rn(t, kMagic);
+            int q = __float_as_int(y) - 0x4B400000;
+            const float frac = __fsub_rn(t, __fsub_rn(y, kMagic));
+            if (rcp == 0.f || fabsf(frac) >= 0.5f - 6.103515625e-05f) q = __float2int_rn(__fdiv_rn(x[e], scale));
+            q = min(max(q, -127), 127);
+            packed |= uint32_t(q & 255) << (8 * e);
+        }
+    }
+    return packed;
+}
+
+__device__ __forceinline__ float finite_rcp(float scale) {
+    const float r = 1.0f / scale;
+    return scale > 0.f && r < 3.0e38f ? r : 0.f;
 }
 
 // TPR threads (a warp or the whole CTA) per run.
@@ -112,6 +145,32 @@ __global__ void __launch_bounds__(PW_THREADS) page_write_kernel(const PageWriteP
         } else {
             const float4* s4 = static_cast<const float4*>(r.src);
             const int n4 = r.n * p.D / 4;  // D is a multiple of 4
+            if constexpr (TPR == 32) {
+                if (n4 <= 32 * PW_REG_F4) {
+                    // the whole run in registers: one read of the source
+                    float4 v[PW_REG_F4];
+                    float amax = 0.f;
+#pragma unroll
+                    for (int u = 0; u < PW_REG_F4; ++u) {
+                        const int j = u * 32 + lane;
+                        v[u] = j < n4 ? __ldcs(s4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int u = 0; u < PW_REG_F4; ++u)
+                        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w))));
+                    float m;
+                    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(m) : "f"(amax));
+                    const float scale = m / 127.0f, rcp = finite_rcp(scale);
+                    if (lane == 0) p.scales[(size_t)r.blk * p.Hkv + r.kvh] = scale;
+                    uint32_t* d4 = static_cast<uint32_t*>(r.dst);
+#pragma unroll
+                    for (int u = 0; u < PW_REG_F4; ++u) {
+                        const int j = u * 32 + lane;
+                        if (j < n4) d4[j] = quantize4(v[u], scale, rcp);
+                    }
+                    continue;
+                }
+            }
             float amax = 0.f;
             for (int j0 = 0; j0 < n4; j0 += TPR * PW_UNROLL) {
                 float4 v[PW_UNROLL];
@@ -134,7 +193,7 @@ __global__ void __launch_bounds__(PW_THREADS) page_write_kernel(const PageWriteP
                 for (int w = 0; w < PW_WARPS; ++w) m = fmaxf(m, s_max[parity][w]);
                 parity ^= 1;
             }
-            const float scale = m / 127.0f;
+            const float scale = m / 127.0f, rcp = finite_rcp(scale);
             if (gl == 0) p.scales[(size_t)r.blk * p.Hkv + r.kvh] = scale;
             uint32_t* d4 = static_cast<uint32_t*>(r.dst);
             for (int j0 = 0; j0 < n4; j0 += TPR * PW_UNROLL) {
@@ -147,17 +206,7 @@ __global__ void __launch_bounds__(PW_THREADS) page_write_kernel(const PageWriteP
 #pragma unroll
                 for (int u = 0; u < PW_UNROLL; ++u) {
                     const int j = j0 + u * TPR + gl;
-                    if (j >= n4) continue;
-                    uint32_t packed = 0;
-                    if (scale > 0.f) {
-                        const float x[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float q = fminf(fmaxf(rintf(__fdiv_rn(x[e], scale)), -127.f), 127.f);
-                            packed |= (uint32_t)(uint8_t)(int8_t)q << (8 * e);
-                        }
-                    }
-                    d4[j] = packed;
+                    if (j < n4) d4[j] = quantize4(v[u], scale, rcp);
                 }
             }
         }
@@ -173,7 +222,9 @@ cudaError_t kvb_launch_page_write(const PageWriteParams& p, bool quantize, cudaS
     const bool cta_runs = run_bytes >= (size_t(64) << 10);
     const int groups = cta_runs ? 1 : PW_WARPS;
     const long long ctas = (runs + groups - 1) / groups;
-    const unsigned grid = (unsigned)std::min<long long>(ctas, (long long)p.num_sms * (cta_runs ? 8 : 4));
+    // CTAs per SM that fit (the warp-per-run quantizer holds a run in registers: about 128 a thread)
+    const int per_sm = cta_runs ? 8 : quantize ? 2 : 4;
+    const unsigned grid = (unsigned)std::min<long long>(ctas, (long long)p.num_sms * per_sm);
     const size_t smem = p.B <= PW_LENS_MAX ? sizeof(int) * (size_t)p.B : 0;
     if (quantize) {
         if (cta_runs) page_write_kernel<true, PW_THREADS><<<grid, PW_THREADS, smem, stream>>>(p);
