@@ -54,7 +54,8 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "torch-sdpa"], default="ours",
+                    help="ours; the reference's CPU implementation; or torch SDPA on a contiguous cache")
     ap.add_argument("--config", type=int, default=3, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--dtype", choices=["f32", "f16", "i8"], default=None)
     ap.add_argument("--kernel", choices=["auto", "simt", "mma", "umma"], default="auto")
@@ -337,6 +338,96 @@ def run_reference_arm(args, w):
     print(json.dumps(line), flush=True)
 
 
+def run_torch_sdpa(args, w):
+    """`--impl torch-sdpa`: the library comparison point on the same GPU (the reference compares
+    itself with llama.cpp and MLX on its own hardware). torch's scaled_dot_product_attention on a
+    contiguous, unpaged cache [1][Hkv][L][D] of the same shape and storage type, the G query heads of a
+    KV head passed as G query rows so that K and V are read once per KV head, as in our kernel. Same
+    metric and algorithmic bytes; pool copies rotated past 4 x L2; CUDA-graph replays of at least 64
+    steps. Single-sequence configs (1-3) with f32 or f16 storage (SDPA takes no int8 cache); rank 0."""
+    import torch
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    if len(w["lens"]) != 1 or w["kv"] == "i8":
+        print(json.dumps({"impl": "torch-sdpa", "unavailable": "single-sequence f32/f16 configs only (1-3)"}),
+              flush=True)
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L, H, Hkv, D = w["lens"][0], w["H"], w["Hkv"], w["D"]
+    dt = torch.float16 if w["kv"] == "f16" else torch.float32
+    elem = 2 if w["kv"] == "f16" else 4
+    nbytes = min_bytes(w, w["lens"], Hkv, H)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    copies = max(1, min(64, math.ceil(4 * l2 / (L * Hkv * D * 2 * elem))))
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(w["seed"])
+
+    def uniform(*shape):
+        return (torch.rand(shape, generator=gen, device=dev) * 2 - 1).to(dt)
+
+    ks = [uniform(1, Hkv, L, D) for _ in range(copies)]
+    vs = [uniform(1, Hkv, L, D) for _ in range(copies)]
+    q = uniform(1, Hkv, H // Hkv, D)
+    chosen = None
+    for name, be in (("flash", SDPBackend.FLASH_ATTENTION), ("cudnn", SDPBackend.CUDNN_ATTENTION),
+                     ("efficient", SDPBackend.EFFICIENT_ATTENTION), ("math", SDPBackend.MATH)):
+        try:
+            with sdpa_kernel(be):
+                F.scaled_dot_product_attention(q, ks[0], vs[0])
+            torch.cuda.synchronize()
+            chosen = (name, be)
+            break
+        except RuntimeError:
+            continue
+    name, be = chosen
+    per_graph = copies * max(1, math.ceil(64 / copies))
+    stream = torch.cuda.Stream(dev)
+    graphs = {}
+
+    def graph_of(n):
+        if n not in graphs:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream), sdpa_kernel(be):
+                F.scaled_dot_product_attention(q, ks[0], vs[0])
+                stream.synchronize()
+                with torch.cuda.graph(g, stream=stream):
+                    for i in range(n):
+                        F.scaled_dot_product_attention(q, ks[i % copies], vs[i % copies])
+            graphs[n] = g
+        return graphs[n]
+
+    def run_steps(n):
+        full, rem = divmod(n, per_graph)
+        with torch.cuda.stream(stream):
+            for _ in range(full):
+                graph_of(per_graph).replay()
+            if rem:
+                graph_of(rem).replay()
+
+    run_steps(max(args.warmup, 3))
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record()
+    run_steps(args.steps)
+    with torch.cuda.stream(stream):
+        e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    value = round(nbytes / (ms * 1e-3) / 1e9, 2)
+    cfg = config_obj(w, None, 1)
+    cfg.update({"layout": "contiguous [1][Hkv][L][D], G query rows per KV head", "sdpa_backend": name,
+                "l2": f"{copies} cache copies rotated", "submission": "cuda graph replay"})
+    print(json.dumps({"impl": "torch-sdpa", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": 1,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 6),
+                      "higher_is_better": True, "dtype": w["kv"], "data": "synthetic: seeded U(-1,1) q/K/V",
+                      "config": cfg, "torch": torch.__version__}), flush=True)
+
+
 def config_obj(w, part, world):
     par = {"replica": "replicas", "sequence": f"sequence-sharded x{world} (LPT)",
            "kv_head": f"kv-head-sharded x{world}"}[w["shard"]]
@@ -431,6 +522,9 @@ def main():
     w = workload(args.config, args.dtype)
     if args.impl == "reference":
         run_reference_arm(args, w)
+        return
+    if args.impl == "torch-sdpa":
+        run_torch_sdpa(args, w)
         return
     if args.op != "decode":
         run_write_path(args, w)
