@@ -63,3 +63,13 @@ def test_reference_arm_prints_the_contract_line():
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
     assert line["cpu_baseline"]["kind"] == "reference" and line["cpu_baseline"]["cores"] >= 1
     assert line["metric"] == bench.METRIC and line["higher_is_better"] is True
+
+
+def test_sdpa_arm_refuses_batched_and_int8_configs():
+    # torch SDPA takes neither a block table nor an int8 cache: batched and int8 configs print the
+    # contract's `unavailable` line (this path needs no GPU)
+    for extra in (["--config", "4"], ["--config", "3"]):
+        out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "torch-sdpa"] + extra,
+                             check=True, capture_output=True, text=True, timeout=300)
+        line = json.loads(out.stdout.strip().splitlines()[-1])
+        assert line["impl"] == "torch-sdpa" and "unavailable" in line
