@@ -63,12 +63,14 @@ def test_cuda_graph_replay():
     del g
 
 
-@pytest.mark.parametrize("kv_type", [oracle.F16, oracle.I8])
-def test_tables_ready_and_dynamic_units_are_bit_identical(kv_type):
+@pytest.mark.parametrize("kv_type,lens", [(oracle.F16, [8000, 0, 3, 5000, 129] * 8),
+                                          (oracle.I8, [8000, 0, 3, 5000, 129] * 8),
+                                          (oracle.F16, [(i * 97) % 701 for i in range(300)])])
+def test_tables_ready_and_dynamic_units_are_bit_identical(kv_type, lens):
     """FLAG_TABLES_READY (lengths and block ids read while the previous kernel finishes) and the
     dynamic hand-out of units (far more units than CTAs here) change no bit of the output, over
-    repeated launches on one workspace (the work counters must come back to zero each time)."""
-    lens = [8000, 0, 3, 5000, 129] * 8
+    repeated launches on one workspace (the work counters must come back to zero each time). The
+    300-sequence case enumerates units densely (more sequences than the per-CTA prefix holds)."""
     case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=lens, kv_type=kv_type, page=64,
                             seed=11)
     d = _dev(case)

@@ -21,6 +21,7 @@ pytestmark = pytest.mark.gpu
 TOL = 2e-5
 
 EDGE = [0, 1, 7, 63, 64, 65, 127, 128, 129, 300, 1025]
+BATCH300 = [(i * 97) % 701 for i in range(300)]  # ragged, 0 to 700 tokens, one empty sequence
 
 CASES = [
     # name, H, Hkv, D, kv_type, page, lens, parts, extra
@@ -54,6 +55,9 @@ CASES = [
     ("long_i8_p128", 32, 8, 128, oracle.I8, 128, [20000], [0, 4096], {}),
     ("long_f16_p64", 32, 8, 128, oracle.F16, 64, [9000, 2500], [0, 512], {}),
     ("batch_ragged_f16_p16", 32, 8, 128, oracle.F16, 16, list(range(0, 1200, 37)), [0], dict(pool_slack=1.1)),
+    # more than 256 sequences: units enumerated densely (no per-CTA prefix), handed out dynamically
+    ("batch300_dense_f16_p16", 32, 8, 128, oracle.F16, 16, BATCH300, [0, 128], dict(pool_slack=1.1)),
+    ("batch300_dense_i8_p64", 32, 8, 128, oracle.I8, 64, BATCH300, [0], dict(varied=True)),
     ("chunk128_edges_i8_p32", 32, 8, 128, oracle.I8, 32, [127, 128, 129, 255, 256, 257, 384], [0, 128, 200], {}),
     ("chunk128_edges_f16_p128", 32, 8, 128, oracle.F16, 128, [127, 128, 129, 255, 256, 257], [0, 128, 200], {}),
     ("gqa2_i8_p64", 16, 8, 128, oracle.I8, 64, [700, 1], [0], dict(varied=True)),
