@@ -1118,7 +1118,8 @@ bool kvb_umma_supported(int kv_type, int D, int page, int qg, int part_tokens) {
     if (D != 128) return false;
     if (!(page == 8 || page == 16 || page == 32 || page == 64 || page == 128 || page == 256)) return false;
     // a partition's pages and chunks must fit the page table and the per-chunk V scale bounds
-    // (part_tokens 0: the automatic size, at most 4096 tokens, 2048 for 8-token pages)
+    // (part_tokens 0: the automatic size, at most 8064 tokens for pages of 32 tokens or more, 4096
+    // for 16-token pages, 2048 for 8-token pages)
     if (part_tokens > 0 && (part_tokens / page + 2 > UM_PT || part_tokens > (UM_UCH - 1) * UM_CHUNK)) return false;
     return qg >= 1 && qg <= 8;
 }

@@ -84,6 +84,18 @@ def test_tables_ready_and_dynamic_units_are_bit_identical(kv_type, lens):
     assert dec.error_flag() == 0
 
 
+def test_automatic_partitions_grow_with_many_units():
+    """With far more units than SMs and pages of 32 tokens or more, the automatic partition exceeds
+    4096 tokens (up to 8064); a small batch keeps the one-wave split."""
+    mk = lambda B, L, page: kvb.device_args(kvb.Shape(B, 64, 8, 128), kvb.KvType.f16, page, (L + page - 1) // page,  # noqa: E731
+                                            L, q=256, k=256, v=256, block_table=256, seq_lens=256, out=256,
+                                            num_blocks=B * ((L + page - 1) // page))
+    big = kvb.paged_part_tokens(mk(256, 131072, 64))
+    assert 4096 < big <= 8064 and big % 128 == 0
+    assert kvb.paged_part_tokens(mk(256, 131072, 16)) <= 4096  # 16-token pages: the page table's bound
+    assert kvb.paged_part_tokens(mk(1, 32768, 128)) <= 4096
+
+
 @pytest.mark.parametrize("kernel", [kvb.Kernel.simt, kvb.Kernel.mma, kvb.Kernel.umma])
 def test_device_refuses_bad_lengths_with_nan_and_flag(kernel):
     case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=[300, 200, 100], kv_type=oracle.F16,

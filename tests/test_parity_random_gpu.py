@@ -58,6 +58,9 @@ CASES = [
     # more than 256 sequences: units enumerated densely (no per-CTA prefix), handed out dynamically
     ("batch300_dense_f16_p16", 32, 8, 128, oracle.F16, 16, BATCH300, [0, 128], dict(pool_slack=1.1)),
     ("batch300_dense_i8_p64", 32, 8, 128, oracle.I8, 64, BATCH300, [0], dict(varied=True)),
+    # 8064-token partitions (63 chunks: the largest the tcgen05 page table and V-scale table take)
+    ("part8064_i8_p64", 32, 8, 128, oracle.I8, 64, [20000, 9000, 8064, 8065], [8064], dict(varied=True)),
+    ("part8064_f16_p32", 64, 8, 128, oracle.F16, 32, [17000, 8063, 129], [8064], {}),
     ("chunk128_edges_i8_p32", 32, 8, 128, oracle.I8, 32, [127, 128, 129, 255, 256, 257, 384], [0, 128, 200], {}),
     ("chunk128_edges_f16_p128", 32, 8, 128, oracle.F16, 128, [127, 128, 129, 255, 256, 257], [0, 128, 200], {}),
     ("gqa2_i8_p64", 16, 8, 128, oracle.I8, 64, [700, 1], [0], dict(varied=True)),
