@@ -93,20 +93,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
 }
 
-// Waits until the shared-memory counter `*c` reaches `target` (another warp raises it), for at most
-// KVB_WAIT_LIMIT_NS (or until `*abort` is set). Returns false when it gave up.
-__device__ __forceinline__ bool wait_counter(volatile int* c, int target, volatile int* abort) {
-    if (*c >= target) return true;
-    const uint64_t t0 = globaltimer_ns();
-    for (uint32_t it = 1;; ++it) {
-        if (*c >= target) return true;
-        if ((it & 255u) == 0) {
-            if (*abort) return false;
-            if (globaltimer_ns() - t0 > KVB_WAIT_LIMIT_NS) return false;
-        }
-    }
-}
-
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
