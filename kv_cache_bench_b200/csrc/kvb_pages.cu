@@ -72,6 +72,10 @@ __device__ __forceinline__ Run run_of(const PageWriteParams& p, int b, int i, in
 // boundary takes the division. t + 1.5 * 2^23 rounds t to that integer (ties to even) and holds it
 // in its low mantissa bits: two full-rate additions instead of a round and a conversion.
 // `rcp` = 1 / scale, or 0 when that is not finite (then every value takes the division).
+// The reference's rounding by way of the IEEE division, kept out of line so that the rare values
+// that need it branch to it instead of every value evaluating it.
+__device__ __noinline__ int quantize_by_division(float x, float scale) { return __float2int_rn(__fdiv_rn(x, scale)); }
+
 __device__ __forceinline__ uint32_t quantize4(const float4 v, float scale, float rcp) {
     constexpr float kMagic = 12582912.f;  // 1.5 * 2^23
     uint32_t packed = 0;
@@ -83,7 +87,7 @@ __device__ __forceinline__ uint32_t quantize4(const float4 v, float scale, float
             const float y = __fadd_rn(t, kMagic);
             int q = __float_as_int(y) - 0x4B400000;
             const float frac = __fsub_rn(t, __fsub_rn(y, kMagic));
-            if (rcp == 0.f || fabsf(frac) >= 0.5f - 6.103515625e-05f) q = __float2int_rn(__fdiv_rn(x[e], scale));
+            if (rcp == 0.f || fabsf(frac) >= 0.5f - 6.103515625e-05f) q = quantize_by_division(x[e], scale);
             q = min(max(q, -127), 127);
             packed |= uint32_t(q & 255) << (8 * e);
         }
