@@ -68,29 +68,33 @@ __device__ __forceinline__ Run run_of(const PageWriteParams& p, int b, int i, in
 // clamp(rint(x / scale), -127, 127) with the IEEE division of the reference. |x / scale| <= 127, so
 // t = x * fl(1 / scale) is within 2^-16 of the exact quotient and fl(x / scale) within 2^-17 of it.
 // When t is at least 2^-14 away from every half-integer, no rounding boundary lies between t and
-// fl(x / scale), and the integer nearest t is the reference's value; only the rare t near a
-// boundary takes the division. t + 1.5 * 2^23 rounds t to that integer (ties to even) and holds it
-// in its low mantissa bits: two full-rate additions instead of a round and a conversion.
-// `rcp` = 1 / scale, or 0 when that is not finite (then every value takes the division).
-// The reference's rounding by way of the IEEE division, kept out of line so that the rare values
-// that need it branch to it instead of every value evaluating it.
-__device__ __noinline__ int quantize_by_division(float x, float scale) { return __float2int_rn(__fdiv_rn(x, scale)); }
-
-__device__ __forceinline__ uint32_t quantize4(const float4 v, float scale, float rcp) {
+// fl(x / scale), and the integer nearest t is the reference's value. t + 1.5 * 2^23 rounds t to that
+// integer (ties to even) and holds it in its low mantissa bits: two full-rate additions instead of a
+// round and a conversion. The fast path flags (in `near`) any value close to a boundary; the caller
+// then redoes its values with quantize4_exact, which takes the division (rare: one test per run, not
+// a branch per value). `rcp` = 1 / scale, finite.
+__device__ __forceinline__ uint32_t quantize4_fast(const float4 v, float rcp, int& near) {
     constexpr float kMagic = 12582912.f;  // 1.5 * 2^23
+    const float x[4] = {v.x, v.y, v.z, v.w};
     uint32_t packed = 0;
-    if (scale > 0.f) {
-        const float x[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float t = __fmul_rn(x[e], rcp);
-            const float y = __fadd_rn(t, kMagic);
-            int q = __float_as_int(y) - 0x4B400000;
-            const float frac = __fsub_rn(t, __fsub_rn(y, kMagic));
-            if (rcp == 0.f || fabsf(frac) >= 0.5f - 6.103515625e-05f) q = quantize_by_division(x[e], scale);
-            q = min(max(q, -127), 127);
-            packed |= uint32_t(q & 255) << (8 * e);
-        }
+    for (int e = 0; e < 4; ++e) {
+        const float t = __fmul_rn(x[e], rcp);
+        const float y = __fadd_rn(t, kMagic);
+        const int q = min(max(__float_as_int(y) - 0x4B400000, -127), 127);
+        near |= fabsf(__fsub_rn(t, __fsub_rn(y, kMagic))) >= 0.5f - 6.103515625e-05f;
+        packed |= uint32_t(q & 255) << (8 * e);
+    }
+    return packed;
+}
+
+__device__ __noinline__ uint32_t quantize4_exact(const float4 v, float scale) {
+    const float x[4] = {v.x, v.y, v.z, v.w};
+    uint32_t packed = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int q = min(max(__float2int_rn(__fdiv_rn(x[e], scale)), -127), 127);
+        packed |= uint32_t(q & 255) << (8 * e);
     }
     return packed;
 }
@@ -167,10 +171,18 @@ __global__ void __launch_bounds__(PW_THREADS) page_write_kernel(const PageWriteP
                     const float scale = m / 127.0f, rcp = finite_rcp(scale);
                     if (lane == 0) p.scales[(size_t)r.blk * p.Hkv + r.kvh] = scale;
                     uint32_t* d4 = static_cast<uint32_t*>(r.dst);
+                    int near = scale > 0.f && rcp == 0.f;
 #pragma unroll
                     for (int u = 0; u < PW_REG_F4; ++u) {
                         const int j = u * 32 + lane;
-                        if (j < n4) d4[j] = quantize4(v[u], scale, rcp);
+                        if (j < n4) d4[j] = scale > 0.f ? quantize4_fast(v[u], rcp, near) : 0u;
+                    }
+                    if (near) {
+#pragma unroll
+                        for (int u = 0; u < PW_REG_F4; ++u) {
+                            const int j = u * 32 + lane;
+                            if (j < n4) d4[j] = quantize4_exact(v[u], scale);
+                        }
                     }
                     continue;
                 }
@@ -207,10 +219,18 @@ __global__ void __launch_bounds__(PW_THREADS) page_write_kernel(const PageWriteP
                     const int j = j0 + u * TPR + gl;
                     v[u] = j < n4 ? __ldcs(s4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
+                int near = scale > 0.f && rcp == 0.f;
 #pragma unroll
                 for (int u = 0; u < PW_UNROLL; ++u) {
                     const int j = j0 + u * TPR + gl;
-                    if (j < n4) d4[j] = quantize4(v[u], scale, rcp);
+                    if (j < n4) d4[j] = scale > 0.f ? quantize4_fast(v[u], rcp, near) : 0u;
+                }
+                if (near) {
+#pragma unroll
+                    for (int u = 0; u < PW_UNROLL; ++u) {
+                        const int j = j0 + u * TPR + gl;
+                        if (j < n4) d4[j] = quantize4_exact(v[u], scale);
+                    }
                 }
             }
         }
