@@ -87,3 +87,32 @@ def test_flags_field_and_unknown_flags_refused():
     c.flags = kvb.FLAG_TABLES_READY | 0x10
     with pytest.raises(ValueError, match="unknown flags"):
         kvb.paged_workspace_bytes(c)
+
+
+def _c_layout(struct, fields):
+    """sizeof and offsetof of a header struct, from a small C program compiled against the header."""
+    import subprocess
+    import tempfile
+    src = ["#include <stdio.h>", "#include <stddef.h>", '#include "kvb_cuda.h"', "int main(void) {",
+           f'  printf("%zu\\n", sizeof({struct}));']
+    src += [f'  printf("%zu\\n", offsetof({struct}, {f}));' for f in fields]
+    src += ["  return 0;", "}"]
+    with tempfile.TemporaryDirectory() as d:
+        c, exe = os.path.join(d, "layout.c"), os.path.join(d, "layout")
+        with open(c, "w") as fh:
+            fh.write("\n".join(src) + "\n")
+        subprocess.run(["gcc", "-std=c11", "-I", os.path.join(ROOT, "include"), c, "-o", exe], check=True)
+        out = subprocess.run([exe], check=True, capture_output=True, text=True).stdout.split()
+    return [int(x) for x in out]
+
+
+@pytest.mark.parametrize("struct,cls", [("kvb_shape", "_CShape"), ("kvb_paged_args", "_CPagedArgs"),
+                                        ("kvb_naive_args", "_CNaiveArgs"), ("kvb_page_write_args", "_CPageWriteArgs")])
+def test_python_structs_match_the_header_layout(struct, cls):
+    # the ctypes mirrors must agree with the C header field for field: a field added on one side only
+    # would shift every later one
+    c = getattr(kvb, cls)
+    names = [f[0] for f in c._fields_]
+    got = _c_layout(struct, names)
+    assert got[0] == ctypes.sizeof(c), (struct, got[0], ctypes.sizeof(c))
+    assert got[1:] == [getattr(c, n).offset for n in names], struct
