@@ -383,6 +383,9 @@ def run_torch_sdpa(args, w):
             break
         except RuntimeError:
             continue
+    if chosen is None:
+        print(json.dumps({"impl": "torch-sdpa", "unavailable": "no SDPA backend ran this shape"}), flush=True)
+        return
     name, be = chosen
     per_graph = copies * max(1, math.ceil(64 / copies))
     stream = torch.cuda.Stream(dev)
