@@ -64,6 +64,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every step from the host")
     ap.add_argument("--ramp-s", type=float, default=1.0, help="untimed load before warm-up (clock ramp)")
+    ap.add_argument("--seqs", type=int, default=None,
+                    help="keep only the first N sequences of the config (a smaller case for profilers)")
     ap.add_argument("--op", choices=["decode", "quantize", "scatter"], default="decode",
                     help="decode step (default) or the page write path in front of it (one GPU)")
     return ap.parse_args()
@@ -100,7 +102,8 @@ def workload(cfg: int, dtype):
 
 def describe(w):
     toks = sum(w["lens"])
-    return (f"config{w['cfg']}: {w['kv']} cache, B={len(w['lens'])}, H={w['H']}/Hkv={w['Hkv']}, D={w['D']}, "
+    cut = f" (first {len(w['lens'])} sequences)" if w.get("cut") else ""
+    return (f"config{w['cfg']}{cut}: {w['kv']} cache, B={len(w['lens'])}, H={w['H']}/Hkv={w['Hkv']}, D={w['D']}, "
             f"page={w['page']}, tokens={toks}, max_len={max(w['lens'])}")
 
 
@@ -523,6 +526,8 @@ def run_write_path(args, w):
 def main():
     args = parse_args()
     w = workload(args.config, args.dtype)
+    if args.seqs is not None and 0 < args.seqs < len(w["lens"]):
+        w["lens"], w["cut"] = w["lens"][:args.seqs], True
     if args.impl == "reference":
         run_reference_arm(args, w)
         return
