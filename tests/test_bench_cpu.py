@@ -73,3 +73,9 @@ def test_sdpa_arm_refuses_batched_and_int8_configs():
                              check=True, capture_output=True, text=True, timeout=300)
         line = json.loads(out.stdout.strip().splitlines()[-1])
         assert line["impl"] == "torch-sdpa" and "unavailable" in line
+
+
+def test_sequence_cap_names_the_cut():
+    w = bench.workload(5, "i8")
+    w["lens"], w["cut"] = w["lens"][:16], True
+    assert "first 16 sequences" in bench.describe(w) and "B=16" in bench.describe(w)
