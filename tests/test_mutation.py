@@ -1,8 +1,8 @@
 """Mutation harness: known bugs planted one at a time, each of which the golden-vector checks must
 catch. The reference's harness (scripts/mutation.sh:29-59) plants them in its GPU kernel and
-expects its GPU tests to fail. On this shared GPU pool no kernel is broken on purpose, so the bugs are
+expects its GPU tests to fail. On a shared GPU no kernel is broken on purpose, so the bugs are
 planted in the CPU oracle (oracle/kvb_oracle.c, compiled from a mutated copy) instead. The checks are
-the ones the CUDA kernels are judged by: the reference's own outputs within the kernel tolerance
+the ones the CUDA kernels are checked against: the reference's own outputs within the kernel tolerance
 (2e-5 absolute, NaN only where the reference has NaN), and its int8 pools and scales exactly. A
 mutant that slips through means those checks could not tell that bug from a correct kernel either."""
 import os
