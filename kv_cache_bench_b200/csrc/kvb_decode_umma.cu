@@ -163,6 +163,13 @@ __device__ __forceinline__ float limbs_to_float(uint32_t r0, uint32_t r1, uint32
             small_int_to_float(int(r2))) * 256.f + small_int_to_float(int(r3));
 }
 
+// The same recombination for limb sums of any int32 value (the int8 O^T accumulator sums up to 64
+// chunks: below 2^28 per limb), with conversions.
+__device__ __forceinline__ float limbs_to_float_wide(uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+    return ((__int2float_rn(int(r0)) * 256.f + __int2float_rn(int(r1))) * 256.f + __int2float_rn(int(r2))) * 256.f +
+           __int2float_rn(int(r3));
+}
+
 __device__ __forceinline__ float max4(float4 v) { return fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)); }
 
 // Largest value among the 32 lanes of the warp (redux.sync on floats, sm_100a).
@@ -186,7 +193,8 @@ struct UCfg {
     static constexpr size_t BAD_OFF = P_OFF + 2 * PBUF;        // [STAGES] a block id of the chunk was refused
     // int8: largest V scale of every chunk of a unit, [2 units][UM_UCH chunks]
     static constexpr size_t VSMAX_OFF = BAD_OFF + STAGES * sizeof(int);
-    static constexpr size_t BAR_OFF = kvb_align_up(VSMAX_OFF + (KVT == 2 ? 2 * UM_UCH : 0) * sizeof(float), 64);
+    // int8: and then the largest V scale of the whole unit, [2 units]
+    static constexpr size_t BAR_OFF = kvb_align_up(VSMAX_OFF + (KVT == 2 ? 2 * UM_UCH + 2 : 0) * sizeof(float), 64);
     // full per (stage, chunk parity); empty per stage; q_full, q_free, s_full, s_free, p_full,
     // o_full, pt_free x2; r_full, r_empty x UM_RQ
     // unit ring: full and empty per entry
@@ -209,7 +217,8 @@ struct UCfg {
     static constexpr size_t XML_OFF = SLOT_QS_OFF + 2 * 8 * sizeof(float);    // [2 slots][2 groups][24] float
     static constexpr size_t XCNT_OFF = XML_OFF + 2 * 2 * 24 * sizeof(float);  // [2] int count, [2] int flags
     static constexpr size_t RING_OFF = XCNT_OFF + 16;                         // [UM_RQ] unit indices
-    static constexpr size_t SMEM = RING_OFF + UM_RQ * sizeof(int) + 1024;
+    static constexpr size_t RESTART_OFF = RING_OFF + UM_RQ * sizeof(int);     // [2] int8 PV restarts O^T
+    static constexpr size_t SMEM = RESTART_OFF + 2 * sizeof(int) + 1024;
 };
 
 static_assert(UCfg<1>::SMEM <= 227 * 1024 && UCfg<2>::SMEM <= 227 * 1024, "shared memory budget");
@@ -257,6 +266,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     uint64_t* r_full = q_full + 14;        // [UM_RQ] unit ring entry written (producer -> consumers)
     uint64_t* r_empty = r_full + UM_RQ;    // [UM_RQ] unit ring entry read (MMA issuers, Qhat warp)
     int* s_ring = reinterpret_cast<int*>(smem + C::RING_OFF);
+    volatile int* p_restart = reinterpret_cast<volatile int*>(smem + C::RESTART_OFF);
     float* red = reinterpret_cast<float*>(smem + C::RED_OFF);
     int* pt_blk = reinterpret_cast<int*>(smem + C::WIN_OFF);
     float* pt_ks = reinterpret_cast<float*>(pt_blk + UM_PT);  // int8 only: [2][UM_PT]
@@ -481,13 +491,18 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                         __syncwarp();
                         // the largest V scale of each of the unit's chunks (an int8 probability scale bound)
                         float* um = unit_vsmax + sb * UM_UCH;
+                        float vunit = 0.f;
                         for (int j = lane; j < c1 - c0 && j < UM_UCH; j += 32) {
                             const int a = max(((c0 + j) * UM_CHUNK) >> lp, pg0) - pg0;
                             const int z = min((((c0 + j + 1) * UM_CHUNK - 1) >> lp), pg1) - pg0;
                             float vmax = 0.f;
                             for (int i = a; i <= z; ++i) vmax = fmaxf(vmax, vs_b[i]);
                             um[j] = vmax;
+                            vunit = fmaxf(vunit, vmax);
                         }
+                        // and the whole unit's (the int8 O^T accumulator's probability scale)
+                        vunit = warp_max(vunit);
+                        if (lane == 0) unit_vsmax[2 * UM_UCH + sb] = vunit;
                         __syncwarp();  // every lane's scale writes happen before the arrive
                         if (lane == 0) mbar_arrive(fb);
                     }
@@ -579,6 +594,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     if (mbar_test(&p_full[par], uint32_t(kk >> 1) & 1)) {
                         tc_fence_after();
                         const uint32_t vt = sbase + st * C::STAGE + NSUB * TILE;
+                        // int8: O^T accumulates over the group's chunks until the softmax restarts it
+                        const bool keep = KVT == 2 && p_restart[par] == 0;
 #pragma unroll
                         for (int s = 0; s < UM_CHUNK / KQK; ++s) {
                             // V^T (MN-major): KQK token rows per instruction = KQK/8 atoms of 1024 B; the
@@ -586,7 +603,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                             const uint32_t voff = s * (KQK / 8) * 1024;
                             const uint32_t poff = (s * 32 / 128) * (C::NMAX * 128) + (s * 32) % 128;
                             tc_mma<KVT>(o_tm, smem_desc(vt + voff, TILE, 1024), smem_desc(pb + poff, 16, 1024),
-                                        idesc_pv, s > 0);
+                                        idesc_pv, s > 0 || keep);
                         }
                         tc_commit(&o_full[par]);
                         tc_commit(&empty[st]);  // K and V of chunk kk are no longer read
@@ -821,6 +838,18 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     tc_ld8(obuf + 24, *reinterpret_cast<uint32_t(*)[8]>(&ro[24]));
                 }
             };
+            // int8: adds the O^T accumulator (its PV products done; probabilities scaled by
+            // kPScale / vunit) to the registers.
+            auto fold_acc = [&](float vunit) {
+                tc_fence_after();
+                load_o();
+                tc_wait_ld();
+                tc_fence_before();
+#pragma unroll
+                for (int g = 0; g < QGP; ++g)
+                    o[g] += limbs_to_float_wide(ro[4 * g], ro[4 * g + 1], ro[4 * g + 2], ro[4 * g + 3]) *
+                            (vunit * kPUnit);
+            };
             auto fold_prev = [&](int kp, bool loaded) {
                 if (!loaded) {
                     if (!*s_abort && !mbar_wait_bounded(&o_full[gi], uint32_t(kp >> 1) & 1, s_abort)) give_up();
@@ -883,7 +912,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 // this token's page scales (int8), read while the tensor-memory loads are in flight
                 // the previous chunk's O^T too, when its PV product is already done (one load wait);
                 // not for int8 with 8 heads, whose S^T and O^T together would not fit the registers
-                constexpr bool kEarlyO = !(KVT == 2 && QGP == 8);
+                constexpr bool kEarlyO = KVT == 1;  // int8 folds O^T only when its max moves
                 const bool early_o = kEarlyO && have_prev && mbar_test(&o_full[gi], uint32_t(k_own >> 1) & 1);
                 if (early_o) load_o();
                 float ks = 1.f, vs = 0.f;
@@ -936,10 +965,34 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     pr[g] = sc[g] > 0.5f * NEG_BIG ? exp2f(sc[g] - m[g]) : 0.f;
                     lsum[g] += pr[g];
                 }
-                const float vscale_cur = KVT == 2 ? unit_vsmax[qb * UM_UCH + min(c - c0, UM_UCH - 1)] : 0.f;
-                // The group's Phat buffer was last read by the PV product of its previous chunk: fold that
-                // chunk's O first (this also waits for that product), then overwrite.
-                if (have_prev) fold_prev(k_own, early_o);
+                // int8: probabilities relative to the unit's largest V scale, constant over the unit
+                const float vscale_cur = KVT == 2 ? unit_vsmax[2 * UM_UCH + qb] : 0.f;
+                if constexpr (KVT == 1) {
+                    // The group's Phat buffer was last read by the PV product of its previous chunk: fold
+                    // that chunk's O first (this also waits for that product), then overwrite.
+                    if (have_prev) fold_prev(k_own, early_o);
+                } else {
+                    // int8: O^T accumulates in tensor memory over the group's chunks (int32, exact). The
+                    // group waits for its previous PV product (it read the Phat buffer about to be
+                    // overwritten), and folds the accumulator into the registers only when the running
+                    // max moved, since the accumulator is relative to the old max; this chunk's PV
+                    // product then restarts it.
+                    int restart = 1;
+                    if (have_prev) {
+                        if (!*s_abort && !mbar_wait_bounded(&o_full[gi], uint32_t(k_own >> 1) & 1, s_abort)) give_up();
+                        bool moved = false;  // group-uniform
+#pragma unroll
+                        for (int g = 0; g < QGP; ++g) moved |= m_prev[g] != m[g];
+                        if (moved) {
+                            fold_acc(vscale_cur);
+#pragma unroll
+                            for (int g = 0; g < QGP; ++g) o[g] *= exp2f(m_prev[g] - m[g]);
+                        } else {
+                            restart = 0;
+                        }
+                    }
+                    if (gt == 0) p_restart[gi] = restart;  // before this chunk's p_full arrival
+                }
                 uint8_t* pbuf = smem + C::P_OFF + gi * C::PBUF;
                 if constexpr (KVT == 1) {
                     const int col = (my_lane % 64) * 2, sb = my_lane / 64;
@@ -990,7 +1043,14 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&pt_free[qb]);  // the unit's scales are no longer read
             }
-            if (have_prev) fold_prev(k_own, false);
+            if (have_prev) {
+                if constexpr (KVT == 1) {
+                    fold_prev(k_own, false);
+                } else {
+                    if (!*s_abort && !mbar_wait_bounded(&o_full[gi], uint32_t(k_own >> 1) & 1, s_abort)) give_up();
+                    fold_acc(vscale_prev);
+                }
+            }
             // ---- unit end: the group's sums over its 128 tokens
             float L[QGP];
 #pragma unroll
