@@ -6,7 +6,8 @@ B200 HBM peak. Effective bytes are the reference's Workload::min_bytes (src/work
 and V of every live token, plus q and out. ``value`` is the whole-job GB/s (sum over ranks of
 bytes per step / the slowest rank's step time).
 
-Workloads (seeded synthetic data generated on the device):
+Workloads (kv_cache_bench_b200.workload; seeded synthetic data written on
+the device by the library's page write path, int8 by the reference-identical quantizer):
   1  f32, 1 x 32/8 heads x 128, context 512, page 16, 64-page pool
   2  f16, context 4096, page 32, 256-page pool, split-K partition 512
   3  int8 (default; --dtype f16 for the fp16 variant), context 32768, page 128, 512-page pool  [default]
@@ -18,14 +19,20 @@ Configs 1-3 are single-sequence steps; with --gpus N every rank runs its own rep
 scaling). Inputs of configs 1-3 fit in L2 (126 MB), so each timed step reads one of R pool copies in
 rotation (R * live bytes > 4 x L2); configs 4-5 are far larger than L2.
 
+``sharded`` (on by default for the single-sequence headline): configs 4 (f16, by sequence) and 5
+(int8 and f16, by KV head) measured at the same N in the same run, each step the decode kernel plus
+the NCCL all-gather and the reorder into global order, captured together in CUDA graphs.
+
 Timing: W warm-up steps, then exactly K steps between a barrier + synchronize on each side, timed
-with CUDA events on the launching stream; max over ranks. Single-GPU replica steps are submitted as
-CUDA-graph replays (one kernel launch per step). NVML samples SM clocks and throttle reasons during
-the timed region. ``e2e`` measures the same metric through the public API (PagedDecoder ->
+with CUDA events on the launching stream; max over ranks. Steps are CUDA-graph replays; every graph
+a timed run replays is captured before the timed region, and a short GPU spin ahead of the start
+event keeps host submission out of the measurement. NVML samples SM clocks and throttle reasons
+during the timed region. ``e2e`` measures the same metric through the public API (PagedDecoder ->
 kvb_paged_decode_async) with per-step host->device copies of the step's inputs (q, sequence
 lengths, block table) from pinned memory and a device->host read of the output; the KV pool is
 device-resident state (written when a page is written), and ``e2e_pool_upload`` additionally copies
-the whole pool every step. ``--impl reference`` times the reference's own CPU implementation
+the whole pool every step. ``parity`` compares the step's own output with the fp64 oracle (outside
+the timed region). ``--impl reference`` times the reference's own CPU implementation
 (oracle/_ref/kvb_ref_cpu, built from its src/reference.cpp and src/workload.hpp) on this host.
 """
 from __future__ import annotations
@@ -34,6 +41,7 @@ import argparse
 import json
 import math
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -45,11 +53,15 @@ sys.path.insert(0, ROOT)
 
 import numpy as np  # noqa: E402
 
+from kv_cache_bench_b200.workload import build_layout, config as workload, min_bytes  # noqa: E402,F401
+
 METRIC = "decode-step µs and effective KV-read GB/s per GPU vs B200 HBM peak"
 FALLBACK_HBM_GBS = 6650.0
+TOL = 2e-5  # the reference's kernel tolerance against the fp64 oracle (tests/gpu_tests.cpp:16)
+SPIN_CYCLES = 200_000  # ~0.1 ms of GPU spin ahead of a start event
 
 
-def parse_args():
+def parse_args(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
@@ -62,42 +74,17 @@ def parse_args():
     ap.add_argument("--part", type=int, default=None, help="override the split-K partition size")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--no-graph", action="store_true", help="launch every step from the host")
+    ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--sharded", default="auto",
+                    help="sharded configs measured after the headline: 'auto' (4:f16,5:i8,5:f16 when the headline "
+                         "is a single-sequence config), 'none', or a list like 4:f16,5:i8")
+    ap.add_argument("--sharded-s", type=float, default=1.5, help="timed seconds per sharded config, at most")
     ap.add_argument("--ramp-s", type=float, default=1.0, help="untimed load before warm-up (clock ramp)")
     ap.add_argument("--seqs", type=int, default=None,
                     help="keep only the first N sequences of the config (a smaller case for profilers)")
     ap.add_argument("--op", choices=["decode", "quantize", "scatter"], default="decode",
                     help="decode step (default) or the page write path in front of it (one GPU)")
-    return ap.parse_args()
-
-
-# ---------------------------------------------------------------------------------------------------
-# workloads
-
-def workload(cfg: int, dtype):
-    if cfg == 1:
-        w = dict(H=32, Hkv=8, D=128, kv="f32", lens=[512], page=16, pool_blocks=64, part=0, seed=1,
-                 shard="replica")
-    elif cfg == 2:
-        w = dict(H=32, Hkv=8, D=128, kv="f16", lens=[4096], page=32, pool_blocks=256, part=512, seed=2,
-                 shard="replica")
-    elif cfg == 3:
-        w = dict(H=32, Hkv=8, D=128, kv="i8", lens=[32768], page=128, pool_blocks=512, part=0, seed=3,
-                 shard="replica")
-    elif cfg == 4:
-        rng = np.random.default_rng(4)
-        lens = np.rint(np.exp(rng.uniform(math.log(512), math.log(32768), 64))).astype(int).tolist()
-        w = dict(H=32, Hkv=8, D=128, kv="f16", lens=lens, page=16, pool_slack=1.1, part=0, seed=4,
-                 shard="sequence")
-    else:
-        rng = np.random.default_rng(5)
-        lens = rng.integers(8192, 131072, 256, endpoint=True).tolist()
-        w = dict(H=64, Hkv=8, D=128, kv="f16", lens=lens, page=64, pool_slack=1.0, part=0, seed=5,
-                 shard="kv_head")
-    if dtype:
-        w["kv"] = dtype
-    w["cfg"] = cfg
-    return w
+    return ap.parse_args(argv)
 
 
 def describe(w):
@@ -107,9 +94,86 @@ def describe(w):
             f"page={w['page']}, tokens={toks}, max_len={max(w['lens'])}")
 
 
-def min_bytes(w, lens, Hkv, H):
-    elem = {"f32": 4, "f16": 2, "i8": 1}[w["kv"]]
-    return float(sum(lens)) * Hkv * w["D"] * 2 * elem + float(len(lens)) * H * w["D"] * 8
+def sharded_list(spec: str, headline: dict):
+    """(config, dtype) pairs of the sharded block."""
+    if spec == "none":
+        return []
+    if spec == "auto":
+        return [(4, "f16"), (5, "i8"), (5, "f16")] if headline["shard"] == "replica" else []
+    out = []
+    for item in spec.split(","):
+        c, _, d = item.partition(":")
+        out.append((int(c), d or None))
+    return out
+
+
+# ---------------------------------------------------------------------------------------------------
+# graph-replayed steps
+
+def graph_plan(n: int, per_graph: int):
+    """Sizes of the graphs a run of n steps replays, in order: whole graphs of per_graph steps, then
+    one graph of the remainder."""
+    full, rem = divmod(max(n, 0), per_graph)
+    return [per_graph] * full + ([rem] if rem else [])
+
+
+class StepRunner:
+    """Runs n steps as replays of captured CUDA graphs. prepare() captures every graph the given
+    step counts need; run() only replays and refuses to capture, so a timed run() holds no capture,
+    instantiation or eager warm-up step."""
+
+    def __init__(self, capture, replay, per_graph: int):
+        self.capture, self.replay, self.per_graph = capture, replay, per_graph
+        self.graphs = {}
+
+    def prepare(self, *counts):
+        for n in counts:
+            for size in graph_plan(n, self.per_graph):
+                if size not in self.graphs:
+                    self.graphs[size] = self.capture(size)
+
+    def run(self, n: int):
+        for size in graph_plan(n, self.per_graph):
+            g = self.graphs.get(size)
+            if g is None:
+                raise RuntimeError(f"graph of {size} steps was not prepared")
+            self.replay(g)
+
+    def release(self):
+        self.graphs.clear()
+
+
+def make_runner(torch, stream, step, per_graph: int):
+    def capture(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            step(0)  # the launch path warmed outside the capture
+            stream.synchronize()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(n):
+                    step(i)
+        stream.synchronize()
+        return g
+
+    def replay(g):
+        with torch.cuda.stream(stream):
+            g.replay()
+
+    return StepRunner(capture, replay, per_graph)
+
+
+def timed_run(torch, stream, runner, n: int):
+    """Device milliseconds of runner.run(n) on `stream`: a short spin first, so the start event is
+    reached only after the host has queued the replays behind it."""
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(SPIN_CYCLES)
+        e0.record()
+    runner.run(n)
+    with torch.cuda.stream(stream):
+        e1.record()
+    return e0, e1
 
 
 # ---------------------------------------------------------------------------------------------------
@@ -171,88 +235,18 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------------------------
-# device data
+# CPU baseline and checker (the reference's own implementation, or the oracle port when it was not
+# built). Everything here runs outside the timed regions.
 
-def build_layout(lens, page, slack, pool_blocks, rng):
-    nblk = [(int(l) + page - 1) // page for l in lens]
-    live = sum(nblk)
-    num_blocks = pool_blocks if pool_blocks else max(live, int(math.ceil(live * slack)))
-    num_blocks = max(num_blocks, live, 1)
-    perm = rng.permutation(num_blocks).astype(np.int32)
-    max_blocks = max(nblk) if nblk else 0
-    table = np.full((len(lens), max(max_blocks, 1)), -1, np.int32)
-    nxt = 0
-    for b, n in enumerate(nblk):
-        table[b, :n] = perm[nxt:nxt + n]
-        nxt += n
-    return table, num_blocks
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
 
-
-def make_pool(torch, num_blocks, hk, page, D, kv, gen, device):
-    """K or V pool [num_blocks][hk][page][D], values U(-1, 1); int8 quantized per (block, KV head) with
-    scale = absmax / 127 (the reference's symmetric scheme, src/reference.cpp:32-51)."""
-    shape = (num_blocks, hk, page, D)
-    if kv in ("f32", "f16"):
-        t = torch.empty(shape, dtype=torch.float32 if kv == "f32" else torch.float16, device=device)
-        step = max(1, (1 << 28) // (hk * page * D))
-        for b0 in range(0, num_blocks, step):
-            t[b0:b0 + step].uniform_(-1, 1, generator=gen)
-        return t, None
-    q8 = torch.empty(shape, dtype=torch.int8, device=device)
-    sc = torch.empty((num_blocks, hk), dtype=torch.float32, device=device)
-    step = max(1, (1 << 27) // (hk * page * D))
-    for b0 in range(0, num_blocks, step):
-        x = torch.empty((min(step, num_blocks - b0), hk, page, D), dtype=torch.float32, device=device)
-        x.uniform_(-1, 1, generator=gen)
-        amax = x.abs().amax(dim=(2, 3))
-        s = amax / 127.0
-        q8[b0:b0 + step] = torch.where(s[:, :, None, None] > 0, torch.round(x / s[:, :, None, None]),
-                                       torch.zeros_like(x)).clamp_(-127, 127).to(torch.int8)
-        sc[b0:b0 + step] = s
-    return q8, sc
-
-
-class Shard:
-    """What one rank holds and computes."""
-
-    def __init__(self, torch, w, rank, world, device, copies):
-        from kv_cache_bench_b200 import shard as sh
-        lens = list(w["lens"])
-        self.H, self.Hkv = w["H"], w["Hkv"]
-        self.seqs = list(range(len(lens)))
-        self.owned = None
-        if w["shard"] == "sequence" and world > 1:
-            self.owned = sh.lpt_assign(lens, world)
-            self.seqs = self.owned[rank]
-        if w["shard"] == "kv_head" and world > 1:
-            hk = sh.kv_head_ranges(w["Hkv"], world)[rank]
-            self.Hkv = len(hk)
-            self.H = w["H"] // world
-        self.lens = [lens[b] for b in self.seqs]
-        self.world, self.rank = world, rank
-        rng = np.random.default_rng(w["seed"] * 1000 + rank)
-        gen = torch.Generator(device=device)
-        gen.manual_seed(w["seed"] * 1000 + rank)
-        table, self.num_blocks = build_layout(self.lens, w["page"], w.get("pool_slack", 1.0), w.get("pool_blocks"),
-                                              rng)
-        D = w["D"]
-        self.q = torch.empty((len(self.lens), self.H, D), dtype=torch.float32, device=device).uniform_(-1, 1,
-                                                                                                         generator=gen)
-        self.table = torch.from_numpy(table).to(device)
-        self.seq_lens = torch.tensor(self.lens, dtype=torch.int32, device=device)
-        self.out = torch.empty_like(self.q)
-        self.pools = []
-        for _ in range(copies):
-            k, ks = make_pool(torch, self.num_blocks, self.Hkv, w["page"], D, w["kv"], gen, device)
-            v, vs = make_pool(torch, self.num_blocks, self.Hkv, w["page"], D, w["kv"], gen, device)
-            self.pools.append((k, v, ks, vs))
-        self.max_len = max(self.lens) if self.lens else 0
-        self.bytes = min_bytes(w, self.lens, self.Hkv, self.H)
-        self.live_pool_bytes = float(sum(self.lens)) * self.Hkv * D * 2 * {"f32": 4, "f16": 2, "i8": 1}[w["kv"]]
-
-
-# ---------------------------------------------------------------------------------------------------
-# CPU baseline (the reference's own implementation, or the oracle port when it was not built)
 
 def sample_lens(w, budget_tokens: int):
     """The first sequences of the workload, in order, up to `budget_tokens` tokens; the last one taken
@@ -310,8 +304,32 @@ def cpu_baseline(w, seconds: float = 12.0):
     ms, nbytes, threads, kind, impl = time_cpu_reference(w, lens, steps)
     sample = (f"{len(lens)} of {len(w['lens'])} sequences, {sum(lens)} of {total} tokens "
               f"({100.0 * sum(lens) / total:.1f}% of the step), {steps} timed steps after 1 warm-up")
-    return {"value": round(nbytes / (ms * 1e-3) / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": kind,
-            "ms_per_step": round(ms, 3), "sample": sample, "impl": impl}
+    return {"value": round(nbytes / (ms * 1e-3) / 1e9, 4), "unit": "GB/s", "cores": threads, "cpu": cpu_model(),
+            "kind": kind, "ms_per_step": round(ms, 3), "sample": sample, "impl": impl}
+
+
+def check_sequences(torch, s, out, picks, threads):
+    """max |gpu - oracle| over local sequences `picks` of DeviceStep `s`, whose output rows are
+    out[i]: the fp64 oracle (oracle/kvb_oracle.c, pinned to the reference's golden vectors) on the
+    very pages the kernel read, copied back from the device."""
+    import oracle
+    kvt = {"f32": oracle.F32, "f16": oracle.F16, "i8": oracle.I8}[s.kv]
+    worst = 0.0
+    for i in picks:
+        q, k, v, table, lens, ks, vs = s.sequence_pages(torch, i)
+        ref = oracle.paged_attention(q, k, v, table, lens, num_kv_heads=s.Hkv, page=s.page, kv_type=kvt,
+                                     k_scale=ks, v_scale=vs, threads=threads)
+        worst = max(worst, oracle.max_abs_diff(out[i:i + 1].cpu().numpy(), ref))
+    return worst
+
+
+def parity_picks(lens):
+    """Local sequences to check: the shortest and the longest (one sequence: itself)."""
+    if not lens:
+        return []
+    lo = min(range(len(lens)), key=lambda i: (lens[i], i))
+    hi = max(range(len(lens)), key=lambda i: (lens[i], -i))
+    return sorted({lo, hi})
 
 
 def run_reference_arm(args, w):
@@ -329,8 +347,8 @@ def run_reference_arm(args, w):
     value = round(nbytes / (ms * 1e-3) / 1e9, 4)
     sample = (f"{len(lens)} of {len(w['lens'])} sequences, {sum(lens)} of {total} tokens "
               f"({100.0 * sum(lens) / total:.1f}% of the step) per step, {steps} timed steps after 1 warm-up")
-    cb = {"value": value, "unit": "GB/s", "cores": threads, "kind": kind, "ms_per_step": round(ms, 3),
-          "sample": sample, "impl": impl}
+    cb = {"value": value, "unit": "GB/s", "cores": threads, "cpu": cpu_model(), "kind": kind,
+          "ms_per_step": round(ms, 3), "sample": sample, "impl": impl}
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
@@ -347,7 +365,8 @@ def run_torch_sdpa(args, w):
     contiguous, unpaged cache [1][Hkv][L][D] of the same shape and storage type, the G query heads of a
     KV head passed as G query rows so that K and V are read once per KV head, as in our kernel. Same
     metric and algorithmic bytes; pool copies rotated past 4 x L2; CUDA-graph replays of at least 64
-    steps. Single-sequence configs (1-3) with f32 or f16 storage (SDPA takes no int8 cache); rank 0."""
+    steps, captured before the timed region. Single-sequence configs (1-3) with f32 or f16 storage
+    (SDPA takes no int8 cache); rank 0."""
     import torch
     import torch.nn.functional as F
     from torch.nn.attention import SDPBackend, sdpa_kernel
@@ -390,40 +409,20 @@ def run_torch_sdpa(args, w):
         print(json.dumps({"impl": "torch-sdpa", "unavailable": "no SDPA backend ran this shape"}), flush=True)
         return
     name, be = chosen
-    per_graph = copies * max(1, math.ceil(64 / copies))
     stream = torch.cuda.Stream(dev)
-    graphs = {}
 
-    def graph_of(n):
-        if n not in graphs:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.stream(stream), sdpa_kernel(be):
-                F.scaled_dot_product_attention(q, ks[0], vs[0])
-                stream.synchronize()
-                with torch.cuda.graph(g, stream=stream):
-                    for i in range(n):
-                        F.scaled_dot_product_attention(q, ks[i % copies], vs[i % copies])
-            graphs[n] = g
-        return graphs[n]
+    def step(i):
+        with sdpa_kernel(be):
+            F.scaled_dot_product_attention(q, ks[i % copies], vs[i % copies])
 
-    def run_steps(n):
-        full, rem = divmod(n, per_graph)
-        with torch.cuda.stream(stream):
-            for _ in range(full):
-                graph_of(per_graph).replay()
-            if rem:
-                graph_of(rem).replay()
-
-    run_steps(max(args.warmup, 3))
+    runner = make_runner(torch, stream, step, copies * max(1, math.ceil(64 / copies)))
+    runner.prepare(max(args.warmup, 3), args.steps)
+    runner.run(max(args.warmup, 3))
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record()
-    run_steps(args.steps)
-    with torch.cuda.stream(stream):
-        e1.record()
+    e0, e1 = timed_run(torch, stream, runner, args.steps)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
+    runner.release()
     value = round(nbytes / (ms * 1e-3) / 1e9, 2)
     cfg = config_obj(w, None, 1)
     cfg.update({"layout": "contiguous [1][Hkv][L][D], G query rows per KV head", "sdpa_backend": name,
@@ -499,6 +498,7 @@ def run_write_path(args, w):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     stream.synchronize()
     with torch.cuda.stream(stream):
+        torch.cuda._sleep(SPIN_CYCLES)
         e0.record()
     for _ in range(args.steps):
         fn(a, stream.cuda_stream)
@@ -523,6 +523,154 @@ def run_write_path(args, w):
         "gpu_launches": args.steps}), flush=True)
 
 
+class Ctx:
+    """Process-wide pieces of one bench run: ranks, device, barrier, max-over-ranks reduction."""
+
+    def __init__(self, torch, dist, rank, world, device):
+        self.torch, self.dist, self.rank, self.world, self.device = torch, dist, rank, world, device
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def reduce(self, x: float, op: str = "max") -> float:
+        t = self.torch.tensor([float(x)], dtype=self.torch.float64, device=self.device)
+        if self.world > 1:
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX if op == "max" else self.dist.ReduceOp.SUM)
+        return float(t.item())
+
+
+def decoder_for(ctx, s, part, kernel):
+    """PagedDecoder and per-copy C arguments over DeviceStep `s`; the workspace sized and zeroed."""
+    import kv_cache_bench_b200 as kvb
+    from kv_cache_bench_b200.torch_ops import PagedDecoder
+    dec = PagedDecoder(ctx.device)
+    # nothing in the step loop writes the lengths or the block table: the kernel may read them while
+    # the previous step finishes
+    cargs = [dec.args(s.q, k, v, s.table, s.seq_lens, s.max_len, out=s.out, k_scale=ks, v_scale=vs,
+                      part_tokens=part, kernel=kernel, tables_ready=True) for (k, v, ks, vs) in s.pools]
+    need = max(kvb.paged_workspace_bytes(c) for c in cargs) if s.lens else 256
+    dec.workspace = ctx.torch.zeros(max(need, 256), dtype=ctx.torch.uint8, device=ctx.device)
+    return dec, cargs
+
+
+class Gather:
+    """The per-rank outputs of a sharded step put together in global order on every rank: one NCCL
+    all-gather, then a reorder (a row gather for sequence shards, a head interleave for KV-head
+    shards). Nothing for replicas and for one rank."""
+
+    def __init__(self, ctx, s, w):
+        from kv_cache_bench_b200 import shard as sh
+        torch = ctx.torch
+        self.ctx, self.s, self.w = ctx, s, w
+        self.mode = None if (ctx.world == 1 or w["shard"] == "replica") else w["shard"]
+        self.final = s.out
+        if self.mode == "sequence":
+            pad = max(len(o) for o in s.owned)
+            self.local = torch.zeros((pad, s.H, w["D"]), dtype=torch.float32, device=ctx.device)
+            self.gathered = torch.empty((ctx.world * pad, s.H, w["D"]), dtype=torch.float32, device=ctx.device)
+            self.gidx = torch.from_numpy(sh.sequence_gather_index(s.owned, pad)).to(ctx.device)
+            self.final = torch.empty((len(w["lens"]), w["H"], w["D"]), dtype=torch.float32, device=ctx.device)
+        elif self.mode == "kv_head":
+            self.gathered = torch.empty((ctx.world,) + tuple(s.out.shape), dtype=torch.float32, device=ctx.device)
+            self.final = torch.empty((len(w["lens"]), w["H"], w["D"]), dtype=torch.float32, device=ctx.device)
+
+    def __call__(self):
+        torch, dist = self.ctx.torch, self.ctx.dist
+        if self.mode == "sequence":
+            self.local[: self.s.out.shape[0]].copy_(self.s.out)
+            dist.all_gather_into_tensor(self.gathered, self.local)
+            torch.index_select(self.gathered, 0, self.gidx, out=self.final)
+        elif self.mode == "kv_head":
+            dist.all_gather_into_tensor(self.gathered, self.s.out)
+            self.final.copy_(self.gathered.permute(1, 0, 2, 3).reshape(self.final.shape))
+        return self.final
+
+    def global_row(self, i):
+        """Row of the gathered output that holds local sequence i's heads of this rank."""
+        b = self.s.seqs[i]
+        if self.mode == "kv_head":
+            h0 = self.s.kv_heads[0] * (self.w["H"] // self.w["Hkv"])
+            return self.final[b, h0:h0 + self.s.H]
+        return self.final[b]
+
+
+def measure(ctx, w, args, *, part, kernel, copies, with_clocks=None, max_seconds=None):
+    """Builds DeviceStep for `w` on this rank and times K decode steps (plus the gather when
+    sharded) as CUDA-graph replays. Returns a dict of the step, its pieces and the timings."""
+    import kv_cache_bench_b200 as kvb
+    from kv_cache_bench_b200.workload import DeviceStep
+    torch = ctx.torch
+    s = DeviceStep(torch, w, device=ctx.device, rank=ctx.rank, world=ctx.world, copies=copies)
+    dec, cargs = decoder_for(ctx, s, part, kernel)
+    gather = Gather(ctx, s, w)
+    stream = torch.cuda.Stream(ctx.device)
+    ws_ptr, ws_n = dec.workspace.data_ptr(), dec.workspace.numel()
+
+    def step(i):
+        if s.lens:
+            kvb.paged_decode_async(cargs[i % copies], ws_ptr, ws_n, stream.cuda_stream)
+        gather()
+
+    if gather.mode:  # the communicator is set up before any capture
+        with torch.cuda.stream(stream):
+            gather()
+        ctx.barrier()
+    # graphs of at least 64 steps (a whole number of pool rotations): consecutive launches inside a
+    # graph overlap through programmatic dependent launch, launches across two replays do not
+    per_graph = copies * max(1, math.ceil(64 / copies))
+    runner = make_runner(torch, stream, step, per_graph)
+    warm = max(args.warmup, 3)
+    steps = args.steps
+    runner.prepare(warm)
+    ctx.barrier()
+    t0 = time.time()
+    runner.run(warm)
+    ctx.barrier()
+    if max_seconds is not None:  # bound the timed run of a long step
+        per_step = ctx.reduce((time.time() - t0) / warm)
+        steps = int(max(5, min(args.steps, max_seconds / max(per_step, 1e-9))))
+    runner.prepare(steps)
+    if with_clocks is not None and args.ramp_s > 0:  # untimed clock ramp
+        runner.prepare(per_graph)
+        t_end = time.time() + args.ramp_s
+        while time.time() < t_end:
+            runner.run(per_graph)
+            stream.synchronize()
+        runner.run(warm)
+    ctx.barrier()
+    if with_clocks is not None:
+        with_clocks.active(True)
+    e0, e1 = timed_run(torch, stream, runner, steps)
+    ctx.barrier()
+    if with_clocks is not None:
+        with_clocks.active(False)
+    ms_total = ctx.reduce(e0.elapsed_time(e1))
+    flag = dec.error_flag(stream) if s.lens else 0
+    runner.release()
+    ms_step = ms_total / max(steps, 1)
+    job_bytes = ctx.reduce(s.bytes, "sum")
+    return dict(s=s, dec=dec, gather=gather, stream=stream, ms_step=ms_step, steps=steps, job_bytes=job_bytes,
+                flag=int(ctx.reduce(flag)), part=kvb.paged_part_tokens(cargs[0]) if s.lens else part,
+                copies=copies)
+
+
+def sharded_parity(ctx, m, threads):
+    """Each rank checks its shortest and longest local sequences against the fp64 oracle, and that the
+    gathered global output holds its rows unchanged; the worst error over ranks."""
+    torch = ctx.torch
+    s, gather = m["s"], m["gather"]
+    picks = parity_picks(s.lens)
+    err = check_sequences(torch, s, s.out, picks, threads) if picks else 0.0
+    same = all(torch.equal(gather.global_row(i), s.out[i]) for i in picks)
+    err = ctx.reduce(err)
+    moved = ctx.reduce(0.0 if same else 1.0)
+    return {"max_abs": err, "tol": TOL, "gather_exact": moved == 0.0, "ok": err <= TOL and moved == 0.0,
+            "checked": f"shortest and longest sequence of each rank ({len(picks)} per rank), fp64 oracle on the pages "
+                       "the kernel read"}
+
+
 def main():
     args = parse_args()
     w = workload(args.config, args.dtype)
@@ -541,8 +689,6 @@ def main():
     import torch.distributed as dist
 
     import kv_cache_bench_b200 as kvb
-    from kv_cache_bench_b200 import shard as sh
-    from kv_cache_bench_b200.torch_ops import PagedDecoder
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -554,95 +700,17 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
+    ctx = Ctx(torch, dist, rank, world, device)
+    threads = max(1, (os.cpu_count() or 1) // world)
 
     # pool copies so that the data a step reads cycles through more than 4 x L2
     l2 = torch.cuda.get_device_properties(device).L2_cache_size
     elem = {"f32": 4, "f16": 2, "i8": 1}[w["kv"]]
     live_est = float(sum(w["lens"])) * w["Hkv"] * w["D"] * 2 * elem / (world if w["shard"] != "replica" else 1)
     copies = max(1, min(64, math.ceil(4 * l2 / max(live_est, 1)))) if w["shard"] == "replica" else 1
-    s = Shard(torch, w, rank, world, device, copies)
     kernel = {"auto": kvb.Kernel.auto, "simt": kvb.Kernel.simt, "mma": kvb.Kernel.mma,
               "umma": kvb.Kernel.umma}[args.kernel]
     part = w["part"] if args.part is None else args.part
-    dec = PagedDecoder(device)
-    stream = torch.cuda.Stream(device)
-
-    def c_args(i):
-        k, v, ks, vs = s.pools[i]
-        # nothing in the step loop writes the lengths or the block table: the kernel may read them
-        # while the previous step finishes
-        return dec.args(s.q, k, v, s.table, s.seq_lens, s.max_len, out=s.out, k_scale=ks, v_scale=vs,
-                        part_tokens=part, kernel=kernel, tables_ready=True)
-
-    cargs = [c_args(i) for i in range(copies)]
-    need = kvb.paged_workspace_bytes(cargs[0])
-    dec.workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=device)
-    ws_ptr, ws_n = dec.workspace.data_ptr(), dec.workspace.numel()
-    part_used = kvb.paged_part_tokens(cargs[0])
-
-    gathered = None
-    if world > 1 and w["shard"] == "sequence":
-        pad = max(len(o) for o in s.owned)
-        local_out = torch.zeros((pad, s.H, w["D"]), dtype=torch.float32, device=device)
-        gathered = torch.empty((world * pad, s.H, w["D"]), dtype=torch.float32, device=device)
-        gidx = torch.from_numpy(sh.sequence_gather_index(s.owned, pad)).to(device)
-    elif world > 1 and w["shard"] == "kv_head":
-        gathered = torch.empty((world,) + tuple(s.out.shape), dtype=torch.float32, device=device)
-    final = torch.empty((len(w["lens"]), w["H"], w["D"]), dtype=torch.float32, device=device)
-
-    def gather():
-        """All-gather of the per-rank outputs into `final` (global order); nothing for replicas."""
-        if gathered is None:
-            return s.out
-        with torch.cuda.stream(stream):
-            if w["shard"] == "sequence":
-                local_out[: s.out.shape[0]].copy_(s.out)
-                dist.all_gather_into_tensor(gathered, local_out)
-                torch.index_select(gathered, 0, gidx, out=final)
-            else:
-                dist.all_gather_into_tensor(gathered, s.out)
-                final.copy_(gathered.permute(1, 0, 2, 3).reshape(final.shape))
-        return final
-
-    def step(i):
-        kvb.paged_decode_async(cargs[i % copies], ws_ptr, ws_n, stream.cuda_stream)
-        gather()
-
-    use_graph = not args.no_graph and gathered is None
-    graphs = {}
-
-    def graph_of(n):
-        if n not in graphs:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.stream(stream):
-                step(0)  # warm the launch path outside capture
-                stream.synchronize()
-                with torch.cuda.graph(g, stream=stream):
-                    for i in range(n):
-                        step(i)
-            graphs[n] = g
-        return graphs[n]
-
-    # graphs of at least 64 steps (a whole number of pool rotations): consecutive launches inside a
-    # graph overlap through programmatic dependent launch, launches across two replays do not
-    per_graph = copies * max(1, math.ceil(64 / copies))
-
-    def run_steps(n):
-        if not use_graph:
-            for i in range(n):
-                step(i)
-            return
-        full, rem = divmod(n, per_graph)
-        with torch.cuda.stream(stream):
-            for _ in range(full):
-                graph_of(per_graph).replay()
-            if rem:
-                graph_of(rem).replay()
 
     try:  # NVML numbers devices physically; map through CUDA_VISIBLE_DEVICES
         nvml_index = torch.cuda._get_nvml_device_index(local)
@@ -650,42 +718,27 @@ def main():
         nvml_index = local
     clocks = ClockSampler(nvml_index)
     clocks.start()
-    clocks.active(True)
-    # untimed clock ramp, then warm-up
-    barrier()
-    t_end = time.time() + args.ramp_s
-    while time.time() < t_end:
-        run_steps(max(copies, 64))
-        stream.synchronize()
-    run_steps(args.warmup)
-    barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record()
-    run_steps(args.steps)
-    with torch.cuda.stream(stream):
-        e1.record()
-    barrier()
-    clocks.active(False)
+    m = measure(ctx, w, args, part=part, kernel=kernel, copies=copies, with_clocks=clocks)
     clocks.stop()
-    ms_total = e0.elapsed_time(e1)
-    flag = dec.error_flag(stream)
-    t = torch.tensor([ms_total], dtype=torch.float64, device=device)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_step = float(t.item()) / max(args.steps, 1)
-    byt = torch.tensor([s.bytes], dtype=torch.float64, device=device)
-    if world > 1:
-        dist.all_reduce(byt)
-    job_bytes = float(byt.item())
+    s, dec = m["s"], m["dec"]
+    ms_step, job_bytes = m["ms_step"], m["job_bytes"]
     value = job_bytes / (ms_step * 1e-3) / 1e9
 
-    # end to end through the public API with host buffers (single replica path and shards alike)
+    # end to end through the public API with host buffers
     e2e = e2e_pool = None
     if not args.no_e2e:
-        e2e, e2e_pool = measure_e2e(torch, dist, s, dec, part, kernel, stream, args, world, barrier, job_bytes, w,
-                                    gather)
+        e2e, e2e_pool = measure_e2e(torch, dist, s, dec, part, kernel, m["stream"], args, world, ctx.barrier,
+                                    job_bytes, w, m["gather"])
+
+    # parity of the step's own output (the checker, outside every timed region)
+    parity = None
+    if not args.no_parity:
+        if w["shard"] == "replica":
+            err = ctx.reduce(check_sequences(torch, s, s.out, parity_picks(s.lens), threads))
+            parity = {"max_abs": err, "tol": TOL, "ok": err <= TOL,
+                      "checked": "every sequence of the step, fp64 oracle on the pages the kernel read"}
+        else:
+            parity = sharded_parity(ctx, m, threads)
 
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -693,39 +746,63 @@ def main():
             cb = cpu_baseline(w)
         except Exception as ex:  # noqa: BLE001
             cb = {"value": None, "error": str(ex)[:200]}
+    per_gpu = s.bytes / (ms_step * 1e-3) / 1e9
+    part_used, flag = m["part"], m["flag"]
+    del m, s, dec
+    torch.cuda.empty_cache()
+
+    # the sharded configs at the same N
+    sharded = {}
+    peak, peak_kind = peak_hbm()
+    for cfg, dt in sharded_list(args.sharded, w):
+        ws = workload(cfg, dt)
+        ms_ = measure(ctx, ws, args, part=ws["part"], kernel=kernel, copies=1, max_seconds=args.sharded_s)
+        entry = {"workload": describe(ws), "parallelism": config_obj(ws, None, world)["parallelism"],
+                 "us_per_step": round(ms_["ms_step"] * 1e3, 3), "steps": ms_["steps"],
+                 "value": round(ms_["job_bytes"] / (ms_["ms_step"] * 1e-3) / 1e9, 2), "unit": "GB/s",
+                 "frac_of_n_peak": round(ms_["job_bytes"] / (ms_["ms_step"] * 1e-3) / 1e9 / (world * peak), 4),
+                 "part_tokens": ms_["part"], "error_flag": ms_["flag"],
+                 "step": "decode kernel + NCCL all-gather + reorder, one CUDA graph" if world > 1 else "decode kernel"}
+        if not args.no_parity:
+            entry["parity"] = sharded_parity(ctx, ms_, threads)
+        sharded[f"config{cfg}_{ws['kv']}"] = entry
+        del ms_
+        torch.cuda.empty_cache()
 
     if rank == 0:
-        peak, peak_kind = peak_hbm()
-        per_gpu = s.bytes / (ms_step * 1e-3) / 1e9
         traffic = read_traffic(w)
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "us_per_step": round(ms_step * 1e3, 3),
             "gbps_per_gpu": round(per_gpu, 2), "higher_is_better": True,
             "scaling": "weak" if w["shard"] == "replica" else "strong", "vs_baseline": None, "dtype": w["kv"],
-            "data": "synthetic: seeded U(-1,1) q/K/V generated on the device"
-                    + ("; int8 quantized per (page, KV head), scale = absmax/127" if w["kv"] == "i8" else ""),
+            "data": "synthetic: seeded U(-1,1) q and fp32 K/V generated on the device"
+                    + ("; int8 by the device quantizer (bit-identical to the reference's quantize_to_paged_i8)"
+                       if w["kv"] == "i8" else ""),
             "config": dict(config_obj(w, part_used, world),
-                           l2=(f"{copies} rotating pool copies ({copies * s.live_pool_bytes / 1e6:.0f} MB live "
+                           l2=(f"{copies} rotating pool copies ({copies * live_est / 1e6:.0f} MB live "
                                f"> 4 x L2 {l2 / 1e6:.0f} MB)" if copies > 1 else
-                               f"inputs {s.live_pool_bytes / 1e6:.0f} MB per GPU > L2 {l2 / 1e6:.0f} MB"),
-                           submission="cuda graph replay" if use_graph else "host launch per step",
+                               f"inputs {live_est / 1e6:.0f} MB per GPU > L2 {l2 / 1e6:.0f} MB"),
+                           submission="cuda graph replay, graphs captured before the timed region",
                            kernel=args.kernel),
             "roofline": {"bound": "hbm", "achieved": round(per_gpu, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(per_gpu / peak, 4), "peak_kind": peak_kind,
-                         "traffic": traffic, "algorithmic_bytes_per_launch": s.bytes,
+                         "traffic": traffic, "algorithmic_bytes_per_launch": min_bytes(w, w["lens"], w["Hkv"], w["H"]),
                          "note": "achieved = min_bytes per launch / device time per step (one decode kernel "
                                  "per step); peak = measured copy bandwidth"},
             "gpu_launches": args.steps, "error_flag": flag, "clocks": clocks.summary(),
         }
+        if parity:
+            line["parity"] = parity
         if e2e:
             line["e2e"] = e2e
         if e2e_pool:
             line["e2e_pool_upload"] = e2e_pool
         if cb:
             line["cpu_baseline"] = cb
+        if sharded:
+            line["sharded"] = sharded
         print(json.dumps(line), flush=True)
-    graphs.clear()
     if world > 1:
         dist.destroy_process_group()
 

@@ -221,10 +221,18 @@ int kvb_scatter_paged(const kvb_page_write_args* args, void* stream);
  * (different streams without ordering, or several host threads) race on it, so serialize them.
  * The array starts zeroed at module load, which is what its error word and split-K counters need;
  * every completed call leaves the counters ready for the next. Bad lengths or block ids give NaN
- * outputs as in kvb_paged_decode_async (the error word itself is not exposed here).
+ * outputs and set bits of the array's error word, as in kvb_paged_decode_async; read them with
+ * kvb_paged_static_error_flag. A call that reported a TIMEOUT (4) or STATE (8) bit can leave the
+ * counters stale, and the next call would then skip work: call kvb_paged_static_error_flag, which
+ * also resets them, before decoding again.
  * The first call on each device looks up the array's address and sets kernel attributes: make it
- * outside any stream capture. */
+ * outside any stream capture. Do not use the library across cudaDeviceReset. */
 int kvb_paged_decode_static(const kvb_paged_args* args, void* stream);
+
+/* kvb_paged_error_flag for the library-owned workspace of kvb_paged_decode_static on the current
+ * device (synchronizes `stream`): reads and clears its error word, and after a TIMEOUT or STATE
+ * bit resets its split-K and work counters. No counterpart in the reference. */
+int kvb_paged_static_error_flag(void* stream, int* flag);
 
 /* Reads and clears the error flag of a workspace (synchronizes `stream`). *flag = 0: no bad
  * length or block id since the last read. Bits: 1 bad length, 2 bad block id, 4 a bounded device

@@ -32,7 +32,7 @@ __all__ = [
     "NaiveArgs", "metal_available", "device_name", "run_paged", "run_paged_steps", "run_naive",
     "begin_pipelined", "end_pipelined", "run_read_bandwidth", "flush_gpu_caches", "Kernel",
     "paged_workspace_bytes", "paged_part_tokens", "paged_decode_async", "paged_error_flag",
-    "library_path", "lib",
+    "paged_decode_static", "paged_static_error_flag", "library_path", "lib",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -124,6 +124,8 @@ _c_scatter = _sig("kvb_scatter_paged", ctypes.c_int, ctypes.POINTER(_CPageWriteA
 _c_decode_static = _sig("kvb_paged_decode_static", ctypes.c_int, ctypes.POINTER(_CPagedArgs), ctypes.c_void_p)
 _c_error_flag = _sig("kvb_paged_error_flag", ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                      ctypes.POINTER(ctypes.c_int))
+_c_static_error_flag = _sig("kvb_paged_static_error_flag", ctypes.c_int, ctypes.c_void_p,
+                            ctypes.POINTER(ctypes.c_int))
 
 
 def _check(rc: int, what: str) -> None:
@@ -365,6 +367,14 @@ def paged_decode_async(c: _CPagedArgs, workspace: int, workspace_bytes: int, str
 def paged_decode_static(c: _CPagedArgs, stream: int = 0) -> None:
     """kvb_paged_decode_static: one decode step with the library-owned workspace (no allocation)."""
     _check(_c_decode_static(ctypes.byref(c), stream or None), "paged_decode_static")
+
+
+def paged_static_error_flag(stream: int = 0) -> int:
+    """kvb_paged_static_error_flag: reads and clears the library-owned workspace's error word on the
+    current device (and resets its counters after a TIMEOUT or STATE bit)."""
+    f = ctypes.c_int()
+    _check(_c_static_error_flag(stream or None, ctypes.byref(f)), "paged_static_error_flag")
+    return f.value
 
 
 STATIC_WORKSPACE_BYTES = 16 << 20

@@ -269,9 +269,18 @@ struct State {
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> timed;
 };
 
+// One state per device: the reference's API is single-device, and a caller that switches devices
+// (cudaSetDevice) gets that device's own stream, workspace and pipeline.
+constexpr int kMaxStateDevices = 64;
+
 State& st() {
-    static State s;
-    return s;
+    static State s[kMaxStateDevices];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        dev = 0;
+    }
+    return s[dev >= 0 && dev < kMaxStateDevices ? dev : 0];
 }
 
 int ensure_ready(State& S) {
@@ -536,23 +545,15 @@ int kvb_scatter_paged(const kvb_page_write_args* args, void* stream) { return pa
 static __device__ __align__(256) unsigned char g_static_workspace[KVB_STATIC_WORKSPACE_BYTES];
 
 // Device address of g_static_workspace on the current device, looked up once per device (with that
-// device current) and cached.
+// device current) and cached. The host-side name g_static_workspace is a stand-in, never a device
+// address: only the looked-up pointer is passed to kernels.
 int static_workspace(void** out) {
-    constexpr int kMaxDevices = 64;
-    static std::mutex mu;
-    static void* addr[kMaxDevices] = {};
-    int dev = 0;
-    KVB_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= kMaxDevices) return fail(KVB_ERR_DEVICE, "device ordinal out of range for the static workspace");
-    std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
-        void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_workspace);
-        if (e != cudaSuccess || !p)
-            return fail(KVB_ERR_DEVICE, std::string("static workspace address: ") + cudaGetErrorString(e));
-        addr[dev] = p;
-    }
-    *out = addr[dev];
+    static KvbPerDevice<void*> addr;
+    const cudaError_t e = addr.get(out, [](void** p) {
+        const cudaError_t r = cudaGetSymbolAddress(p, g_static_workspace);
+        return r == cudaSuccess && !*p ? cudaErrorInvalidSymbol : r;
+    });
+    if (e != cudaSuccess) return fail(KVB_ERR_DEVICE, std::string("static workspace address: ") + cudaGetErrorString(e));
     return KVB_OK;
 }
 
@@ -569,6 +570,16 @@ int kvb_paged_decode_static(const kvb_paged_args* a, void* stream) {
     void* ws = nullptr;
     if (int rc = static_workspace(&ws)) return rc;
     return launch_paged(a, ws, static_cast<cudaStream_t>(stream));
+}
+
+int kvb_paged_static_error_flag(void* stream, int* flag) {
+    if (!flag) return fail(KVB_ERR_INVALID, "null flag");
+    void* ws = nullptr;
+    if (int rc = static_workspace(&ws)) return rc;
+    unsigned h = 0;
+    if (int rc = read_clear_flag(ws, static_cast<cudaStream_t>(stream), &h)) return rc;
+    *flag = (int)h;
+    return KVB_OK;
 }
 
 int kvb_paged_error_flag(void* workspace, void* stream, int* flag) {

@@ -489,16 +489,17 @@ __global__ void __launch_bounds__(MMA_THREADS, 2)
 template <int KVT, int D, int QGM>
 cudaError_t launch_one(const DecodeParams& p, const CUtensorMap& tk, const CUtensorMap& tv, const LaunchInfo& li) {
     using C = MmaCfg<KVT, D>;
-    static int blocks_per_sm = 0;
-    if (!blocks_per_sm) {
-        cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<KVT, D, QGM>,
+    static KvbPerDevice<int> per_device;  // the shared-memory attribute and occupancy, per device
+    int blocks_per_sm = 0;
+    const cudaError_t e = per_device.get(&blocks_per_sm, [](int* n) {
+        cudaError_t r = cudaFuncSetAttribute(decode_mma_kernel<KVT, D, QGM>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, int(C::SMEM));
-        if (e != cudaSuccess) return e;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks_per_sm, decode_mma_kernel<KVT, D, QGM>,
-                                                          MMA_THREADS, C::SMEM);
-        if (e != cudaSuccess) return e;
-        if (blocks_per_sm < 1) blocks_per_sm = 1;
-    }
+        if (r != cudaSuccess) return r;
+        r = cudaOccupancyMaxActiveBlocksPerMultiprocessor(n, decode_mma_kernel<KVT, D, QGM>, MMA_THREADS, C::SMEM);
+        if (*n < 1) *n = 1;
+        return r;
+    });
+    if (e != cudaSuccess) return e;
     const long long upper = (long long)p.B * p.nhg * p.max_parts;
     const long long grid = std::min<long long>(upper, (long long)li.num_sms * blocks_per_sm);
     if (grid <= 0) return cudaSuccess;

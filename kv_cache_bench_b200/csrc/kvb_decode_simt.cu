@@ -242,13 +242,15 @@ __global__ void __launch_bounds__(SIMT_THREADS) decode_simt_kernel(const DecodeP
 
 template <int KVT, int D, int QGM>
 cudaError_t launch_one(const DecodeParams& p, const LaunchInfo& li) {
-    static int blocks_per_sm = 0;
-    if (!blocks_per_sm) {
-        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks_per_sm,
-                                                                     decode_simt_kernel<KVT, D, QGM>, SIMT_THREADS, 0);
-        if (e != cudaSuccess) return e;
-        if (blocks_per_sm < 1) blocks_per_sm = 1;
-    }
+    static KvbPerDevice<int> per_device;  // occupancy, per device
+    int blocks_per_sm = 0;
+    const cudaError_t e = per_device.get(&blocks_per_sm, [](int* n) {
+        const cudaError_t r =
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(n, decode_simt_kernel<KVT, D, QGM>, SIMT_THREADS, 0);
+        if (*n < 1) *n = 1;
+        return r;
+    });
+    if (e != cudaSuccess) return e;
     const long long upper = (long long)p.B * p.nhg * p.max_parts;
     const long long grid = std::min<long long>(upper, (long long)li.num_sms * blocks_per_sm);
     if (grid <= 0) return cudaSuccess;

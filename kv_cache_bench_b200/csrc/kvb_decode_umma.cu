@@ -1150,13 +1150,14 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
 template <int KVT, int QGP>
 cudaError_t launch_one(const DecodeParams& p, const CUtensorMap& tk, const CUtensorMap& tv, const LaunchInfo& li) {
     using C = UCfg<KVT>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(decode_umma_kernel<KVT, QGP>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(C::SMEM));
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    static KvbPerDevice<int> configured;  // the shared-memory attribute, set on each device
+    int done = 0;
+    cudaError_t e = configured.get(&done, [](int* v) {
+        *v = 1;
+        return cudaFuncSetAttribute(decode_umma_kernel<KVT, QGP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(C::SMEM));
+    });
+    if (e != cudaSuccess) return e;
     const long long upper = (long long)p.B * p.nhg * p.max_parts;
     const long long grid = std::min<long long>(upper, (long long)li.num_sms);
     if (grid <= 0) return cudaSuccess;

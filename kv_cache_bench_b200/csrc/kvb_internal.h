@@ -5,7 +5,45 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 #include <cuda_runtime.h>
+
+// A value set up once per device: kernel attributes (cudaFuncSetAttribute), occupancy and symbol
+// addresses belong to a device's context, so a process that launches on several devices needs each
+// of them once per device. get() runs `init(T*)` the first time it is called with a device current
+// and returns the cached value afterwards; safe to call from several host threads (the fast path is
+// one atomic load). Values do not survive cudaDeviceReset: the library must not be used across one.
+template <typename T>
+class KvbPerDevice {
+public:
+    template <typename F>
+    cudaError_t get(T* out, F&& init) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+        if (!ready_[dev].load(std::memory_order_acquire)) {
+            std::lock_guard<std::mutex> lock(mu_);
+            if (!ready_[dev].load(std::memory_order_relaxed)) {
+                T v{};
+                e = init(&v);
+                if (e != cudaSuccess) return e;
+                value_[dev] = v;
+                ready_[dev].store(true, std::memory_order_release);
+            }
+        }
+        *out = value_[dev];
+        return cudaSuccess;
+    }
+
+private:
+    static constexpr int kMaxDevices = 64;
+    std::mutex mu_;
+    std::atomic<bool> ready_[kMaxDevices] = {};
+    T value_[kMaxDevices] = {};
+};
 
 // Bounded device waits give up after this much wall time (the kernel then reports
 // KVB_DEVERR_TIMEOUT and returns instead of hanging the GPU).

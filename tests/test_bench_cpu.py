@@ -79,3 +79,46 @@ def test_sequence_cap_names_the_cut():
     w = bench.workload(5, "i8")
     w["lens"], w["cut"] = w["lens"][:16], True
     assert "first 16 sequences" in bench.describe(w) and "B=16" in bench.describe(w)
+
+
+@pytest.mark.parametrize("steps,warmup", [(20, 5), (2000, 20), (64, 0), (1, 3), (65, 64)])
+def test_timed_run_replays_only_prepared_graphs(steps, warmup):
+    """bench.py times K steps as replays of graphs captured beforehand: once prepare() has seen the
+    warm-up and step counts, run() of either count captures nothing (a capture inside the timed
+    region would time instantiation and an eager step along with the decode)."""
+    captured, replayed = [], []
+    runner = bench.StepRunner(capture=lambda n: captured.append(n) or ("graph", n),
+                              replay=lambda g: replayed.append(g[1]), per_graph=64)
+    runner.prepare(max(warmup, 3), steps)
+    before = list(captured)
+    runner.run(max(warmup, 3))
+    runner.run(steps)
+    assert captured == before  # nothing captured while running
+    assert sum(replayed) == max(warmup, 3) + steps
+    assert all(n <= 64 for n in replayed)
+
+
+def test_unprepared_run_refuses_to_capture():
+    runner = bench.StepRunner(capture=lambda n: n, replay=lambda g: None, per_graph=64)
+    runner.prepare(64)
+    with pytest.raises(RuntimeError, match="not prepared"):
+        runner.run(20)
+
+
+def test_graph_plan_covers_the_count():
+    for n in (0, 1, 63, 64, 65, 2000):
+        plan = bench.graph_plan(n, 64)
+        assert sum(plan) == n and all(0 < k <= 64 for k in plan)
+
+
+def test_sharded_block_configs():
+    assert bench.sharded_list("auto", bench.workload(3, None)) == [(4, "f16"), (5, "i8"), (5, "f16")]
+    assert bench.sharded_list("auto", bench.workload(4, None)) == []
+    assert bench.sharded_list("none", bench.workload(3, None)) == []
+    assert bench.sharded_list("5:i8", bench.workload(3, None)) == [(5, "i8")]
+
+
+def test_parity_picks_shortest_and_longest():
+    assert bench.parity_picks([]) == []
+    assert bench.parity_picks([7]) == [0]
+    assert bench.parity_picks([5, 9, 1, 9]) == [1, 2]
