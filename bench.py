@@ -546,10 +546,10 @@ def decoder_for(ctx, s, part, kernel):
     import kv_cache_bench_b200 as kvb
     from kv_cache_bench_b200.torch_ops import PagedDecoder
     dec = PagedDecoder(ctx.device)
-    # nothing in the step loop writes the lengths or the block table: the kernel may read them while
-    # the previous step finishes
+    # nothing in the step loop writes the lengths, the block table, q, the pools or the scales: the
+    # kernel may read them while the previous step finishes
     cargs = [dec.args(s.q, k, v, s.table, s.seq_lens, s.max_len, out=s.out, k_scale=ks, v_scale=vs,
-                      part_tokens=part, kernel=kernel, tables_ready=True) for (k, v, ks, vs) in s.pools]
+                      part_tokens=part, kernel=kernel, tables_ready=True, inputs_ready=True) for (k, v, ks, vs) in s.pools]
     need = max(kvb.paged_workspace_bytes(c) for c in cargs) if s.lens else 256
     dec.workspace = ctx.torch.zeros(max(need, 256), dtype=ctx.torch.uint8, device=ctx.device)
     return dec, cargs
@@ -841,9 +841,9 @@ def measure_e2e(torch, dist, s, dec, part, kernel, stream, args, world, barrier,
     result = gather()
     torch.cuda.synchronize()
     hout = torch.empty(result.shape, dtype=result.dtype, pin_memory=True)
-    # the lengths and the table arrive by host copy each step (no kernel writes them)
+    # the inputs arrive by host copy each step (no kernel writes them)
     cargs = [dec.args(q, k, v, table, lens, s.max_len, out=s.out, k_scale=ks, v_scale=vs, part_tokens=part,
-                      kernel=kernel, tables_ready=True) for (k, v, ks, vs) in s.pools]
+                      kernel=kernel, tables_ready=True, inputs_ready=True) for (k, v, ks, vs) in s.pools]
     need = max(kvb.paged_workspace_bytes(c) for c in cargs)
     if need > dec.workspace.numel():
         dec.workspace = torch.zeros(need, dtype=torch.uint8, device=s.q.device)
@@ -890,7 +890,7 @@ def measure_e2e(torch, dist, s, dec, part, kernel, stream, args, world, barrier,
         lens2 = stage2[off_l:off_l + l_b].view(torch.int32)
         table2 = stage2[off_t:off_t + t_b].view(torch.int32).view(s.table.shape)
         cargs2 = [dec.args(q2, k, v, table2, lens2, s.max_len, out=out2, k_scale=ks, v_scale=vs,
-                           part_tokens=part, kernel=kernel, tables_ready=True) for (k, v, ks, vs) in s.pools]
+                           part_tokens=part, kernel=kernel, tables_ready=True, inputs_ready=True) for (k, v, ks, vs) in s.pools]
         stages, outs, slot_args = (stage, stage2), (s.out, out2), (cargs, cargs2)
         houts = (hout, torch.empty(result.shape, dtype=result.dtype, pin_memory=True))
         s_in, s_out = torch.cuda.Stream(s.q.device), torch.cuda.Stream(s.q.device)

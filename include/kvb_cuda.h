@@ -95,6 +95,13 @@ typedef struct kvb_paged_args {
  *   instead of after it; q, the pools, the scales and the workspace are still read after it. A
  *   decode loop whose tables come from host copies, or that launches steps back to back, sets it. */
 #define KVB_FLAG_TABLES_READY 1
+/* KVB_FLAG_INPUTS_READY (with KVB_FLAG_TABLES_READY): q, the K/V pools and the int8 scales are not
+ *   written by the kernel launched right before this call on the same stream either. The
+ *   tensor-core kernel then streams the pages while that kernel finishes: each of its warps waits
+ *   for it only before its first access to the workspace or the output. Back-to-back decode steps,
+ *   and steps whose inputs arrive by host copy, set it; a step right after the kernel that appends
+ *   to the cache or computes q does not. */
+#define KVB_FLAG_INPUTS_READY 2
 
 /* src/metal_attn.hpp:71-80 (NaiveArgs): contiguous cache [B][Hkv][max_len][D], fp32 or fp16. */
 typedef struct kvb_naive_args {

@@ -76,6 +76,9 @@ class _CPagedArgs(ctypes.Structure):
 # kvb_paged_args.flags (include/kvb_cuda.h): the lengths and block table are not written by the kernel
 # launched right before the call on its stream, so the tensor-core kernel may read them early.
 FLAG_TABLES_READY = 1
+# ... and q, the pools and the scales are not written by it either (needs FLAG_TABLES_READY): the
+# tensor-core kernel streams the pages while that kernel finishes.
+FLAG_INPUTS_READY = 2
 
 
 class _CPageWriteArgs(ctypes.Structure):
@@ -338,12 +341,14 @@ def flush_gpu_caches() -> None:
 def device_args(shape: Shape, kv_type: KvType, page_size: int, max_blocks: int, max_len: int, *, q: int, k: int,
                 v: int, block_table: int, seq_lens: int, out: int, num_blocks: int, part_tokens: int = 0,
                 share_kv: bool = True, k_scale: int = 0, v_scale: int = 0,
-                kernel: Kernel = Kernel.auto, tables_ready: bool = False) -> _CPagedArgs:
-    """kvb_paged_args over raw device pointers (ints). tables_ready sets FLAG_TABLES_READY."""
+                kernel: Kernel = Kernel.auto, tables_ready: bool = False, inputs_ready: bool = False) -> _CPagedArgs:
+    """kvb_paged_args over raw device pointers (ints). tables_ready sets FLAG_TABLES_READY;
+    inputs_ready sets FLAG_INPUTS_READY as well."""
     return _CPagedArgs(shape._c(), int(kv_type), page_size, max_blocks, max_len, part_tokens, q or None, k or None,
                        v or None, block_table or None, seq_lens or None, out or None, 1 if share_kv else 0,
                        k_scale or None, v_scale or None, int(num_blocks), int(kernel),
-                       FLAG_TABLES_READY if tables_ready else 0)
+                       (FLAG_TABLES_READY if tables_ready or inputs_ready else 0)
+                       | (FLAG_INPUTS_READY if inputs_ready else 0))
 
 
 def paged_workspace_bytes(c: _CPagedArgs) -> int:

@@ -151,7 +151,9 @@ int check_static(const kvb_paged_args* a) {
     if (s.num_heads % s.num_kv_heads != 0) return fail(KVB_ERR_INVALID, "H % Hkv != 0");
     if (a->max_blocks < 0) return fail(KVB_ERR_INVALID, "max_blocks < 0");
     if (a->kernel < KVB_KERNEL_AUTO || a->kernel > KVB_KERNEL_UMMA) return fail(KVB_ERR_INVALID, "unknown kernel");
-    if (a->flags & ~KVB_FLAG_TABLES_READY) return fail(KVB_ERR_INVALID, "unknown flags");
+    if (a->flags & ~(KVB_FLAG_TABLES_READY | KVB_FLAG_INPUTS_READY)) return fail(KVB_ERR_INVALID, "unknown flags");
+    if ((a->flags & KVB_FLAG_INPUTS_READY) && !(a->flags & KVB_FLAG_TABLES_READY))
+        return fail(KVB_ERR_INVALID, "KVB_FLAG_INPUTS_READY needs KVB_FLAG_TABLES_READY");
     if (s.batch > 0 && (!a->q || !a->out || !a->seq_lens)) return fail(KVB_ERR_INVALID, "null q, out or seq_lens");
     if (s.batch > 0 && a->max_len > 0) {
         if (!a->k || !a->v || !a->block_table) return fail(KVB_ERR_INVALID, "null k, v or block_table");
@@ -230,6 +232,7 @@ int launch_paged(const kvb_paged_args* a, void* ws, cudaStream_t stream) {
     p.q_scale = 1.4426950408889634f / std::sqrt(float(s.head_dim));
     p.launch = next_launch_id();
     p.tables_ready = (a->flags & KVB_FLAG_TABLES_READY) != 0;
+    p.inputs_ready = (a->flags & KVB_FLAG_INPUTS_READY) != 0;
 
     if (g.kernel < 0)
         return fail(KVB_ERR_INVALID, "the requested tensor-core kernel does not support this shape, page size or dtype");
@@ -266,6 +269,7 @@ struct State {
     uint32_t flush_value = 0;
     bool pipelined = false;
     bool pipeline_checks = false;  // a run in the current pipeline needs its error flag checked
+    bool after_naive = false;      // the last kernel on the stream was the naive baseline (it writes an output)
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> timed;
 };
 
@@ -654,17 +658,22 @@ int kvb_run_paged(const kvb_paged_args* a, int steps, double* gpu_ms) {
     }
     cudaEvent_t e0, e1;
     if (int rc = begin_timed(S, &e0, &e1)) return rc;
-    // Nothing on the library's stream writes the lengths or the block table (uploads are host
-    // copies), so every step may read them while the previous one finishes.
+    // Kernels on the library's stream write no lengths, block tables, q, pools or scales (uploads
+    // are host copies; decode steps, flushes and the bandwidth probe write only their own outputs),
+    // so every step may read its inputs while the previous kernel finishes. After the naive baseline,
+    // whose output buffer a caller could pass as q, the first step reads q after it.
     kvb_paged_args ready = *a;
-    ready.flags |= KVB_FLAG_TABLES_READY;
+    ready.flags |= KVB_FLAG_TABLES_READY | KVB_FLAG_INPUTS_READY;
     for (int i = 0; i < steps; ++i) {
-        if (int rc = launch_paged(&ready, S.ws, S.stream)) {
+        kvb_paged_args step = ready;
+        if (i == 0 && S.after_naive) step.flags &= ~KVB_FLAG_INPUTS_READY;
+        if (int rc = launch_paged(&step, S.ws, S.stream)) {
             cudaEventDestroy(e0);
             cudaEventDestroy(e1);
             return rc;
         }
     }
+    if (steps > 0) S.after_naive = false;
     return end_timed(S, e0, e1, gpu_ms, true);
 }
 
@@ -702,6 +711,7 @@ int kvb_run_naive(const kvb_naive_args* a, double* gpu_ms) {
         if (int rc = prefetch(S, p, n)) return rc;
     cudaEvent_t e0, e1;
     if (int rc = begin_timed(S, &e0, &e1)) return rc;
+    S.after_naive = true;
     const cudaError_t e = kvb_launch_naive(a->q, a->k, a->v, a->seq_lens, a->out, static_cast<float*>(S.scores),
                                            s.batch, s.num_heads, s.num_kv_heads, s.head_dim, a->max_len, a->kv_type,
                                            S.stream);

@@ -337,6 +337,10 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     // one, so the unit enumeration and the producer's first block ids are read while that kernel
     // finishes; q, the pools, the scales and the workspace are read only after the wait.
     const bool early = p.tables_ready != 0;
+    // With inputs_ready as well, q, the pools and the scales are not written by the kernel before this
+    // one either: every read of them may come before the PDL wait, and each role waits only before its
+    // first access to the workspace or the output (wait_prev). The MMA warps touch neither.
+    const bool defer = early && p.inputs_ready != 0;
     if (!early) {
         pdl_wait();
         pdl_trigger();
@@ -347,6 +351,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         prefix = s_prefix;
     }
     const long long total = unit_total(p, prefix);
+    auto unit_of = [&](long long i, Unit& uu) { return unit_at(p, prefix, prefix ? s_lens : nullptr, i, uu); };
     const int lp = __ffs(p.page) - 1;  // pages are powers of two on this path
     // Block ids of a unit's pages into the page table (producer warp); refused ones (outside
     // [0, num_blocks)) become -2.
@@ -366,16 +371,23 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     if (early) {
         if (warp == UM_PRODUCER) {
             Unit u0;
-            if ((long long)blockIdx.x < total && unit_at(p, prefix, prefix ? s_lens : nullptr, blockIdx.x, u0) &&
+            if ((long long)blockIdx.x < total && unit_of(blockIdx.x, u0) &&
                 u0.nparts > 0) {
                 read_block_ids(u0);
                 ids_early = true;
             }
         }
-        pdl_wait();
+        if (!defer) pdl_wait();
         pdl_trigger();
     }
-    note_counter_count(p);
+    bool waited = !defer;  // this thread has passed the PDL wait
+    auto wait_prev = [&]() {
+        if (!waited) {
+            pdl_wait();
+            waited = true;
+        }
+    };
+    if (!defer) note_counter_count(p);
 
     auto give_up = [&]() {
         *s_abort = 1;
@@ -393,7 +405,19 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         unsigned* wc = work_counters(p);
         const bool dyn = total > (long long)gridDim.x;
         unsigned nxt = 0;
-        if (dyn && lane == 0) nxt = atomicAdd(&wc[0], 1u);
+        bool asked = false;
+        // The producer's first workspace access: the counter count, then (with more units than CTAs)
+        // the request for its second unit, made while its first one streams.
+        auto ask_next = [&]() {
+            if (asked) return;
+            asked = true;
+            if (!waited) {
+                wait_prev();
+                if (blockIdx.x == 0 && lane == 0) p.error_flag[1] = unsigned(p.B * p.nhg);
+            }
+            if (dyn && lane == 0) nxt = atomicAdd(&wc[0], 1u);
+        };
+        if (!defer) ask_next();
         int wpos = 0;
         auto publish = [&](int v) {
             const int e = wpos % UM_RQ;
@@ -417,7 +441,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         int unit_no = 0;
         int kp = 0;  // running chunk index
         for (;;) {
-            const bool real = idx < total && unit_at(p, prefix, prefix ? s_lens : nullptr, idx, u);
+            const bool real = idx < total && unit_of(idx, u);
             // A unit is published once its first chunk's loads are on their way (a tokenless one at once).
             if (real && u.nparts == 0) publish(int(idx));
             if (real && u.nparts > 0) {
@@ -429,6 +453,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 const int c0 = u.t0 / UM_CHUNK - (kp & 1), c1 = (u.t1 + UM_CHUNK - 1) / UM_CHUNK;
                 for (int c = c0; c < c1; ++c) {
                     const int tok0 = c * UM_CHUNK;
+                    if (kp == STAGES) ask_next();  // the ring is full: wait for the previous grid now
                     if (lane == 0 && !*s_abort && !mbar_wait_bounded(&empty[stage], phase ^ 1u, s_abort)) give_up();
                     __syncwarp();
                     // lane j < nbox owns box j (one page, or 128 rows of a larger page)
@@ -513,6 +538,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 ++unit_no;
             }
             // the next unit
+            ask_next();
             if (!dyn) break;
             long long nidx = 0;
             if (lane == 0) {
@@ -529,6 +555,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             if (nidx >= total) break;
             idx = nidx;
         }
+        ask_next();
         publish(-1);
     } else if (warp == UM_MMA0 || warp == UM_MMA1) {
         // ------------------------------------------------------------------ MMA issuers
@@ -570,7 +597,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                         units_done = true;
                         break;
                     }
-                    if (!unit_at(p, prefix, prefix ? s_lens : nullptr, v, u) || u.nparts == 0) continue;
+                    if (!unit_of(v, u) || u.nparts == 0) continue;
                     ++unit_no;
                     qb = unit_no & 1;
                     const int k_base = k_end;
@@ -684,7 +711,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         // The producer's first entry is unit blockIdx.x whenever that is a unit: it is taken without
         // waiting for the ring (which is on the first unit's critical path), and its entry is
         // consumed with the next one.
-        bool first = blockIdx.x < total && unit_at(p, prefix, prefix ? s_lens : nullptr, blockIdx.x, u);
+        bool first = blockIdx.x < total && unit_of(blockIdx.x, u);
         bool first_entry = first;
         for (int n = 0;; ++n) {
             // the next unit with tokens; units without tokens get their outputs here
@@ -698,12 +725,13 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                         ring_next();
                     }
                     const int v = ring_next();
-                    if (v < 0 || !unit_at(p, prefix, prefix ? s_lens : nullptr, v, u)) break;
+                    if (v < 0 || !unit_of(v, u)) break;
                 }
                 if (u.nparts > 0) {
                     more = true;
                     break;
                 }
+                wait_prev();
                 store_tokenless_unit<UM_D>(p, u, lane, 32);
             }
             const int qb = n & 1;
@@ -1052,6 +1080,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 }
             }
             // ---- unit end: the group's sums over its 128 tokens
+            wait_prev();  // the workspace and the output come next
             float L[QGP];
 #pragma unroll
             for (int g = 0; g < QGP; ++g) {

@@ -94,6 +94,7 @@ struct DecodeParams {
     float q_scale;     // log2(e) / sqrt(D): scores come out in log2 units
     unsigned launch;   // launch id (high bit set): tells this launch's counter values from stale ones
     int tables_ready;  // KVB_FLAG_TABLES_READY: lengths and block table may be read before the PDL wait
+    int inputs_ready;  // KVB_FLAG_INPUTS_READY (with tables_ready): q, pools and scales may be read before it too
 };
 
 // The page write path (kvb_pages.cu): a contiguous cache into the paged pool.

@@ -87,6 +87,12 @@ def test_flags_field_and_unknown_flags_refused():
     c.flags = kvb.FLAG_TABLES_READY | 0x10
     with pytest.raises(ValueError, match="unknown flags"):
         kvb.paged_workspace_bytes(c)
+    c.flags = kvb.FLAG_INPUTS_READY  # says more than FLAG_TABLES_READY, so needs it
+    with pytest.raises(ValueError, match="needs KVB_FLAG_TABLES_READY"):
+        kvb.paged_workspace_bytes(c)
+    c = kvb.device_args(kvb.Shape(1, 8, 2, 128), kvb.KvType.f16, 16, 4, 64, q=16, k=16, v=16, block_table=16,
+                        seq_lens=16, out=16, num_blocks=4, part_tokens=16, inputs_ready=True)
+    assert c.flags == kvb.FLAG_TABLES_READY | kvb.FLAG_INPUTS_READY
 
 
 def _c_layout(struct, fields):

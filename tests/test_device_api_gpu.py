@@ -67,16 +67,18 @@ def test_cuda_graph_replay():
                                           (oracle.I8, [8000, 0, 3, 5000, 129] * 8),
                                           (oracle.F16, [(i * 97) % 701 for i in range(300)])])
 def test_tables_ready_and_dynamic_units_are_bit_identical(kv_type, lens):
-    """FLAG_TABLES_READY (lengths and block ids read while the previous kernel finishes) and the
-    dynamic hand-out of units (far more units than CTAs here) change no bit of the output, over
+    """FLAG_TABLES_READY (lengths and block ids read while the previous kernel finishes),
+    FLAG_INPUTS_READY (pages streamed before it finishes) and the dynamic hand-out of units (far more
+    units than CTAs here) change no bit of the output, over
     repeated launches on one workspace (the work counters must come back to zero each time). The
     300-sequence case enumerates units densely (more sequences than the per-CTA prefix holds)."""
     case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=lens, kv_type=kv_type, page=64,
                             seed=11)
     d = _dev(case)
     dec = PagedDecoder()
-    outs = [_call(dec, d, case.max_len, part_tokens=512, tables_ready=ready).clone()
-            for ready in (False, True, True, False, True)]
+    flags = [dict(), dict(tables_ready=True), dict(tables_ready=True, inputs_ready=True), dict(),
+             dict(tables_ready=True, inputs_ready=True), dict(tables_ready=True)]
+    outs = [_call(dec, d, case.max_len, part_tokens=512, **f).clone() for f in flags]
     torch.cuda.synchronize()
     assert oracle.max_abs_diff(outs[0].cpu().numpy(), case.reference()) <= TOL
     for o in outs[1:]:
@@ -140,3 +142,48 @@ def test_host_path_refuses_bad_block_ids_before_launch():
     from tests.cuda_runner import run_case
     with pytest.raises(ValueError, match="block"):
         run_case(case)
+
+
+@pytest.mark.parametrize("kernel", [kvb.Kernel.simt, kvb.Kernel.mma, kvb.Kernel.umma])
+def test_stale_arrival_counter_reports_state_and_the_flag_read_resets_it(kernel):
+    """A split-K arrival counter left past its partition count (what an aborted launch or two
+    launches sharing one workspace leave behind) is planted in the workspace on the host: the next
+    launch reports STATE (8) instead of merging, kvb_paged_error_flag resets the counters, and the
+    launch after it is correct again."""
+    case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=[3000, 700], kv_type=oracle.F16,
+                            page=64, seed=9)
+    d = _dev(case)
+    dec = PagedDecoder()
+    ref = case.reference()
+    out = _call(dec, d, case.max_len, part_tokens=512, kernel=kernel)
+    torch.cuda.synchronize()
+    assert oracle.max_abs_diff(out.cpu().numpy(), ref) <= TOL and dec.error_flag() == 0
+    # counter of (sequence 0, head group 0): the clean epoch with 1000 arrivals already counted
+    dec.workspace[256:264].view(torch.int64).fill_((0x7FFFFFFF << 32) | 1000)
+    _call(dec, d, case.max_len, part_tokens=512, kernel=kernel)
+    torch.cuda.synchronize()
+    assert dec.error_flag() & 8
+    out = torch.full_like(d["q"], float("nan"))
+    _call(dec, d, case.max_len, part_tokens=512, kernel=kernel, out=out)
+    torch.cuda.synchronize()
+    assert oracle.max_abs_diff(out.cpu().numpy(), ref) <= TOL
+    assert dec.error_flag() == 0
+
+
+@pytest.mark.parametrize("kv_type,lens,part", [(oracle.I8, [32768], 0), (oracle.F16, [20000, 3000, 0, 129], 2048),
+                                               (oracle.I8, [9000, 9000, 4000], 0)])
+def test_single_wave_launches_with_inputs_ready_are_bit_identical(kv_type, lens, part):
+    """With FLAG_INPUTS_READY the pages stream before the previous kernel's end: back-to-back
+    launches on one workspace, each with one unit per CTA, give the oracle's result, bit-identical to
+    the launch without the flags."""
+    case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=lens, kv_type=kv_type, page=128,
+                            seed=13)
+    d = _dev(case)
+    dec = PagedDecoder()
+    base = _call(dec, d, case.max_len, part_tokens=part).clone()
+    outs = [_call(dec, d, case.max_len, part_tokens=part, tables_ready=True, inputs_ready=True) for _ in range(6)]
+    torch.cuda.synchronize()
+    assert oracle.max_abs_diff(base.cpu().numpy(), case.reference()) <= TOL
+    for o in outs:
+        assert torch.equal(o, base)
+    assert dec.error_flag() == 0

@@ -7,7 +7,9 @@ libkvbcuda.so. They generate their own seeded workloads, run the reference's fp6
 check the kernel: 846 checks (2e-5 kernel tolerance, fp16 and int8 storage bounds, per-query-head
 ablation) and 2051 length-boundary checks (empty sequences, page/partition boundaries, capacity,
 refusals before any device work, NaN-aware comparison). The reference published 0 failures for
-both on its Metal kernel (results/make-test.txt).
+both on its Metal kernel (results/make-test.txt). oracle/_ref/kvbench is its bench/bench.cpp, run
+for the read-bandwidth probe, a short sweep (pipelined timing with a cache flush before every
+rep, bench/bench.cpp:101-120) and the accuracy table.
 """
 import os
 import re
@@ -19,11 +21,11 @@ pytestmark = pytest.mark.gpu
 REF = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref")
 
 
-def _run(name, timeout):
+def _run(name, timeout, *args):
     exe = os.path.join(REF, name)
     if not os.path.exists(exe):
         pytest.skip(f"{exe} not built (the reference tree was absent at build time)")
-    p = subprocess.run([exe], capture_output=True, text=True, timeout=timeout)
+    p = subprocess.run([exe, *args], capture_output=True, text=True, timeout=timeout)
     return p.returncode, p.stdout + p.stderr
 
 
@@ -39,3 +41,41 @@ def test_reference_boundary_tests_pass_unchanged():
     print(out[-2000:])
     m = re.search(r"(\d+) checks, (\d+) failed", out)
     assert rc == 0 and m and int(m.group(1)) == 2051 and int(m.group(2)) == 0, out[-3000:]
+
+
+def _csv(out, header):
+    lines = [l for l in out.splitlines() if l and not l.startswith("#")]
+    assert lines and lines[0] == header, out[-2000:]
+    return [dict(zip(header.split(","), l.split(","))) for l in lines[1:]]
+
+
+def test_reference_kvbench_read_bandwidth_probe():
+    rc, out = _run("kvbench", 600, "--bw", "--reps=10")
+    print(out)
+    rows = _csv(out, "impl,bytes,reps,median_us,min_us,max_us,gbps")
+    assert rc == 0 and len(rows) == 1 and rows[0]["impl"] == "read_bw"
+    assert int(rows[0]["bytes"]) == 512 << 20 and float(rows[0]["gbps"]) > 1000  # B200 HBM, not a host copy
+
+
+def test_reference_kvbench_sweep_row():
+    rc, out = _run("kvbench", 900, "--lens=4096", "--pages=32", "--types=f16,i8", "--reps=10", "--cpu-reps=1")
+    print(out)
+    rows = _csv(out, "impl,dtype,batch,seq_len,page,part,reps,median_us,min_us,max_us,gbps,max_diff_vs_naive,kv_bytes")
+    assert rc == 0
+    impls = {(r["impl"], r["dtype"]) for r in rows}
+    assert {("gpu_naive", "f16"), ("cpu_ref_fp64", "f16"), ("gpu_paged", "f16"), ("gpu_paged", "i8")} <= impls
+    for r in rows:
+        assert float(r["median_us"]) > 0 and float(r["gbps"]) > 0
+        if r["impl"] == "gpu_paged" and r["dtype"] == "f16":
+            assert float(r["max_diff_vs_naive"]) <= 2e-5  # paged kernel vs the naive baseline on the same data
+
+
+def test_reference_kvbench_accuracy_table():
+    rc, out = _run("kvbench", 900, "--accuracy", "--lens=1024", "--pages=16,128")
+    print(out)
+    rows = _csv(out, "data,dtype,seq_len,page,max_abs_err,rms_err")
+    assert rc == 0 and len(rows) == 2 * 3 * 2  # uniform/varied x f32/f16/i8 x pages
+    for r in rows:
+        # against the fp32-data fp64 reference: f32 at kernel precision, f16 / i8 at their storage error
+        bound = {"f32": 2e-5, "f16": 5e-3, "i8": 5e-2}[r["dtype"]]
+        assert float(r["max_abs_err"]) <= bound, r

@@ -77,3 +77,25 @@ def test_static_workspace_refuses_oversize_before_launch():
         kvb.paged_decode_static(a, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     assert (out == 7.0).all()  # nothing was launched
+
+
+def test_static_error_word_is_read_and_cleared():
+    """kvb_paged_static_error_flag reads the library-owned workspace's error word: a refused length
+    (NaN outputs, bit 1) shows once and is cleared by the read; a correct call follows."""
+    case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=[900, 300], kv_type=oracle.I8,
+                            page=64, seed=23)
+    d = _dev(case)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert kvb.paged_static_error_flag(stream) == 0
+    d["lens"][1] = 100_000  # beyond max_len and the block table
+    out = torch.full_like(d["q"], 0.0)
+    kvb.paged_decode_static(_args(d, case.max_len, out), stream)
+    assert kvb.paged_static_error_flag(stream) & 1
+    assert kvb.paged_static_error_flag(stream) == 0
+    assert torch.isnan(out[1]).all()
+    d["lens"][1] = 300
+    out = torch.full_like(d["q"], float("nan"))
+    kvb.paged_decode_static(_args(d, case.max_len, out), stream)
+    torch.cuda.synchronize()
+    assert oracle.max_abs_diff(out.cpu().numpy(), case.reference()) <= TOL
+    assert kvb.paged_static_error_flag(stream) == 0
