@@ -163,6 +163,7 @@ int check_static(const kvb_paged_args* a) {
         return fail(KVB_ERR_INVALID, "q and out must be 16-byte aligned");
     if ((long long)s.batch * s.num_heads * s.head_dim > (1LL << 31))
         return fail(KVB_ERR_INVALID, "q/out larger than 2^31 elements");
+    if (s.num_heads > 65536) return fail(KVB_ERR_INVALID, "more than 65536 query heads");
     return KVB_OK;
 }
 
@@ -228,6 +229,13 @@ int launch_paged(const kvb_paged_args* a, void* ws, cudaStream_t stream) {
     p.max_len = a->max_len;
     p.part_tokens = g.part;
     p.max_parts = g.max_parts;
+    // work units are numbered below 2^31 and divided by these launch constants on the device
+    if ((long long)s.batch * g.nhg * g.max_parts >= (1LL << 31))
+        return fail(KVB_ERR_INVALID, "more than 2^31 split-K work units (batch x head groups x partitions)");
+    p.div_part = kvb_div_make((uint32_t)g.part);
+    p.div_gpk = kvb_div_make((uint32_t)g.gpk);
+    p.div_parts = kvb_div_make((uint32_t)g.max_parts);
+    p.div_seq = kvb_div_make((uint32_t)(g.nhg * g.max_parts));
     p.num_blocks = a->num_blocks;
     p.q_scale = 1.4426950408889634f / std::sqrt(float(s.head_dim));
     p.launch = next_launch_id();

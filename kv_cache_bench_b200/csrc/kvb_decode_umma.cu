@@ -216,8 +216,8 @@ struct UCfg {
     static constexpr size_t SLOT_QS_OFF = SLOT_UNIT_OFF + 2 * 64;             // [2][8] float
     static constexpr size_t XML_OFF = SLOT_QS_OFF + 2 * 8 * sizeof(float);    // [2 slots][2 groups][24] float
     static constexpr size_t XCNT_OFF = XML_OFF + 2 * 2 * 24 * sizeof(float);  // [2] int count, [2] int flags
-    static constexpr size_t RING_OFF = XCNT_OFF + 16;                         // [UM_RQ] unit indices
-    static constexpr size_t RESTART_OFF = RING_OFF + UM_RQ * sizeof(int);     // [2] int8 PV restarts O^T
+    static constexpr size_t RING_OFF = XCNT_OFF + 16;                         // [UM_RQ] decoded units (64 B)
+    static constexpr size_t RESTART_OFF = RING_OFF + UM_RQ * 64;              // [2] int8 PV restarts O^T
     static constexpr size_t SMEM = RESTART_OFF + 2 * sizeof(int) + 1024;
 };
 
@@ -227,6 +227,7 @@ static_assert(UCfg<1>::MISC_OFF % 64 == 0 && UCfg<2>::MISC_OFF % 64 == 0, "align
 static_assert(UCfg<1>::Q_OFF % 1024 == 0 && UCfg<1>::P_OFF % 1024 == 0 && UCfg<2>::P_OFF % 1024 == 0,
               "swizzled operands need 1024-byte alignment");
 static_assert(UCfg<2>::SCRATCH_FLOATS >= UM_THREADS, "prefix scan scratch");
+static_assert(UM_THREADS >= KVB_PREFIX_MAX, "one thread per sequence in the unit prefix");
 static_assert(sizeof(Unit) <= 64, "unit slot");
 
 template <int KVT, int QGP>  // QGP: query heads per group, padded to 1, 2, 4 or 8
@@ -265,7 +266,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     uint64_t* pt_free = q_full + 12;       // [2] int8 scale buffer read (softmax -> producer)
     uint64_t* r_full = q_full + 14;        // [UM_RQ] unit ring entry written (producer -> consumers)
     uint64_t* r_empty = r_full + UM_RQ;    // [UM_RQ] unit ring entry read (MMA issuers, Qhat warp)
-    int* s_ring = reinterpret_cast<int*>(smem + C::RING_OFF);
+    auto ring_at = [&](int e) -> Unit& { return *reinterpret_cast<Unit*>(smem + C::RING_OFF + 64 * e); };
     volatile int* p_restart = reinterpret_cast<volatile int*>(smem + C::RESTART_OFF);
     float* red = reinterpret_cast<float*>(smem + C::RED_OFF);
     int* pt_blk = reinterpret_cast<int*>(smem + C::WIN_OFF);
@@ -347,11 +348,15 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     }
     const int* prefix = nullptr;
     if (p.B <= KVB_PREFIX_MAX) {
-        build_unit_prefix(p, s_prefix, reinterpret_cast<int*>(scratch), tid, UM_THREADS, 1, s_lens);
+        build_unit_prefix_wide(p, s_prefix, reinterpret_cast<int*>(scratch), tid, UM_THREADS, 1, s_lens);
         prefix = s_prefix;
     }
     const long long total = unit_total(p, prefix);
     auto unit_of = [&](long long i, Unit& uu) { return unit_at(p, prefix, prefix ? s_lens : nullptr, i, uu); };
+    // The CTA's first unit is unit blockIdx.x (when that is a unit): decoded here once for every role.
+    // Later units are decoded by the producer alone and reach the other roles through the unit ring.
+    Unit u_first;
+    const bool has_first = (long long)blockIdx.x < total && unit_of(blockIdx.x, u_first);
     const int lp = __ffs(p.page) - 1;  // pages are powers of two on this path
     // Block ids of a unit's pages into the page table (producer warp); refused ones (outside
     // [0, num_blocks)) become -2.
@@ -369,13 +374,9 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     };
     bool ids_early = false;  // producer: the first unit's block ids are already in the page table
     if (early) {
-        if (warp == UM_PRODUCER) {
-            Unit u0;
-            if ((long long)blockIdx.x < total && unit_of(blockIdx.x, u0) &&
-                u0.nparts > 0) {
-                read_block_ids(u0);
-                ids_early = true;
-            }
+        if (warp == UM_PRODUCER && has_first && u_first.nparts > 0) {
+            read_block_ids(u_first);
+            ids_early = true;
         }
         if (!defer) pdl_wait();
         pdl_trigger();
@@ -419,14 +420,15 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         };
         if (!defer) ask_next();
         int wpos = 0;
-        auto publish = [&](int v) {
+        auto publish = [&](const Unit* uu) {  // nullptr ends the ring
             const int e = wpos % UM_RQ;
             if (lane == 0 && wpos >= UM_RQ && !*s_abort &&
                 !mbar_wait_bounded(&r_empty[e], ((wpos / UM_RQ) - 1) & 1, s_abort))
                 give_up();
             __syncwarp();
             if (lane == 0) {
-                s_ring[e] = v;
+                if (uu) ring_at(e) = *uu;
+                else ring_at(e).b = -1;
                 mbar_arrive(&r_full[e]);
             }
             ++wpos;
@@ -441,9 +443,15 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         int unit_no = 0;
         int kp = 0;  // running chunk index
         for (;;) {
-            const bool real = idx < total && unit_of(idx, u);
+            bool real;
+            if (unit_no == 0 && idx == (long long)blockIdx.x) {
+                real = has_first;
+                u = u_first;
+            } else {
+                real = idx < total && unit_of(idx, u);
+            }
             // A unit is published once its first chunk's loads are on their way (a tokenless one at once).
-            if (real && u.nparts == 0) publish(int(idx));
+            if (real && u.nparts == 0) publish(&u);
             if (real && u.nparts > 0) {
                 const int pg0 = u.t0 >> lp, pg1 = (u.t1 - 1) >> lp;  // the unit's pages (pg1 - pg0 < UM_PT)
                 const int npg = min(pg1 - pg0 + 1, UM_PT);
@@ -499,7 +507,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                             tma_load_2d(st + NSUB * TILE + off, &tmv, fb, x, y, policy);
                         }
                     }
-                    if (c == c0) publish(int(idx));
+                    if (c == c0) publish(&u);
                     if (scales_due) {
                         // the softmax warps are done with this scale buffer's previous unit
                         if (lane == 0 && unit_no >= 2 && !*s_abort &&
@@ -556,7 +564,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             idx = nidx;
         }
         ask_next();
-        publish(-1);
+        publish(nullptr);
     } else if (warp == UM_MMA0 || warp == UM_MMA1) {
         // ------------------------------------------------------------------ MMA issuers
         // Warp 9 issues the products of the even chunks (running index), warp 10 those of the odd
@@ -590,14 +598,15 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     // the next unit from the ring, once published (units without tokens are skipped)
                     const int e = rpos % UM_RQ;
                     if (!mbar_test(&r_full[e], uint32_t(rpos / UM_RQ) & 1)) break;
-                    const int v = s_ring[e];
+                    const Unit v = ring_at(e);
                     mbar_arrive(&r_empty[e]);
                     ++rpos;
-                    if (v < 0) {
+                    if (v.b < 0) {
                         units_done = true;
                         break;
                     }
-                    if (!unit_of(v, u) || u.nparts == 0) continue;
+                    if (v.nparts == 0) continue;
+                    u = v;
                     ++unit_no;
                     qb = unit_no & 1;
                     const int k_base = k_end;
@@ -697,21 +706,25 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         // with nparts < 0 ends the groups' loop. Units without tokens get their outputs here.
         Unit u;
         int rpos = 0;  // next unit ring entry
-        auto ring_next = [&]() {  // the next published unit index, -1 at the end (every lane)
+        auto ring_next = [&](Unit& uu) {  // the next published unit into uu (every lane); false at the end
             const int e = rpos % UM_RQ;
-            int v = -1;
+            int ok = 0;
             if (lane == 0) {
                 if (!*s_abort && !mbar_wait_bounded(&r_full[e], uint32_t(rpos / UM_RQ) & 1, s_abort)) give_up();
-                if (!*s_abort) v = s_ring[e];
-                mbar_arrive(&r_empty[e]);
+                ok = !*s_abort && ring_at(e).b >= 0;
             }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (ok) uu = ring_at(e);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&r_empty[e]);
             ++rpos;
-            return __shfl_sync(0xffffffffu, v, 0);
+            return ok != 0;
         };
         // The producer's first entry is unit blockIdx.x whenever that is a unit: it is taken without
         // waiting for the ring (which is on the first unit's critical path), and its entry is
         // consumed with the next one.
-        bool first = blockIdx.x < total && unit_of(blockIdx.x, u);
+        bool first = has_first;
+        if (first) u = u_first;
         bool first_entry = first;
         for (int n = 0;; ++n) {
             // the next unit with tokens; units without tokens get their outputs here
@@ -722,10 +735,10 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 } else {
                     if (first_entry) {
                         first_entry = false;
-                        ring_next();
+                        Unit skip;
+                        ring_next(skip);
                     }
-                    const int v = ring_next();
-                    if (v < 0 || !unit_of(v, u)) break;
+                    if (!ring_next(u)) break;
                 }
                 if (u.nparts > 0) {
                     more = true;
@@ -766,13 +779,16 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     const float x[4] = {xs[j].x * p.q_scale, xs[j].y * p.q_scale, xs[j].z * p.q_scale,
                                         xs[j].w * p.q_scale};
                     const float amax = warp_max(fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3]))));
-                    int e = 0;
-                    frexpf(amax, &e);
-                    const bool live = amax > 0.f && amax < 3.0e38f;
+                    // amax = f * 2^e with f in [0.5, 1), from the exponent bits; heads with amax below
+                    // 2^-90 have scores that round to 0 and are treated as zero, which keeps every
+                    // power of two below in range
+                    const int e = int((__float_as_uint(amax) >> 23) & 0xffu) - 126;
+                    const bool live = amax >= 8.0779356e-28f && amax < 3.0e38f;  // 2^-90
                     if constexpr (KVT == 1) {
                         // x * 2^(14 - e) in [-2^14, 2^14): hi + lo halves
-                        const float pre = live ? ldexpf(1.f, 14 - e) : 1.f;
-                        if (lane == 0) s_qs[qb * 8 + g] = 1.f / pre;
+                        // x * 2^(14 - e) and its inverse factor 2^(e - 14)
+                        const float pre = live ? __uint_as_float(uint32_t(127 + 14 - e) << 23) : 1.f;
+                        if (lane == 0) s_qs[qb * 8 + g] = live ? __uint_as_float(uint32_t(127 - 14 + e) << 23) : 1.f;
                         uint32_t hi[2], lo[2];
 #pragma unroll
                         for (int t = 0; t < 2; ++t) {
@@ -789,8 +805,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                             make_uint2(lo[0], lo[1]);
                     } else {
                         // integer x * 2^(30 - e) with |.| < 2^30, as four signed limbs
-                        const float pre = live ? ldexpf(1.f, 30 - e) : 1.f;
-                        if (lane == 0) s_qs[qb * 8 + g] = 1.f / pre;
+                        const float pre = live ? __uint_as_float(uint32_t(127 + 30 - e) << 23) : 1.f;
+                        if (lane == 0) s_qs[qb * 8 + g] = live ? __uint_as_float(uint32_t(127 - 30 + e) << 23) : 1.f;
                         // Limbs of element i packed in w[i] (byte 3 = limb 0 .. byte 0 = limb 3): adding 128
                         // to each of the three lower signed digits turns them into plain bytes (no
                         // carries), so the digits are the bytes of x + 0x808080 with those three flipped

@@ -224,6 +224,26 @@ __device__ __forceinline__ uint32_t i8cross_to_h2(uint32_t wa, uint32_t wb, uint
 
 // ---- work units ---------------------------------------------------------------------------------
 
+// n / f.d for 0 <= n < 2^31 (see KvbDiv).
+__device__ __forceinline__ int kvb_div(int n, const KvbDiv& f) { return int((__umulhi(unsigned(n), f.m) + unsigned(n)) >> f.l); }
+
+// n / d and n % d for 0 <= n < 2^31 and 1 <= d whose quotient is below 2^20: a float estimate within
+// one of n / d (the inputs, the reciprocal and the product are each rounded once, a relative error
+// below 2^-21 of a quotient below 2^20) and one correction step.
+__device__ __forceinline__ int div_small_quotient(int n, int d, int* rem) {
+    int q = __float2int_rz(__int2float_rn(n) * __frcp_rn(__int2float_rn(d)));
+    int r = n - q * d;
+    if (r < 0) {
+        --q;
+        r += d;
+    } else if (r >= d) {
+        ++q;
+        r -= d;
+    }
+    *rem = r;
+    return q;
+}
+
 // One work unit is one split-K partition [t0, t1) of one sequence b for one group of query heads
 // that share a KV head. Units are numbered sequence-major, then head group, then partition.
 struct Unit {
@@ -240,7 +260,7 @@ struct Unit {
 __device__ __forceinline__ int seq_partitions(const DecodeParams& p, int len, bool* bad) {
     *bad = len < 0 || len > p.max_len || (long long)len > (long long)p.max_blocks * p.page;
     if (*bad || len == 0) return 0;
-    return (len + p.part_tokens - 1) / p.part_tokens;
+    return kvb_div(len - 1, p.div_part) + 1;
 }
 
 __device__ __forceinline__ Unit make_unit(const DecodeParams& p, int b, int hg, int part, int len) {
@@ -250,9 +270,10 @@ __device__ __forceinline__ Unit make_unit(const DecodeParams& p, int b, int hg, 
     u.part = part;
     u.len = len;
     u.nparts = seq_partitions(p, len, &u.bad);
-    u.kvh = hg / p.gpk;
-    u.h0 = u.kvh * p.G + (hg % p.gpk) * p.qg;
-    u.nh = min(p.qg, p.G - (hg % p.gpk) * p.qg);
+    u.kvh = kvb_div(hg, p.div_gpk);
+    const int in_kvh = hg - u.kvh * p.gpk;  // head group within the KV head
+    u.h0 = u.kvh * p.G + in_kvh * p.qg;
+    u.nh = min(p.qg, p.G - in_kvh * p.qg);
     u.t0 = part * p.part_tokens;
     u.t1 = u.nparts ? min(len, u.t0 + p.part_tokens) : 0;
     return u;
@@ -266,6 +287,7 @@ __device__ __forceinline__ Unit make_unit(const DecodeParams& p, int b, int hg, 
 // partitions, which is no unit at all. `prefix` and `lens` as in UnitCursor.
 __device__ __forceinline__ bool unit_at(const DecodeParams& P, const int* prefix, const int* lens, long long idx,
                                         Unit& u) {
+    int b, hg, part, len;
     if (prefix) {
         // largest b with prefix[b] <= idx
         int lo = 0, hi = P.B - 1;
@@ -274,22 +296,21 @@ __device__ __forceinline__ bool unit_at(const DecodeParams& P, const int* prefix
             if (prefix[mid] <= idx) lo = mid;
             else hi = mid - 1;
         }
-        const int b = lo;
-        const int len = lens ? lens[b] : __ldg(P.seq_lens + b);
+        b = lo;
+        len = lens ? lens[b] : __ldg(P.seq_lens + b);
         bool bad;
         const int per = max(1, seq_partitions(P, len, &bad));
-        const int local = int(idx - prefix[b]);
-        u = make_unit(P, b, local / per, local % per, len);
-        return true;
+        hg = div_small_quotient(int(idx - prefix[b]), per, &part);
+    } else {
+        // unit indices stay below 2^31 (the host refuses larger launches)
+        b = kvb_div(int(idx), P.div_seq);
+        const int rem = int(idx) - b * int(P.div_seq.d);
+        hg = kvb_div(rem, P.div_parts);
+        part = rem - hg * P.max_parts;
+        len = __ldg(P.seq_lens + b);
+        bool bad;
+        if (part >= max(1, seq_partitions(P, len, &bad))) return false;
     }
-    const long long per_seq = (long long)P.nhg * P.max_parts;
-    const int b = int(idx / per_seq);
-    const int rem = int(idx % per_seq);
-    const int hg = rem / P.max_parts, part = rem % P.max_parts;
-    const int len = __ldg(P.seq_lens + b);
-    bool bad;
-    const int np = seq_partitions(P, len, &bad);
-    if (part >= max(1, np)) return false;
     u = make_unit(P, b, hg, part, len);
     return true;
 }
@@ -345,6 +366,36 @@ __device__ __forceinline__ void build_unit_prefix(const DecodeParams& p, int* pr
     named_barrier(bar_id, nthreads);
     const int off = scratch[tid];
     for (int b = s0; b < s1; ++b) prefix[b + 1] += off;
+    if (tid == 0) prefix[0] = 0;
+    named_barrier(bar_id, nthreads);
+}
+
+// build_unit_prefix for blocks with at least one thread per sequence (nthreads >= KVB_PREFIX_MAX, a
+// multiple of 32): thread b counts sequence b, each warp scans its 32 counts with shuffles, and each
+// thread adds the totals of the warps before its own. A few dozen instructions, against the slice
+// loops and the unrolled multi-round scan of the general form. `scratch` holds nthreads / 32 ints.
+__device__ __forceinline__ void build_unit_prefix_wide(const DecodeParams& p, int* prefix, int* scratch, int tid,
+                                                       int nthreads, uint32_t bar_id, int* lens_out) {
+    int v = 0;
+    if (tid < p.B) {
+        bool bad;
+        const int len = __ldg(p.seq_lens + tid);
+        lens_out[tid] = len;
+        v = p.nhg * max(1, seq_partitions(p, len, &bad));
+    }
+    const int lane = tid & 31, w = tid >> 5;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+    }
+    if (lane == 31) scratch[w] = incl;
+    named_barrier(bar_id, nthreads);
+    int off = 0;
+#pragma unroll 1
+    for (int i = 0; i < w; ++i) off += scratch[i];
+    if (tid < p.B) prefix[tid + 1] = off + incl;
     if (tid == 0) prefix[0] = 0;
     named_barrier(bar_id, nthreads);
 }

@@ -69,6 +69,22 @@ private:
 // Tokens per TMA stage of the tensor-core kernel.
 #define KVB_CHUNK 64
 
+// Division by an invariant divisor d in [1, 2^31) of numerators in [0, 2^31) with a multiply-high,
+// an add and a shift (T. Granlund, P. Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994): with l = ceil(log2 d) and m = floor(2^32 (2^l - d) / d) + 1,
+// n / d = (umulhi(n, m) + n) >> l; the sum stays below 2^32 because umulhi(n, m) < n < 2^31. The
+// kernels divide unit indices by launch constants this way (kvb_div in kvb_device.cuh).
+struct KvbDiv {
+    uint32_t d, m, l;
+};
+
+inline KvbDiv kvb_div_make(uint32_t d) {
+    uint32_t l = 0;
+    while ((1ull << l) < d) ++l;
+    const uint64_t m = ((1ull << 32) * ((1ull << l) - d)) / d + 1;
+    return KvbDiv{d, uint32_t(m), l};
+}
+
 // Everything a decode launch needs. Pointers are device pointers.
 struct DecodeParams {
     const float* q;          // [B][H][D]
@@ -95,6 +111,8 @@ struct DecodeParams {
     unsigned launch;   // launch id (high bit set): tells this launch's counter values from stale ones
     int tables_ready;  // KVB_FLAG_TABLES_READY: lengths and block table may be read before the PDL wait
     int inputs_ready;  // KVB_FLAG_INPUTS_READY (with tables_ready): q, pools and scales may be read before it too
+    // the launch's invariant divisors: part_tokens, gpk, max_parts, nhg * max_parts
+    KvbDiv div_part, div_gpk, div_parts, div_seq;
 };
 
 // The page write path (kvb_pages.cu): a contiguous cache into the paged pool.
