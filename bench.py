@@ -27,11 +27,13 @@ Timing: W warm-up steps, then exactly K steps between a barrier + synchronize on
 with CUDA events on the launching stream; max over ranks. Steps are CUDA-graph replays; every graph
 a timed run replays is captured before the timed region, and a short GPU spin ahead of the start
 event keeps host submission out of the measurement. NVML samples SM clocks and throttle reasons
-during the timed region. ``e2e`` measures the same metric through the public API (PagedDecoder ->
-kvb_paged_decode_async) with per-step host->device copies of the step's inputs (q, sequence
-lengths, block table) from pinned memory and a device->host read of the output; the KV pool is
-device-resident state (written when a page is written), and ``e2e_pool_upload`` additionally copies
-the whole pool every step. ``parity`` compares the step's own output with the fp64 oracle (outside
+during the timed region. ``e2e`` measures the same metric through the public API
+(kvb_paged_decode_async) with per-step host->device copies of the step's inputs (q, sequence
+lengths, block table) from pinned memory and a device->host read of the output, as a serving loop
+runs it: the copies and the launch of each step captured in CUDA graphs, the copies double-buffered
+on side streams; ``e2e_host_launch`` is the same with every copy and launch issued from the host
+each step. The KV pool is device-resident state (written when a page is written), and
+``e2e_pool_upload`` additionally copies the whole pool every step. ``parity`` compares the step's own output with the fp64 oracle (outside
 the timed region). ``--impl reference`` times the reference's own CPU implementation
 (oracle/_ref/kvb_ref_cpu, built from its src/reference.cpp and src/workload.hpp) on this host.
 """
@@ -725,10 +727,13 @@ def main():
     value = job_bytes / (ms_step * 1e-3) / 1e9
 
     # end to end through the public API with host buffers
-    e2e = e2e_pool = None
+    e2e = e2e_pool = e2e_launch = None
     if not args.no_e2e:
-        e2e, e2e_pool = measure_e2e(torch, dist, s, dec, part, kernel, m["stream"], args, world, ctx.barrier,
-                                    job_bytes, w, m["gather"])
+        e2e_launch, e2e_pool = measure_e2e(torch, dist, s, dec, part, kernel, m["stream"], args, world, ctx.barrier,
+                                           job_bytes, w, m["gather"])
+        e2e = e2e_launch
+        if m["gather"].mode is None:
+            e2e = measure_e2e_graph(torch, dist, s, dec, part, kernel, args, world, ctx.barrier, job_bytes)
 
     # parity of the step's own output (the checker, outside every timed region)
     parity = None
@@ -796,6 +801,8 @@ def main():
             line["parity"] = parity
         if e2e:
             line["e2e"] = e2e
+        if e2e_launch and e2e_launch is not e2e:
+            line["e2e_host_launch"] = e2e_launch
         if e2e_pool:
             line["e2e_pool_upload"] = e2e_pool
         if cb:
@@ -805,6 +812,107 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def measure_e2e_graph(torch, dist, s, dec, part, kernel, args, world, barrier, job_bytes):
+    """End to end as a serving loop runs decode steps: CUDA graphs of 64 steps, each step a
+    host->device copy of its inputs (q, sequence lengths, block table, one packed pinned buffer), the
+    kvb_paged_decode_async launch reading them where they landed, and the device->host copy of its
+    output into pinned memory. Two staging and two output buffers alternate; the input copies run on
+    one side stream and the readbacks on another, so step i+1's inputs land and step i-1's output
+    leaves while step i's kernel runs (graph edges keep every buffer's writer after its last reader).
+    Every timed step copies its inputs in and its output out. Replicas and one rank only."""
+    import kv_cache_bench_b200 as kvb
+
+    def align(n):
+        return (n + 255) // 256 * 256
+
+    dev = s.q.device
+    q_b, l_b, t_b = s.q.numel() * 4, s.seq_lens.numel() * 4, s.table.numel() * 4
+    off_l = align(q_b)
+    off_t = off_l + align(l_b)
+    total = off_t + t_b
+    host = torch.empty(total, dtype=torch.uint8, pin_memory=True)
+    host[:q_b].copy_(s.q.cpu().view(-1).view(torch.uint8))
+    host[off_l:off_l + l_b].copy_(s.seq_lens.cpu().view(-1).view(torch.uint8))
+    host[off_t:off_t + t_b].copy_(s.table.cpu().view(-1).view(torch.uint8))
+    stages = [torch.empty(total, dtype=torch.uint8, device=dev) for _ in range(2)]
+    outs = [torch.empty_like(s.out) for _ in range(2)]
+    houts = [torch.empty(s.out.shape, dtype=s.out.dtype, pin_memory=True) for _ in range(2)]
+    cargs = []
+    for b in range(2):
+        st = stages[b]
+        q = st[:q_b].view(torch.float32).view(s.q.shape)
+        lens = st[off_l:off_l + l_b].view(torch.int32)
+        table = st[off_t:off_t + t_b].view(torch.int32).view(s.table.shape)
+        cargs.append([dec.args(q, k, v, table, lens, s.max_len, out=outs[b], k_scale=ks, v_scale=vs,
+                               part_tokens=part, kernel=kernel, tables_ready=True, inputs_ready=True)
+                      for (k, v, ks, vs) in s.pools])
+    need = max(kvb.paged_workspace_bytes(c) for c in cargs[0])
+    if need > dec.workspace.numel():
+        dec.workspace = torch.zeros(need, dtype=torch.uint8, device=dev)
+    ws, wsn = dec.workspace.data_ptr(), dec.workspace.numel()
+    stream, s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    copies = len(s.pools)
+    per_graph = copies * max(1, math.ceil(64 / copies))
+    if per_graph % 2:
+        per_graph *= 2  # whole buffer pairs per graph
+
+    def capture(n):
+        with torch.cuda.stream(stream):  # warm the launch path outside the capture
+            kvb.paged_decode_async(cargs[0][0], ws, wsn, stream.cuda_stream)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        ev_in = [torch.cuda.Event() for _ in range(n)]
+        ev_k = [torch.cuda.Event() for _ in range(n)]
+        ev_out = [torch.cuda.Event() for _ in range(n)]
+        with torch.cuda.graph(g, stream=stream):
+            s_in.wait_stream(stream)
+            s_out.wait_stream(stream)
+            for i in range(n):
+                b = i & 1
+                with torch.cuda.stream(s_in):  # step i's inputs, once step i-2's kernel read the buffer
+                    if i >= 2:
+                        s_in.wait_event(ev_k[i - 2])
+                    stages[b].copy_(host, non_blocking=True)
+                    ev_in[i].record(s_in)
+                stream.wait_event(ev_in[i])
+                if i >= 2:  # step i-2's readback of this output buffer is done
+                    stream.wait_event(ev_out[i - 2])
+                kvb.paged_decode_async(cargs[b][i % copies], ws, wsn, stream.cuda_stream)
+                ev_k[i].record(stream)
+                with torch.cuda.stream(s_out):  # step i's output
+                    s_out.wait_event(ev_k[i])
+                    houts[b].copy_(outs[b], non_blocking=True)
+                    ev_out[i].record(s_out)
+            stream.wait_stream(s_in)
+            stream.wait_stream(s_out)
+        stream.synchronize()
+        return g
+
+    def replay(g):
+        with torch.cuda.stream(stream):
+            g.replay()
+
+    runner = StepRunner(capture, replay, per_graph)
+    n = max(args.steps, 1)
+    runner.prepare(per_graph, n)
+    runner.run(per_graph)
+    barrier()
+    e0, e1 = timed_run(torch, stream, runner, n)
+    barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / n], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    ok = torch.equal(houts[(n - 1) & 1], outs[(n - 1) & 1].cpu())
+    runner.release()
+    return {"value": round(job_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 6),
+            "h2d_bytes_per_step": int(total), "d2h_bytes_per_step": int(houts[0].numel() * 4), "steps": n,
+            "readback_matches_device": bool(ok),
+            "api": "kvb_paged_decode_async (C ABI) in CUDA graphs of %d steps: per step one packed pinned "
+                   "host->device input copy, the launch, one device->pinned host output copy; copies on two "
+                   "side streams, double-buffered" % per_graph}
 
 
 def measure_e2e(torch, dist, s, dec, part, kernel, stream, args, world, barrier, job_bytes, w, gather):

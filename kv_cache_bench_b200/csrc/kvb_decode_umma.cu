@@ -28,7 +28,7 @@
 //     probabilities (per chunk) are integers below 2^30 written as four signed 8-bit limbs,
 //     x = ((l0*256 + l1)*256 + l2)*256 + l3, so S and O come out as four exact int32 partial
 //     products recombined in fp32. The int8 scales are applied outside the MMA: k_scale to the
-//     scores, v_scale folded into the probability integers (relative to the chunk's largest scale).
+//     scores, v_scale folded into the probability integers (relative to the unit's largest scale).
 //   fp16 (kind::f16, fp32 accumulate): K and V are the stored halves; q and p are split as
 //     fp16(x) + fp16(x - fp16(x)) (about 22 significant bits), q prescaled per head by a power of two.
 // N = (limbs or halves) x (query heads, padded): int8 4 x {1,2,4,8} -> 8..32, fp16 2 x {4,8} -> 8, 16.
@@ -54,7 +54,8 @@ constexpr int UM_SOFT = 128;          // threads of one softmax group
 constexpr int UM_D = 128;             // head dim
 constexpr int TILE = UM_CHUNK * 128;  // bytes of one [128 rows][128 B] swizzled tile
 constexpr int UM_PT = 264;            // page-table entries: pages of one partition, at most
-constexpr int UM_UCH = 64;            // chunks of one partition, at most (partitions <= 8064 tokens)
+constexpr int UM_UCH = 64;            // chunks of one partition, at most (partitions <= 8064 tokens; the
+                                      // int8 O^T accumulator sums at most 64 chunks below 2^22 per limb)
 constexpr int UM_GRED = 144;          // reduction floats per softmax group
 constexpr int UM_TMEM_COLS = 256;     // tensor-memory columns of the CTA
 constexpr int UM_XCOL = 128;          // first column of the groups' unit shares
@@ -123,17 +124,38 @@ __device__ __forceinline__ void tc_st8(uint32_t taddr, const uint32_t (&r)[8]) {
 }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Shared-memory matrix descriptor: 128-byte swizzle, 1024-byte atoms (8 rows of 128 B).
-// lbo / sbo in bytes (leading: stride between 128-byte column groups of an MN-major operand;
-// stride: between 8-row groups).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+// Shared-memory matrix descriptor. Layout (swizzling mode): SWZ_128B, atoms of 8 rows of 128 B
+// (1024 B); SWZ_32B, atoms of 8 rows of 32 B (256 B). lbo / sbo in bytes (leading: stride between the
+// swizzle-width column groups of an MN-major operand; stride: between 8-row groups).
+constexpr uint64_t SWZ_128B = 2, SWZ_32B = 6;
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint64_t layout = SWZ_128B) {
     uint64_t d = 0;
     d |= (uint64_t)((addr >> 4) & 0x3FFF);
     d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
     d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
     d |= (uint64_t)1 << 46;  // descriptor version for sm_100
-    d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+    d |= layout << 61;
     return d;
+}
+
+// Phat^T (the PV product's B operand) is MN-major with the 32-byte swizzle: token t's row holds its
+// N probability values (int8 limbs or fp16 halves, in MMA column order) as 32 contiguous bytes at
+// byte 32 t, the two 16-byte halves exchanged for tokens with bit 2 set (address bit 4 XOR bit 7).
+// A thread writes its whole row with one or two vector stores. WORDS: 32-bit words written (1 .. 8).
+template <int WORDS>
+__device__ __forceinline__ void store_p_row(uint8_t* pbuf, int t, const uint32_t (&w)[WORDS]) {
+    uint8_t* row = pbuf + 32 * t;
+    const int x = ((t >> 2) & 1) * 16;
+    if constexpr (WORDS == 8) {
+        *reinterpret_cast<uint4*>(row + x) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(row + (16 ^ x)) = make_uint4(w[4], w[5], w[6], w[7]);
+    } else if constexpr (WORDS == 4) {
+        *reinterpret_cast<uint4*>(row + x) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else if constexpr (WORDS == 2) {
+        *reinterpret_cast<uint2*>(row + x) = make_uint2(w[0], w[1]);
+    } else {
+        *reinterpret_cast<uint32_t*>(row + x) = w[0];
+    }
 }
 
 // Instruction descriptor: D format (1 = f32, 2 = s32), A and B format (kind::f16: 0 = f16; kind::i8:
@@ -191,10 +213,9 @@ struct UCfg {
     static constexpr size_t Q_OFF = RING;                      // 2 Qhat buffers (1024-aligned)
     static constexpr size_t P_OFF = Q_OFF + 2 * QBUF;          // 2 Phat buffers
     static constexpr size_t BAD_OFF = P_OFF + 2 * PBUF;        // [STAGES] a block id of the chunk was refused
-    // int8: largest V scale of every chunk of a unit, [2 units][UM_UCH chunks]
+    // int8: the largest V scale of a unit's pages, [2 units]
     static constexpr size_t VSMAX_OFF = BAD_OFF + STAGES * sizeof(int);
-    // int8: and then the largest V scale of the whole unit, [2 units]
-    static constexpr size_t BAR_OFF = kvb_align_up(VSMAX_OFF + (KVT == 2 ? 2 * UM_UCH + 2 : 0) * sizeof(float), 64);
+    static constexpr size_t BAR_OFF = kvb_align_up(VSMAX_OFF + (KVT == 2 ? 2 : 0) * sizeof(float), 64);
     // full per (stage, chunk parity); empty per stage; q_full, q_free, s_full, s_free, p_full,
     // o_full, pt_free x2; r_full, r_empty x UM_RQ
     // unit ring: full and empty per entry
@@ -239,8 +260,11 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     constexpr int qgp = QGP;
     constexpr int RPH = KVT == 1 ? 2 : 4;  // rows of Qhat/Phat per head (halves or limbs)
     constexpr int N = RPH * qgp < 8 ? 8 : RPH * qgp;  // MMA N
+    // The PV product reads Phat^T MN-major, whose rows it takes in 16-byte units: an int8 row of 8
+    // values is padded to 16 (zero bytes, never written; the extra O^T columns are never read).
+    constexpr int NPV = (KVT == 2 && N < 16) ? 16 : N;
     // Probabilities are exp2(score - m) <= 2^kTau (lazy re-referencing). int8: p * v_scale / (largest
-    // v_scale of the chunk) * kPScale is an integer below 2^30; kPUnit = 1 / kPScale.
+    // v_scale of the unit) * kPScale is an integer below 2^30; kPUnit = 1 / kPScale.
     constexpr float kTau = KVT == 1 ? 8.f : 2.f;
     constexpr float kPScale = 268435456.f;          // 2^28 = 2^(30 - kTau) for int8
     constexpr float kPUnit = 3.7252902984619141e-09f;  // 2^-28
@@ -249,7 +273,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
     int* stage_bad = reinterpret_cast<int*>(smem + C::BAD_OFF);
-    float* unit_vsmax = reinterpret_cast<float*>(smem + C::VSMAX_OFF);  // int8: [2][UM_UCH]
+    float* unit_vsmax = reinterpret_cast<float*>(smem + C::VSMAX_OFF);  // int8: [2]
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
     // Chunk k (running index over the CTA's units) lives in stage k % STAGES and is announced on
     // full[k % (2 * STAGES)]: a stage alternates between even and odd chunks, whose consumers (MMA
@@ -514,28 +538,20 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                             !mbar_wait_bounded(&pt_free[sb], ((unit_no - 2) >> 1) & 1, s_abort))
                             give_up();
                         __syncwarp();
+                        // the unit's page scales, and the largest V scale among them (the probability
+                        // scale of the int8 O^T accumulator, constant over the unit)
                         float* ks_b = pt_ks + sb * UM_PT;
                         float* vs_b = pt_vs + sb * UM_PT;
+                        float vunit = 0.f;
                         for (int i = lane; i < npg; i += 32) {
                             const int b2 = pt_blk[i];
+                            const float vsi = b2 >= 0 ? __ldg(p.v_scale + (size_t)b2 * p.Hkv + u.kvh) : 0.f;
                             ks_b[i] = b2 >= 0 ? __ldg(p.k_scale + (size_t)b2 * p.Hkv + u.kvh) : 0.f;
-                            vs_b[i] = b2 >= 0 ? __ldg(p.v_scale + (size_t)b2 * p.Hkv + u.kvh) : 0.f;
+                            vs_b[i] = vsi;
+                            vunit = fmaxf(vunit, vsi);
                         }
-                        __syncwarp();
-                        // the largest V scale of each of the unit's chunks (an int8 probability scale bound)
-                        float* um = unit_vsmax + sb * UM_UCH;
-                        float vunit = 0.f;
-                        for (int j = lane; j < c1 - c0 && j < UM_UCH; j += 32) {
-                            const int a = max(((c0 + j) * UM_CHUNK) >> lp, pg0) - pg0;
-                            const int z = min((((c0 + j + 1) * UM_CHUNK - 1) >> lp), pg1) - pg0;
-                            float vmax = 0.f;
-                            for (int i = a; i <= z; ++i) vmax = fmaxf(vmax, vs_b[i]);
-                            um[j] = vmax;
-                            vunit = fmaxf(vunit, vmax);
-                        }
-                        // and the whole unit's (the int8 O^T accumulator's probability scale)
                         vunit = warp_max(vunit);
-                        if (lane == 0) unit_vsmax[2 * UM_UCH + sb] = vunit;
+                        if (lane == 0) unit_vsmax[sb] = vunit;
                         __syncwarp();  // every lane's scale writes happen before the arrive
                         if (lane == 0) mbar_arrive(fb);
                     }
@@ -579,7 +595,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             const uint32_t idesc_qk =
                 KVT == 1 ? instr_desc(1, 0, 0, 0, 0, N, 128) : instr_desc(2, 1, 1, 0, 0, N, 128);
             const uint32_t idesc_pv =
-                KVT == 1 ? instr_desc(1, 0, 0, 1, 0, N, 128) : instr_desc(2, 1, 0, 1, 0, N, 128);
+                KVT == 1 ? instr_desc(1, 0, 0, 1, 1, NPV, 128) : instr_desc(2, 1, 0, 1, 1, NPV, 128);
             constexpr int KQK = KVT == 1 ? 16 : 32;  // contraction elements per instruction
             const uint32_t s_tm = tmem + 32 * par, o_tm = tmem + 64 + 32 * par;
             const uint32_t pb = sbase + uint32_t(C::P_OFF) + par * C::PBUF;
@@ -635,11 +651,12 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
 #pragma unroll
                         for (int s = 0; s < UM_CHUNK / KQK; ++s) {
                             // V^T (MN-major): KQK token rows per instruction = KQK/8 atoms of 1024 B; the
-                            // second 64-dim slice of fp16 rows is the next tile (LBO).
+                            // second 64-dim slice of fp16 rows is the next tile (LBO). Phat^T (MN-major,
+                            // 32-byte swizzle): KQK token rows of 32 B, atoms of 8 rows 256 B apart.
                             const uint32_t voff = s * (KQK / 8) * 1024;
-                            const uint32_t poff = (s * 32 / 128) * (C::NMAX * 128) + (s * 32) % 128;
-                            tc_mma<KVT>(o_tm, smem_desc(vt + voff, TILE, 1024), smem_desc(pb + poff, 16, 1024),
-                                        idesc_pv, s > 0 || keep);
+                            const uint32_t poff = s * KQK * 32;
+                            tc_mma<KVT>(o_tm, smem_desc(vt + voff, TILE, 1024),
+                                        smem_desc(pb + poff, C::PBUF, 256, SWZ_32B), idesc_pv, s > 0 || keep);
                         }
                         tc_commit(&o_full[par]);
                         tc_commit(&empty[st]);  // K and V of chunk kk are no longer read
@@ -1010,7 +1027,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     lsum[g] += pr[g];
                 }
                 // int8: probabilities relative to the unit's largest V scale, constant over the unit
-                const float vscale_cur = KVT == 2 ? unit_vsmax[2 * UM_UCH + qb] : 0.f;
+                const float vscale_cur = KVT == 2 ? unit_vsmax[qb] : 0.f;
                 if constexpr (KVT == 1) {
                     // The group's Phat buffer was last read by the PV product of its previous chunk: fold
                     // that chunk's O first (this also waits for that product), then overwrite.
@@ -1039,14 +1056,19 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 }
                 uint8_t* pbuf = smem + C::P_OFF + gi * C::PBUF;
                 if constexpr (KVT == 1) {
-                    const int col = (my_lane % 64) * 2, sb = my_lane / 64;
+                    // this token's row of Phat^T: the hi halves of the heads, then the lo halves
+                    uint16_t h[2 * QGP];
 #pragma unroll
                     for (int g = 0; g < QGP; ++g) {
                         const __half hi = __float2half_rn(pr[g]);
                         const __half lo = __float2half_rn(pr[g] - __half2float(hi));
-                        *reinterpret_cast<__half*>(pbuf + sb * (C::NMAX * 128) + swz_off(g, col)) = hi;
-                        *reinterpret_cast<__half*>(pbuf + sb * (C::NMAX * 128) + swz_off(QGP + g, col)) = lo;
+                        h[g] = __half_as_ushort(hi);
+                        h[QGP + g] = __half_as_ushort(lo);
                     }
+                    uint32_t w[QGP];
+#pragma unroll
+                    for (int j = 0; j < QGP; ++j) w[j] = uint32_t(h[2 * j]) | uint32_t(h[2 * j + 1]) << 16;
+                    store_p_row<QGP>(pbuf, my_lane, w);
                     // fp16 V rows outside the partition may hold stale data or dead pool slots, or were
                     // never loaded: zero this token's V row so 0 * NaN cannot reach O.
                     if (!valid) {
@@ -1058,21 +1080,14 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                                 sts128_zero(smem_u32(vrow + sb2 * TILE + my_lane * 128 + ch * 16));
                     }
                 } else {
-                    // probability * v_scale / (largest v_scale of the chunk) as an unsigned integer below
-                    // 2^30 whose four bytes are the four limbs (byte 3 = limb 0). Four neighbouring
-                    // tokens exchange them so that lane c of each quad writes limb row c for all four
-                    // tokens as one 32-bit word.
+                    // probability * v_scale / (largest v_scale of the unit) as an unsigned integer below
+                    // 2^30 whose four bytes are the four limbs (byte 3 = limb 0); this token's row of
+                    // Phat^T holds head g's limbs 0..3 at bytes 4g..4g+3, so each word is byte-reversed.
                     const float f = vscale_cur > 0.f ? vs / vscale_cur * kPScale : 0.f;
-                    const int quad = lane & ~3, qc = lane & 3;
-                    const uint32_t sel = uint32_t(3 - qc) | (uint32_t(7 - qc) << 4);  // byte 3 - qc of a, of b
+                    uint32_t w[QGP];
 #pragma unroll
-                    for (int g = 0; g < QGP; ++g) {
-                        const uint32_t xi = __float2uint_rn(pr[g] * f);
-                        const uint32_t v0 = __shfl_sync(0xffffffffu, xi, quad), v1 = __shfl_sync(0xffffffffu, xi, quad + 1);
-                        const uint32_t v2 = __shfl_sync(0xffffffffu, xi, quad + 2), v3 = __shfl_sync(0xffffffffu, xi, quad + 3);
-                        const uint32_t w = __byte_perm(__byte_perm(v0, v1, sel), __byte_perm(v2, v3, sel), 0x5410);
-                        *reinterpret_cast<uint32_t*>(pbuf + swz_off(g * 4 + qc, (my_lane & ~3))) = w;
-                    }
+                    for (int g = 0; g < QGP; ++g) w[g] = __byte_perm(__float2uint_rn(pr[g] * f), 0u, 0x0123);
+                    store_p_row<QGP>(pbuf, my_lane, w);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -1176,7 +1191,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     }
                 }
                 // count the partition in; the last partition's CTA merges them all
-                finish_partition<UM_D, 20>(p, u, gt, UM_SOFT, gbar, &s_xcnt[2 + gi]);
+                finish_partition<UM_D, 12>(p, u, gt, UM_SOFT, gbar, &s_xcnt[2 + gi]);
             }
             // this warp is done with the unit's slot (its factors, both shares)
             tc_fence_before();
@@ -1223,7 +1238,7 @@ bool kvb_umma_supported(int kv_type, int D, int page, int qg, int part_tokens) {
     if (kv_type != 1 && kv_type != 2) return false;
     if (D != 128) return false;
     if (!(page == 8 || page == 16 || page == 32 || page == 64 || page == 128 || page == 256)) return false;
-    // a partition's pages and chunks must fit the page table and the per-chunk V scale bounds
+    // a partition's pages and chunks must fit the page table and the int8 O^T accumulator's bound
     // (part_tokens 0: the automatic size, at most 8064 tokens for pages of 32 tokens or more, 4096
     // for 16-token pages, 2048 for 8-token pages)
     if (part_tokens > 0 && (part_tokens / page + 2 > UM_PT || part_tokens > (UM_UCH - 1) * UM_CHUNK)) return false;
