@@ -233,7 +233,8 @@ class ClockSampler:
         if not self.nv:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples),
+                "window": "the last 0.25 s of the untimed load before the warm-up, the warm-up and the timed steps"}
 
 
 # ---------------------------------------------------------------------------------------------------
@@ -638,6 +639,10 @@ def measure(ctx, w, args, *, part, kernel, copies, with_clocks=None, max_seconds
         runner.prepare(per_graph)
         t_end = time.time() + args.ramp_s
         while time.time() < t_end:
+            # NVML samples every few ms: a short timed run (20 steps of config 3 last 0.4 ms) would see
+            # none, so sampling covers the last quarter second of this continuous load as well
+            if time.time() > t_end - 0.25:
+                with_clocks.active(True)
             runner.run(per_graph)
             stream.synchronize()
         runner.run(warm)
