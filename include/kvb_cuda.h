@@ -96,8 +96,8 @@ typedef struct kvb_paged_args {
  *   decode loop whose tables come from host copies, or that launches steps back to back, sets it. */
 #define KVB_FLAG_TABLES_READY 1
 /* KVB_FLAG_INPUTS_READY (with KVB_FLAG_TABLES_READY): q, the K/V pools and the int8 scales are not
- *   written by the kernel launched right before this call on the same stream either. The
- *   tensor-core kernel then streams the pages while that kernel finishes: each of its warps waits
+ *   written by the kernel launched right before this call on the same stream either. The tcgen05
+ *   and CUDA-core kernels then read the pages while that kernel finishes: each warp (thread) waits
  *   for it only before its first access to the workspace or the output. Back-to-back decode steps,
  *   and steps whose inputs arrive by host copy, set it; a step right after the kernel that appends
  *   to the cache or computes q does not. */

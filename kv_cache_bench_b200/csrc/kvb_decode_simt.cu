@@ -105,19 +105,31 @@ __global__ void __launch_bounds__(SIMT_THREADS) decode_simt_kernel(const DecodeP
 
     const int tid = threadIdx.x, lane = tid & 31, l16 = lane & 15;
     const int slot = tid >> 4;
-    pdl_wait();
+    // With KVB_FLAG_TABLES_READY and KVB_FLAG_INPUTS_READY, the lengths, block table, q, pools and
+    // scales are not written by the kernel before this one: they are read while it finishes, and
+    // each thread waits for it only before its first write (outputs, partials, split-K counters).
+    const bool defer = p.tables_ready && p.inputs_ready;
+    if (!defer) pdl_wait();
     pdl_trigger();
+    bool waited = !defer;
+    auto wait_prev = [&]() {
+        if (!waited) {
+            pdl_wait();
+            waited = true;
+        }
+    };
     const int* prefix = nullptr;
     if (p.B <= KVB_PREFIX_MAX) {
         build_unit_prefix(p, s_prefix, reinterpret_cast<int*>(s_slot_o), tid, SIMT_THREADS, 1);
         prefix = s_prefix;
     }
-    note_counter_count(p);
+    if (!defer) note_counter_count(p);
     UnitCursor cur{&p, prefix, (long long)blockIdx.x, unit_total(p, prefix)};
 
     Unit u;
     while (cur.advance(u)) {
         if (u.nparts == 0) {
+            wait_prev();
             store_tokenless_unit<D>(p, u, tid, SIMT_THREADS);
             continue;
         }
@@ -210,6 +222,7 @@ __global__ void __launch_bounds__(SIMT_THREADS) decode_simt_kernel(const DecodeP
                 }
             }
         }
+        wait_prev();  // the outputs, partials and counters come next
         if (bad) raise_error(p.error_flag, KVB_DEVERR_BLOCK);
         // Also the barrier after which the previous unit's epilogue buffers are free.
         const int unit_bad = __syncthreads_or(bad);
@@ -237,6 +250,10 @@ __global__ void __launch_bounds__(SIMT_THREADS) decode_simt_kernel(const DecodeP
         }
         finish_partition<D>(p, u, tid, SIMT_THREADS, 1, &s_flag);
         __syncthreads();
+    }
+    if (defer) {
+        wait_prev();
+        note_counter_count(p);
     }
 }
 

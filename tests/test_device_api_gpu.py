@@ -187,3 +187,22 @@ def test_single_wave_launches_with_inputs_ready_are_bit_identical(kv_type, lens,
     for o in outs:
         assert torch.equal(o, base)
     assert dec.error_flag() == 0
+
+
+@pytest.mark.parametrize("kv_type,page,lens", [(oracle.F32, 16, [512]), (oracle.F32, 7, [3000, 0, 130, 65]),
+                                               (oracle.I8, 48, [2000, 1, 700])])
+def test_cuda_core_kernel_with_inputs_ready_is_bit_identical(kv_type, page, lens):
+    """The CUDA-core kernel reads its inputs before the previous kernel ends when both early flags
+    are set and waits only before its writes: back-to-back launches give the oracle's result,
+    bit-identical to launches without the flags."""
+    case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=lens, kv_type=kv_type, page=page,
+                            seed=17)
+    d = _dev(case)
+    dec = PagedDecoder()
+    base = _call(dec, d, case.max_len, kernel=kvb.Kernel.simt).clone()
+    outs = [_call(dec, d, case.max_len, kernel=kvb.Kernel.simt, inputs_ready=True).clone() for _ in range(5)]
+    torch.cuda.synchronize()
+    assert oracle.max_abs_diff(base.cpu().numpy(), case.reference()) <= TOL
+    for o in outs:
+        assert torch.equal(o, base)
+    assert dec.error_flag() == 0
