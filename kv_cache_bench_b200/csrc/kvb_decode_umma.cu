@@ -307,9 +307,42 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     int* s_xcnt = reinterpret_cast<int*>(smem + C::XCNT_OFF);       // [slot] groups done, [group] flag
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // The unit enumeration starts with the sequence lengths and the block table: have them on the
-    // way to L2 while the CTA sets up (the table cooperatively across CTAs, when it is small).
-    if (tid < p.B && tid < KVB_PREFIX_MAX) prefetch_l2(p.seq_lens + tid);
+    const int lp = __ffs(p.page) - 1;  // pages are powers of two on this path
+    // With tables_ready the lengths and the block table are not written by the kernel before this
+    // one, so the unit enumeration and the producer's first block ids are read while that kernel
+    // finishes, and their reads start here, ahead of the setup.
+    const bool early = p.tables_ready != 0;
+    // The unit enumeration starts with the sequence lengths (prefix mode: thread b reads length b)
+    // and the block table: have them on the way while the CTA sets up (the table cooperatively
+    // across CTAs, when it is small).
+    int my_len = 0;
+    if (tid < p.B && tid < KVB_PREFIX_MAX) {
+        if (early) my_len = __ldg(p.seq_lens + tid);
+        else prefetch_l2(p.seq_lens + tid);
+    }
+    // The producer also guesses its first unit before the lengths arrive: unit blockIdx.x of the
+    // dense numbering (max_parts partitions for every sequence), which is the first unit whenever
+    // every sequence before it has max_parts partitions (a single sequence of max_len tokens, for
+    // one). It reads the guessed unit's block ids (up to 64 pages) at once, and uses them if the
+    // decoded first unit is the guessed one.
+    int g_b = -1, g_hg = 0, g_part = 0, g_npg = 0;
+    int g_ids[2] = {0, 0};
+    if (early && warp == UM_PRODUCER && (long long)blockIdx.x < (long long)p.B * p.div_seq.d) {
+        g_b = kvb_div(int(blockIdx.x), p.div_seq);
+        const int rem = int(blockIdx.x) - g_b * int(p.div_seq.d);
+        g_hg = kvb_div(rem, p.div_parts);
+        g_part = rem - g_hg * p.max_parts;
+        const int t0 = g_part * p.part_tokens;  // below max_len, as g_part < max_parts
+        const int t1 = min(p.max_len, t0 + p.part_tokens);
+        const int pg0 = t0 >> lp;
+        const int npg = min(((t1 - 1) >> lp) - pg0 + 1, p.max_blocks - pg0);
+        if (npg > 0 && npg <= 64) {
+            g_npg = npg;
+            const int* bt = p.block_table + (size_t)g_b * p.max_blocks + pg0;
+            if (lane < npg) g_ids[0] = __ldg(bt + lane);
+            if (lane + 32 < npg) g_ids[1] = __ldg(bt + lane + 32);
+        }
+    }
     {
         const size_t tb = (size_t)p.B * p.max_blocks * sizeof(int);
         if (tb <= (size_t(256) << 10))
@@ -358,11 +391,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     const uint32_t tmem = *s_tmem;
     // tensor-memory columns: S^T buffers at 0 and 32, O^T buffers at 64 and 96 (one per chunk parity),
     // the groups' shares of a unit at UM_XCOL + 8 * (2 * slot + group)
-    // With tables_ready the lengths and the block table are not written by the kernel before this
-    // one, so the unit enumeration and the producer's first block ids are read while that kernel
-    // finishes; q, the pools, the scales and the workspace are read only after the wait.
-    const bool early = p.tables_ready != 0;
-    // With inputs_ready as well, q, the pools and the scales are not written by the kernel before this
+    // With tables_ready alone, q, the pools, the scales and the workspace are read only after the
+    // PDL wait. With inputs_ready as well, q, the pools and the scales are not written by the kernel before this
     // one either: every read of them may come before the PDL wait, and each role waits only before its
     // first access to the workspace or the output (wait_prev). The MMA warps touch neither.
     const bool defer = early && p.inputs_ready != 0;
@@ -372,7 +402,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     }
     const int* prefix = nullptr;
     if (p.B <= KVB_PREFIX_MAX) {
-        build_unit_prefix_wide(p, s_prefix, reinterpret_cast<int*>(scratch), tid, UM_THREADS, 1, s_lens);
+        if (!early && tid < p.B) my_len = __ldg(p.seq_lens + tid);
+        build_unit_prefix_wide(p, s_prefix, reinterpret_cast<int*>(scratch), tid, UM_THREADS, 1, s_lens, my_len);
         prefix = s_prefix;
     }
     const long long total = unit_total(p, prefix);
@@ -381,25 +412,29 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     // Later units are decoded by the producer alone and reach the other roles through the unit ring.
     Unit u_first;
     const bool has_first = (long long)blockIdx.x < total && unit_of(blockIdx.x, u_first);
-    const int lp = __ffs(p.page) - 1;  // pages are powers of two on this path
     // Block ids of a unit's pages into the page table (producer warp); refused ones (outside
     // [0, num_blocks)) become -2.
+    auto table_entry = [&](int blk) { return blk < 0 || (long long)blk >= p.num_blocks ? -2 : blk; };
     auto read_block_ids = [&](const Unit& uu) {
         const int* bt = p.block_table + (size_t)uu.b * p.max_blocks;
         const int pg0 = uu.t0 >> lp, pg1 = (uu.t1 - 1) >> lp;
         const int npg = min(pg1 - pg0 + 1, UM_PT);  // the host keeps partitions within UM_PT pages
         __syncwarp();
-        for (int i = lane; i < npg; i += 32) {
-            int blk = __ldg(bt + pg0 + i);
-            if (blk < 0 || (long long)blk >= p.num_blocks) blk = -2;
-            pt_blk[i] = blk;
-        }
+        for (int i = lane; i < npg; i += 32) pt_blk[i] = table_entry(__ldg(bt + pg0 + i));
         __syncwarp();
     };
     bool ids_early = false;  // producer: the first unit's block ids are already in the page table
     if (early) {
         if (warp == UM_PRODUCER && has_first && u_first.nparts > 0) {
-            read_block_ids(u_first);
+            // the guess holds the unit's pages (its first page is the guess's, its last one no later)
+            if (g_npg > 0 && u_first.b == g_b && u_first.hg == g_hg && u_first.part == g_part) {
+                __syncwarp();
+                if (lane < g_npg) pt_blk[lane] = table_entry(g_ids[0]);
+                if (lane + 32 < g_npg) pt_blk[lane + 32] = table_entry(g_ids[1]);
+                __syncwarp();
+            } else {
+                read_block_ids(u_first);
+            }
             ids_early = true;
         }
         if (!defer) pdl_wait();

@@ -373,13 +373,13 @@ __device__ __forceinline__ void build_unit_prefix(const DecodeParams& p, int* pr
 // build_unit_prefix for blocks with at least one thread per sequence (nthreads >= KVB_PREFIX_MAX, a
 // multiple of 32): thread b counts sequence b, each warp scans its 32 counts with shuffles, and each
 // thread adds the totals of the warps before its own. A few dozen instructions, against the slice
-// loops and the unrolled multi-round scan of the general form. `scratch` holds nthreads / 32 ints.
+// loops and the unrolled multi-round scan of the general form. `scratch` holds nthreads / 32 ints;
+// `len` is thread tid's read of seq_lens[tid] (tid < B), which the caller may have started early.
 __device__ __forceinline__ void build_unit_prefix_wide(const DecodeParams& p, int* prefix, int* scratch, int tid,
-                                                       int nthreads, uint32_t bar_id, int* lens_out) {
+                                                       int nthreads, uint32_t bar_id, int* lens_out, int len) {
     int v = 0;
     if (tid < p.B) {
         bool bad;
-        const int len = __ldg(p.seq_lens + tid);
         lens_out[tid] = len;
         v = p.nhg * max(1, seq_partitions(p, len, &bad));
     }
