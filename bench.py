@@ -61,6 +61,8 @@ METRIC = "decode-step µs and effective KV-read GB/s per GPU vs B200 HBM peak"
 FALLBACK_HBM_GBS = 6650.0
 TOL = 2e-5  # the reference's kernel tolerance against the fp64 oracle (tests/gpu_tests.cpp:16)
 SPIN_CYCLES = 200_000  # ~0.1 ms of GPU spin ahead of a start event
+E2E_BUFS = 2  # input staging / output buffers of the graph-captured e2e loop
+STEADY_STEPS = 1000  # the longer run reported beside a short K-step run
 
 
 def parse_args(argv=None):
@@ -74,6 +76,11 @@ def parse_args(argv=None):
     ap.add_argument("--dtype", choices=["f32", "f16", "i8"], default=None)
     ap.add_argument("--kernel", choices=["auto", "simt", "mma", "umma"], default="auto")
     ap.add_argument("--part", type=int, default=None, help="override the split-K partition size")
+    ap.add_argument("--no-step-stream", action="store_true",
+                    help="leave KVB_FLAG_STEP_STREAM out of the timed steps (partitions sized for one step's "
+                         "latency instead of a stream of steps)")
+    ap.add_argument("--latency-reps", type=int, default=200,
+                    help="single steps timed alone, each after an L2 flush (0: none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
@@ -544,15 +551,16 @@ class Ctx:
         return float(t.item())
 
 
-def decoder_for(ctx, s, part, kernel):
+def decoder_for(ctx, s, part, kernel, step_stream):
     """PagedDecoder and per-copy C arguments over DeviceStep `s`; the workspace sized and zeroed."""
     import kv_cache_bench_b200 as kvb
     from kv_cache_bench_b200.torch_ops import PagedDecoder
     dec = PagedDecoder(ctx.device)
     # nothing in the step loop writes the lengths, the block table, q, the pools or the scales: the
-    # kernel may read them while the previous step finishes
+    # kernel may read them while the previous step finishes; the steps are a back-to-back stream
     cargs = [dec.args(s.q, k, v, s.table, s.seq_lens, s.max_len, out=s.out, k_scale=ks, v_scale=vs,
-                      part_tokens=part, kernel=kernel, tables_ready=True, inputs_ready=True) for (k, v, ks, vs) in s.pools]
+                      part_tokens=part, kernel=kernel, tables_ready=True, inputs_ready=True, step_stream=step_stream)
+             for (k, v, ks, vs) in s.pools]
     need = max(kvb.paged_workspace_bytes(c) for c in cargs) if s.lens else 256
     dec.workspace = ctx.torch.zeros(max(need, 256), dtype=ctx.torch.uint8, device=ctx.device)
     return dec, cargs
@@ -606,7 +614,7 @@ def measure(ctx, w, args, *, part, kernel, copies, with_clocks=None, max_seconds
     from kv_cache_bench_b200.workload import DeviceStep
     torch = ctx.torch
     s = DeviceStep(torch, w, device=ctx.device, rank=ctx.rank, world=ctx.world, copies=copies)
-    dec, cargs = decoder_for(ctx, s, part, kernel)
+    dec, cargs = decoder_for(ctx, s, part, kernel, not args.no_step_stream)
     gather = Gather(ctx, s, w)
     stream = torch.cuda.Stream(ctx.device)
     ws_ptr, ws_n = dec.workspace.data_ptr(), dec.workspace.numel()
@@ -654,13 +662,57 @@ def measure(ctx, w, args, *, part, kernel, copies, with_clocks=None, max_seconds
     if with_clocks is not None:
         with_clocks.active(False)
     ms_total = ctx.reduce(e0.elapsed_time(e1))
+    steady = None
+    if with_clocks is not None and steps < STEADY_STEPS:
+        # consecutive steps overlap, so a short run pays one pipeline fill and drain: the same steps
+        # over a longer run, reported beside the K-step figure
+        runner.prepare(STEADY_STEPS)
+        ctx.barrier()
+        f0, f1 = timed_run(torch, stream, runner, STEADY_STEPS)
+        ctx.barrier()
+        steady = ctx.reduce(f0.elapsed_time(f1)) / STEADY_STEPS
     flag = dec.error_flag(stream) if s.lens else 0
     runner.release()
     ms_step = ms_total / max(steps, 1)
     job_bytes = ctx.reduce(s.bytes, "sum")
     return dict(s=s, dec=dec, gather=gather, stream=stream, ms_step=ms_step, steps=steps, job_bytes=job_bytes,
+                steady_ms_step=steady,
                 flag=int(ctx.reduce(flag)), part=kvb.paged_part_tokens(cargs[0]) if s.lens else part,
                 copies=copies)
+
+
+def measure_latency(ctx, m, part, kernel, reps):
+    """One decode step with nothing in flight, as the reference times a run (its command buffer's GPU
+    time, caches flushed before every run): each step follows an L2 flush (a 256 MiB device write) and
+    is timed alone by events around its launch, without flags (partitions by the latency rule, every
+    read after the programmatic-launch wait). Median and minimum over `reps`, max over ranks."""
+    import kv_cache_bench_b200 as kvb
+    torch = ctx.torch
+    s, dec, stream = m["s"], m["dec"], m["stream"]
+    cargs = [dec.args(s.q, k, v, s.table, s.seq_lens, s.max_len, out=s.out, k_scale=ks, v_scale=vs,
+                      part_tokens=part, kernel=kernel) for (k, v, ks, vs) in s.pools]
+    need = max(kvb.paged_workspace_bytes(c) for c in cargs)
+    if need > dec.workspace.numel():
+        dec.workspace = torch.zeros(need, dtype=torch.uint8, device=ctx.device)
+    ws, wsn = dec.workspace.data_ptr(), dec.workspace.numel()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=ctx.device)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    with torch.cuda.stream(stream):
+        for i in range(3):  # warm the launch path
+            kvb.paged_decode_async(cargs[i % len(cargs)], ws, wsn, stream.cuda_stream)
+        for i, (e0, e1) in enumerate(ev):
+            flush.fill_(i & 0xff)
+            e0.record(stream)
+            kvb.paged_decode_async(cargs[i % len(cargs)], ws, wsn, stream.cuda_stream)
+            e1.record(stream)
+    stream.synchronize()
+    us = sorted(e0.elapsed_time(e1) * 1e3 for e0, e1 in ev)
+    med = ctx.reduce(us[len(us) // 2])
+    return {"us": round(med, 3), "min_us": round(ctx.reduce(us[0]), 3), "reps": reps,
+            "gbps": round(s.bytes / (med * 1e-6) / 1e9, 2), "part_tokens": kvb.paged_part_tokens(cargs[0]),
+            "flags": "none", "l2": "256 MiB device write before each step",
+            "note": "one step with nothing in flight (the reference's per-run GPU time); value is the "
+                    "throughput of back-to-back steps"}
 
 
 def sharded_parity(ctx, m, threads):
@@ -728,8 +780,11 @@ def main():
     m = measure(ctx, w, args, part=part, kernel=kernel, copies=copies, with_clocks=clocks)
     clocks.stop()
     s, dec = m["s"], m["dec"]
-    ms_step, job_bytes = m["ms_step"], m["job_bytes"]
+    ms_step, job_bytes, steady_ms = m["ms_step"], m["job_bytes"], m["steady_ms_step"]
     value = job_bytes / (ms_step * 1e-3) / 1e9
+    latency = None
+    if args.latency_reps > 0 and w["shard"] == "replica" and s.lens:
+        latency = measure_latency(ctx, m, part, kernel, args.latency_reps)
 
     # end to end through the public API with host buffers
     e2e = e2e_pool = e2e_launch = None
@@ -794,6 +849,7 @@ def main():
                                f"> 4 x L2 {l2 / 1e6:.0f} MB)" if copies > 1 else
                                f"inputs {live_est / 1e6:.0f} MB per GPU > L2 {l2 / 1e6:.0f} MB"),
                            submission="cuda graph replay, graphs captured before the timed region",
+                           flags="TABLES_READY|INPUTS_READY" + ("" if args.no_step_stream else "|STEP_STREAM"),
                            kernel=args.kernel),
             "roofline": {"bound": "hbm", "achieved": round(per_gpu, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(per_gpu / peak, 4), "peak_kind": peak_kind,
@@ -804,6 +860,13 @@ def main():
         }
         if parity:
             line["parity"] = parity
+        if steady_ms is not None:
+            line["steady"] = {"us_per_step": round(steady_ms * 1e3, 3), "steps": STEADY_STEPS,
+                              "value": round(job_bytes / (steady_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                              "note": "the same back-to-back steps over a longer run; a K-step run includes one "
+                                      "fill and drain of the steps in flight"}
+        if latency:
+            line["latency"] = latency
         if e2e:
             line["e2e"] = e2e
         if e2e_launch and e2e_launch is not e2e:
@@ -823,15 +886,21 @@ def measure_e2e_graph(torch, dist, s, dec, part, kernel, args, world, barrier, j
     """End to end as a serving loop runs decode steps: CUDA graphs of 64 steps, each step a
     host->device copy of its inputs (q, sequence lengths, block table, one packed pinned buffer), the
     kvb_paged_decode_async launch reading them where they landed, and the device->host copy of its
-    output into pinned memory. Two staging and two output buffers alternate; the input copies run on
-    one side stream and the readbacks on another, so step i+1's inputs land and step i-1's output
-    leaves while step i's kernel runs (graph edges keep every buffer's writer after its last reader).
-    Every timed step copies its inputs in and its output out. Replicas and one rank only."""
+    output into pinned memory. E2E_BUFS staging and output buffers rotate; the input copies run on
+    one side stream and the readbacks on another, so later steps' inputs land and earlier steps'
+    outputs leave while a step's kernel runs (graph edges keep every buffer's writer after its last
+    reader). Every timed step copies its inputs in and its output out. Replicas and one rank only.
+
+    The launches leave out KVB_FLAG_STEP_STREAM: a kernel node that also waits for a copy does not
+    start early behind the previous kernel, so the steps of this loop do not overlap, and the latency
+    rule's partitions serve it better (config 3 int8: 24.3 µs per step against 37.7 with the step
+    stream's, four buffers)."""
     import kv_cache_bench_b200 as kvb
 
     def align(n):
         return (n + 255) // 256 * 256
 
+    nb = E2E_BUFS
     dev = s.q.device
     q_b, l_b, t_b = s.q.numel() * 4, s.seq_lens.numel() * 4, s.table.numel() * 4
     off_l = align(q_b)
@@ -841,11 +910,11 @@ def measure_e2e_graph(torch, dist, s, dec, part, kernel, args, world, barrier, j
     host[:q_b].copy_(s.q.cpu().view(-1).view(torch.uint8))
     host[off_l:off_l + l_b].copy_(s.seq_lens.cpu().view(-1).view(torch.uint8))
     host[off_t:off_t + t_b].copy_(s.table.cpu().view(-1).view(torch.uint8))
-    stages = [torch.empty(total, dtype=torch.uint8, device=dev) for _ in range(2)]
-    outs = [torch.empty_like(s.out) for _ in range(2)]
-    houts = [torch.empty(s.out.shape, dtype=s.out.dtype, pin_memory=True) for _ in range(2)]
+    stages = [torch.empty(total, dtype=torch.uint8, device=dev) for _ in range(nb)]
+    outs = [torch.empty_like(s.out) for _ in range(nb)]
+    houts = [torch.empty(s.out.shape, dtype=s.out.dtype, pin_memory=True) for _ in range(nb)]
     cargs = []
-    for b in range(2):
+    for b in range(nb):
         st = stages[b]
         q = st[:q_b].view(torch.float32).view(s.q.shape)
         lens = st[off_l:off_l + l_b].view(torch.int32)
@@ -859,9 +928,8 @@ def measure_e2e_graph(torch, dist, s, dec, part, kernel, args, world, barrier, j
     ws, wsn = dec.workspace.data_ptr(), dec.workspace.numel()
     stream, s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     copies = len(s.pools)
-    per_graph = copies * max(1, math.ceil(64 / copies))
-    if per_graph % 2:
-        per_graph *= 2  # whole buffer pairs per graph
+    unit = copies * nb // math.gcd(copies, nb)  # whole pool rotations and buffer rounds per graph
+    per_graph = unit * max(1, math.ceil(64 / unit))
 
     def capture(n):
         with torch.cuda.stream(stream):  # warm the launch path outside the capture
@@ -875,15 +943,15 @@ def measure_e2e_graph(torch, dist, s, dec, part, kernel, args, world, barrier, j
             s_in.wait_stream(stream)
             s_out.wait_stream(stream)
             for i in range(n):
-                b = i & 1
-                with torch.cuda.stream(s_in):  # step i's inputs, once step i-2's kernel read the buffer
-                    if i >= 2:
-                        s_in.wait_event(ev_k[i - 2])
+                b = i % nb
+                with torch.cuda.stream(s_in):  # step i's inputs, once the buffer's previous kernel read it
+                    if i >= nb:
+                        s_in.wait_event(ev_k[i - nb])
                     stages[b].copy_(host, non_blocking=True)
                     ev_in[i].record(s_in)
                 stream.wait_event(ev_in[i])
-                if i >= 2:  # step i-2's readback of this output buffer is done
-                    stream.wait_event(ev_out[i - 2])
+                if i >= nb:  # the readback of this output buffer's previous step is done
+                    stream.wait_event(ev_out[i - nb])
                 kvb.paged_decode_async(cargs[b][i % copies], ws, wsn, stream.cuda_stream)
                 ev_k[i].record(stream)
                 with torch.cuda.stream(s_out):  # step i's output
@@ -910,14 +978,15 @@ def measure_e2e_graph(torch, dist, s, dec, part, kernel, args, world, barrier, j
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    ok = torch.equal(houts[(n - 1) & 1], outs[(n - 1) & 1].cpu())
+    last = graph_plan(n, per_graph)[-1] - 1  # the last step of the last replayed graph
+    ok = torch.equal(houts[last % nb], outs[last % nb].cpu())
     runner.release()
     return {"value": round(job_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 6),
             "h2d_bytes_per_step": int(total), "d2h_bytes_per_step": int(houts[0].numel() * 4), "steps": n,
             "readback_matches_device": bool(ok),
             "api": "kvb_paged_decode_async (C ABI) in CUDA graphs of %d steps: per step one packed pinned "
                    "host->device input copy, the launch, one device->pinned host output copy; copies on two "
-                   "side streams, double-buffered" % per_graph}
+                   "side streams, %d rotating buffers" % (per_graph, nb)}
 
 
 def measure_e2e(torch, dist, s, dec, part, kernel, stream, args, world, barrier, job_bytes, w, gather):
@@ -1003,7 +1072,8 @@ def measure_e2e(torch, dist, s, dec, part, kernel, stream, args, world, barrier,
         lens2 = stage2[off_l:off_l + l_b].view(torch.int32)
         table2 = stage2[off_t:off_t + t_b].view(torch.int32).view(s.table.shape)
         cargs2 = [dec.args(q2, k, v, table2, lens2, s.max_len, out=out2, k_scale=ks, v_scale=vs,
-                           part_tokens=part, kernel=kernel, tables_ready=True, inputs_ready=True) for (k, v, ks, vs) in s.pools]
+                           part_tokens=part, kernel=kernel, tables_ready=True, inputs_ready=True)
+                 for (k, v, ks, vs) in s.pools]
         stages, outs, slot_args = (stage, stage2), (s.out, out2), (cargs, cargs2)
         houts = (hout, torch.empty(result.shape, dtype=result.dtype, pin_memory=True))
         s_in, s_out = torch.cuda.Stream(s.q.device), torch.cuda.Stream(s.q.device)

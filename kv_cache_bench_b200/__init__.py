@@ -79,6 +79,9 @@ FLAG_TABLES_READY = 1
 # ... and q, the pools and the scales are not written by it either (needs FLAG_TABLES_READY): the
 # tensor-core kernel streams the pages while that kernel finishes.
 FLAG_INPUTS_READY = 2
+# ... and the call is one of a stream of independent steps launched back to back (needs
+# FLAG_INPUTS_READY): with few (sequence, head group) pairs, partitions sized for throughput.
+FLAG_STEP_STREAM = 4
 
 
 class _CPageWriteArgs(ctypes.Structure):
@@ -341,14 +344,16 @@ def flush_gpu_caches() -> None:
 def device_args(shape: Shape, kv_type: KvType, page_size: int, max_blocks: int, max_len: int, *, q: int, k: int,
                 v: int, block_table: int, seq_lens: int, out: int, num_blocks: int, part_tokens: int = 0,
                 share_kv: bool = True, k_scale: int = 0, v_scale: int = 0,
-                kernel: Kernel = Kernel.auto, tables_ready: bool = False, inputs_ready: bool = False) -> _CPagedArgs:
+                kernel: Kernel = Kernel.auto, tables_ready: bool = False, inputs_ready: bool = False,
+                step_stream: bool = False) -> _CPagedArgs:
     """kvb_paged_args over raw device pointers (ints). tables_ready sets FLAG_TABLES_READY;
-    inputs_ready sets FLAG_INPUTS_READY as well."""
+    inputs_ready sets FLAG_INPUTS_READY as well; step_stream sets FLAG_STEP_STREAM and both others."""
     return _CPagedArgs(shape._c(), int(kv_type), page_size, max_blocks, max_len, part_tokens, q or None, k or None,
                        v or None, block_table or None, seq_lens or None, out or None, 1 if share_kv else 0,
                        k_scale or None, v_scale or None, int(num_blocks), int(kernel),
-                       (FLAG_TABLES_READY if tables_ready or inputs_ready else 0)
-                       | (FLAG_INPUTS_READY if inputs_ready else 0))
+                       (FLAG_TABLES_READY if tables_ready or inputs_ready or step_stream else 0)
+                       | (FLAG_INPUTS_READY if inputs_ready or step_stream else 0)
+                       | (FLAG_STEP_STREAM if step_stream else 0))
 
 
 def paged_workspace_bytes(c: _CPagedArgs) -> int:

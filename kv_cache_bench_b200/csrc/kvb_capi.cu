@@ -126,9 +126,15 @@ Geometry geometry(const kvb_paged_args* a, int num_sms) {
         long long part_max = umma && a->page_size >= 16 ? 4096 : 2048;  // tcgen05: its page table
         const long long S = std::max<long long>(1, (long long)s.batch * g.nhg);
         const long long slots = (umma ? 1LL : 2LL) * std::max(1, num_sms);
-        if (umma && a->page_size >= 32 && S * (((long long)a->max_len + part_max - 1) / part_max) > 64 * slots)
+        // A step stream (KVB_FLAG_STEP_STREAM) on the tcgen05 kernel: about a third of the CTA slots
+        // per step, so three steps stream at once (each CTA's fixed start and end overlap other
+        // steps' streaming); partitions up to 8064 tokens where the page table holds them.
+        const bool stream = umma && (a->flags & KVB_FLAG_STEP_STREAM) && 3 * S <= slots;
+        if (umma && a->page_size >= 32 &&
+            (stream || S * (((long long)a->max_len + part_max - 1) / part_max) > 64 * slots))
             part_max = 8064;
         long long n = S < slots ? std::max<long long>(1, slots / S) : 1;
+        if (stream) n = std::max<long long>(1, (slots + 3 * S / 2) / (3 * S));  // slots / 3S, rounded
         n = std::max<long long>(n, ((long long)a->max_len + part_max - 1) / part_max);
         const long long per = ((long long)a->max_len + n - 1) / n;
         g.part = (int)std::max<long long>(chunk, (per + chunk - 1) / chunk * chunk);
@@ -151,9 +157,12 @@ int check_static(const kvb_paged_args* a) {
     if (s.num_heads % s.num_kv_heads != 0) return fail(KVB_ERR_INVALID, "H % Hkv != 0");
     if (a->max_blocks < 0) return fail(KVB_ERR_INVALID, "max_blocks < 0");
     if (a->kernel < KVB_KERNEL_AUTO || a->kernel > KVB_KERNEL_UMMA) return fail(KVB_ERR_INVALID, "unknown kernel");
-    if (a->flags & ~(KVB_FLAG_TABLES_READY | KVB_FLAG_INPUTS_READY)) return fail(KVB_ERR_INVALID, "unknown flags");
+    if (a->flags & ~(KVB_FLAG_TABLES_READY | KVB_FLAG_INPUTS_READY | KVB_FLAG_STEP_STREAM))
+        return fail(KVB_ERR_INVALID, "unknown flags");
     if ((a->flags & KVB_FLAG_INPUTS_READY) && !(a->flags & KVB_FLAG_TABLES_READY))
         return fail(KVB_ERR_INVALID, "KVB_FLAG_INPUTS_READY needs KVB_FLAG_TABLES_READY");
+    if ((a->flags & KVB_FLAG_STEP_STREAM) && !(a->flags & KVB_FLAG_INPUTS_READY))
+        return fail(KVB_ERR_INVALID, "KVB_FLAG_STEP_STREAM needs KVB_FLAG_INPUTS_READY");
     if (s.batch > 0 && (!a->q || !a->out || !a->seq_lens)) return fail(KVB_ERR_INVALID, "null q, out or seq_lens");
     if (s.batch > 0 && a->max_len > 0) {
         if (!a->k || !a->v || !a->block_table) return fail(KVB_ERR_INVALID, "null k, v or block_table");

@@ -520,7 +520,10 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 const int c0 = u.t0 / UM_CHUNK - (kp & 1), c1 = (u.t1 + UM_CHUNK - 1) / UM_CHUNK;
                 for (int c = c0; c < c1; ++c) {
                     const int tok0 = c * UM_CHUNK;
-                    if (kp == STAGES) ask_next();  // the ring is full: wait for the previous grid now
+                    // With more units than CTAs, the second unit is requested once the ring is full (after
+                    // the wait for the previous grid). A CTA with a single unit waits only at its end, so
+                    // its whole unit may stream while the previous grid runs.
+                    if (kp == STAGES && dyn) ask_next();
                     if (lane == 0 && !*s_abort && !mbar_wait_bounded(&empty[stage], phase ^ 1u, s_abort)) give_up();
                     __syncwarp();
                     // lane j < nbox owns box j (one page, or 128 rows of a larger page)

@@ -37,7 +37,8 @@ class PagedDecoder:
         self.workspace = torch.zeros(256, dtype=torch.uint8, device=self.device)
 
     def args(self, q, k_pool, v_pool, block_table, seq_lens, max_len, *, out, k_scale=None, v_scale=None,
-             part_tokens=0, share_kv=True, kernel=Kernel.auto, tables_ready=False, inputs_ready=False):
+             part_tokens=0, share_kv=True, kernel=Kernel.auto, tables_ready=False, inputs_ready=False,
+             step_stream=False):
         B, H, D = q.shape
         num_blocks, Hkv, page, D2 = k_pool.shape
         if D2 != D or v_pool.shape != k_pool.shape:
@@ -52,16 +53,16 @@ class PagedDecoder:
                            part_tokens=part_tokens, share_kv=share_kv,
                            k_scale=k_scale.data_ptr() if k_scale is not None else 0,
                            v_scale=v_scale.data_ptr() if v_scale is not None else 0, kernel=kernel,
-                           tables_ready=tables_ready, inputs_ready=inputs_ready)
+                           tables_ready=tables_ready, inputs_ready=inputs_ready, step_stream=step_stream)
 
     def __call__(self, q, k_pool, v_pool, block_table, seq_lens, max_len, *, k_scale=None, v_scale=None,
                  part_tokens=0, share_kv=True, kernel=Kernel.auto, out=None, stream=None, tables_ready=False,
-                 inputs_ready=False):
+                 inputs_ready=False, step_stream=False):
         if out is None:
             out = torch.empty_like(q)
         c = self.args(q, k_pool, v_pool, block_table, seq_lens, max_len, out=out, k_scale=k_scale,
                       v_scale=v_scale, part_tokens=part_tokens, share_kv=share_kv, kernel=kernel,
-                      tables_ready=tables_ready, inputs_ready=inputs_ready)
+                      tables_ready=tables_ready, inputs_ready=inputs_ready, step_stream=step_stream)
         need = paged_workspace_bytes(c)
         if need > self.workspace.numel():
             self.workspace = torch.zeros(need, dtype=torch.uint8, device=self.device)

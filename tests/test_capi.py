@@ -93,6 +93,12 @@ def test_flags_field_and_unknown_flags_refused():
     c = kvb.device_args(kvb.Shape(1, 8, 2, 128), kvb.KvType.f16, 16, 4, 64, q=16, k=16, v=16, block_table=16,
                         seq_lens=16, out=16, num_blocks=4, part_tokens=16, inputs_ready=True)
     assert c.flags == kvb.FLAG_TABLES_READY | kvb.FLAG_INPUTS_READY
+    c.flags = kvb.FLAG_TABLES_READY | kvb.FLAG_STEP_STREAM  # a step stream is a stream of ready inputs
+    with pytest.raises(ValueError, match="needs KVB_FLAG_INPUTS_READY"):
+        kvb.paged_workspace_bytes(c)
+    c = kvb.device_args(kvb.Shape(1, 8, 2, 128), kvb.KvType.f16, 16, 4, 64, q=16, k=16, v=16, block_table=16,
+                        seq_lens=16, out=16, num_blocks=4, part_tokens=16, step_stream=True)
+    assert c.flags == kvb.FLAG_TABLES_READY | kvb.FLAG_INPUTS_READY | kvb.FLAG_STEP_STREAM
 
 
 def _c_layout(struct, fields):

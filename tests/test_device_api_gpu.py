@@ -189,6 +189,29 @@ def test_single_wave_launches_with_inputs_ready_are_bit_identical(kv_type, lens,
     assert dec.error_flag() == 0
 
 
+@pytest.mark.parametrize("kv_type,lens", [(oracle.I8, [32768]), (oracle.F16, [32768]), (oracle.I8, [9000, 20000, 700]),
+                                           (oracle.F16, [5000, 0, 129])])
+def test_step_stream_steps_overlap_and_match_a_lone_launch(kv_type, lens):
+    """FLAG_STEP_STREAM: longer partitions for few (sequence, head group) pairs, and back-to-back
+    steps on one workspace with several of them streaming at once: each step gives the oracle's
+    result, bit-identical to a lone launch (no flags) with the same partition size."""
+    case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=lens, kv_type=kv_type, page=128,
+                            seed=19)
+    d = _dev(case)
+    dec = PagedDecoder()
+    kw = dict(k_scale=d.get("ks"), v_scale=d.get("vs"))
+    part_one = dec.part_tokens(d["q"], d["k"], d["v"], d["table"], d["lens"], case.max_len, inputs_ready=True, **kw)
+    part = dec.part_tokens(d["q"], d["k"], d["v"], d["table"], d["lens"], case.max_len, step_stream=True, **kw)
+    assert part > part_one
+    base = _call(dec, d, case.max_len, part_tokens=part).clone()
+    outs = [_call(dec, d, case.max_len, step_stream=True) for _ in range(12)]
+    torch.cuda.synchronize()
+    assert oracle.max_abs_diff(base.cpu().numpy(), case.reference()) <= TOL
+    for o in outs:
+        assert torch.equal(o, base)
+    assert dec.error_flag() == 0
+
+
 @pytest.mark.parametrize("kv_type,page,lens", [(oracle.F32, 16, [512]), (oracle.F32, 7, [3000, 0, 130, 65]),
                                                (oracle.I8, 48, [2000, 1, 700])])
 def test_cuda_core_kernel_with_inputs_ready_is_bit_identical(kv_type, page, lens):

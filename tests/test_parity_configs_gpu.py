@@ -78,6 +78,16 @@ def test_config3_full_size(dtype):
     err = oracle.max_abs_diff(s.out.cpu().numpy(), ref)
     assert err <= TOL, err
     _storage_bound_check(s, 0, inputs)
+    # bench.py's timed steps: a step stream (6 partitions of 5504 tokens per KV head, 48 units), its
+    # steps back to back on one workspace
+    assert dec.part_tokens(s.q, k, v, s.table, s.seq_lens, s.max_len, k_scale=ks, v_scale=vs, step_stream=True) == 5504
+    outs = [dec(s.q, k, v, s.table, s.seq_lens, s.max_len, k_scale=ks, v_scale=vs, step_stream=True)
+            for _ in range(8)]
+    torch.cuda.synchronize()
+    assert dec.error_flag() == 0
+    err = oracle.max_abs_diff(outs[0].cpu().numpy(), ref)
+    assert err <= TOL, err
+    assert all(torch.equal(o, outs[0]) for o in outs)
     if dtype == "i8":
         # bench's int8 pool is what the reference's quantizer makes of the same fp32 values
         k32, v32 = s.sequence_fp32(torch, 0)
