@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         for (int s = 0; s < STAGES; ++s) mbar_init(&empty[s], 1);
         for (int i = 0; i < 2; ++i) {
             mbar_init(&q_full[i], 1);
-            mbar_init(&q_free[i], 2 + 2 * UM_SOFT / 32);
+            mbar_init(&q_free[i], 1 + 2 * UM_SOFT / 32);
             mbar_init(&s_full[i], 1);
             mbar_init(&s_free[i], UM_SOFT / 32);
             mbar_init(&p_full[i], UM_SOFT / 32);
@@ -621,69 +621,73 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         publish(nullptr);
     } else if (warp == UM_MMA0 || warp == UM_MMA1) {
         // ------------------------------------------------------------------ MMA issuers
-        // Warp 9 issues the products of the even chunks (running index), warp 10 those of the odd
-        // ones, each into its own S^T and O^T buffers. One thread per warp polls: each pass issues the
-        // oldest pending O^T product if its Phat is written (that releases the stage to the producer),
-        // and the next S^T product if its stage is loaded and the previous S^T of this parity was read
-        // (so the softmax finds S^T_k ready when it finishes chunk k-2). Neither waits behind the other.
+        // Warp 9 issues every S^T = K Qhat^T product, warp 10 every O^T = V^T Phat^T product, each
+        // in running chunk order (chunk k's products go to the S^T and O^T buffers of parity k & 1,
+        // whose softmax group takes chunk k). One thread per warp, and every wait is a blocking
+        // mbarrier wait, so neither issuer takes issue slots from the softmax warps that share its
+        // SM sub-partition, and neither kind of product waits behind the other: S^T_k goes out as
+        // soon as its stage is loaded and S^T_{k-2} was read, and O^T_k as soon as Phat_k is
+        // written (which also releases the stage to the producer). One thread issuing four or eight
+        // products takes 0.2-0.3 us, so one issuer for both kinds put that on the other's path.
         // QK for int8: A = K (signed), B = q limbs (signed). PV: A = V (signed), B = probability
         // bytes (unsigned).
-        const int par = warp == UM_MMA0 ? 0 : 1;
+        const bool s_issuer = warp == UM_MMA0;
         if (lane == 0) {
-            const uint32_t idesc_qk =
-                KVT == 1 ? instr_desc(1, 0, 0, 0, 0, N, 128) : instr_desc(2, 1, 1, 0, 0, N, 128);
-            const uint32_t idesc_pv =
-                KVT == 1 ? instr_desc(1, 0, 0, 1, 1, NPV, 128) : instr_desc(2, 1, 0, 1, 1, NPV, 128);
+            const uint32_t idesc =
+                s_issuer ? (KVT == 1 ? instr_desc(1, 0, 0, 0, 0, N, 128) : instr_desc(2, 1, 1, 0, 0, N, 128))
+                         : (KVT == 1 ? instr_desc(1, 0, 0, 1, 1, NPV, 128) : instr_desc(2, 1, 0, 1, 1, NPV, 128));
             constexpr int KQK = KVT == 1 ? 16 : 32;  // contraction elements per instruction
-            const uint32_t s_tm = tmem + 32 * par, o_tm = tmem + 64 + 32 * par;
-            const uint32_t pb = sbase + uint32_t(C::P_OFF) + par * C::PBUF;
-            Unit u;
+            auto wait_on = [&](uint64_t* bar, uint32_t parity) {
+                if (!*s_abort && !mbar_wait_bounded(bar, parity, s_abort)) give_up();
+                return !*s_abort;
+            };
             int rpos = 0;  // next unit ring entry
-            bool have_unit = false, units_done = false, need_q = false;
-            int unit_no = -1, qb = 0;
-            int qk = 0, k_end = 0;         // next own chunk for S^T; end of the current unit's chunks
-            // own chunks with S^T issued and O^T pending: the older one (pv_k0) and the newer one
-            int pv_k0 = 0, pv_st0 = 0, pv_k1 = 0, pv_st1 = 0, pv_n = 0;
-            uint32_t spins = 0;
-            uint64_t t_idle = 0;
+            int unit_no = -1, k_end = 0;
             while (!*s_abort) {
-                bool progress = false;
-                while (!have_unit && !units_done) {
-                    // the next unit from the ring, once published (units without tokens are skipped)
-                    const int e = rpos % UM_RQ;
-                    if (!mbar_test(&r_full[e], uint32_t(rpos / UM_RQ) & 1)) break;
-                    const Unit v = ring_at(e);
-                    mbar_arrive(&r_empty[e]);
-                    ++rpos;
-                    if (v.b < 0) {
-                        units_done = true;
-                        break;
-                    }
-                    if (v.nparts == 0) continue;
-                    u = v;
-                    ++unit_no;
-                    qb = unit_no & 1;
-                    const int k_base = k_end;
-                    k_end = k_base + (u.t1 + UM_CHUNK - 1) / UM_CHUNK - u.t0 / UM_CHUNK + (k_base & 1);
-                    qk = k_base + ((k_base & 1) != par ? 1 : 0);
-                    have_unit = true;
-                    need_q = true;
-                }
-                // A unit with no chunk of this parity: release its Qhat buffer once it was written
-                // (not earlier, or this warp could count a later unit's release into an earlier phase).
-                if (have_unit && qk >= k_end) {
-                    if (mbar_test(&q_full[qb], (unit_no >> 1) & 1)) {
-                        tc_commit(&q_free[qb]);
-                        have_unit = false;
-                        progress = true;
-                    }
-                }
-                // ---- O^T = V^T Phat^T for the oldest pending chunk
-                if (pv_n > 0) {
-                    const int kk = pv_k0, st = pv_st0;
-                    if (mbar_test(&p_full[par], uint32_t(kk >> 1) & 1)) {
+                // the next unit from the ring (units without tokens are skipped; -1 ends it)
+                const int e = rpos % UM_RQ;
+                if (!wait_on(&r_full[e], uint32_t(rpos / UM_RQ) & 1)) break;
+                const Unit v = ring_at(e);
+                mbar_arrive(&r_empty[e]);
+                ++rpos;
+                if (v.b < 0) break;
+                if (v.nparts == 0) continue;
+                ++unit_no;
+                const int qb = unit_no & 1;
+                const int k_base = k_end;
+                k_end = k_base + (v.t1 + UM_CHUNK - 1) / UM_CHUNK - v.t0 / UM_CHUNK + (k_base & 1);
+                if (s_issuer) {
+                    if (!wait_on(&q_full[qb], (unit_no >> 1) & 1)) break;  // the unit's Qhat is written
+                    const uint32_t qaddr = sbase + uint32_t(C::Q_OFF) + qb * C::QBUF;
+                    for (int k = k_base; k < k_end; ++k) {
+                        // chunk k's stage loaded, and S^T_{k-2} (same buffer) read
+                        const int par = k & 1;
+                        const uint32_t use = uint32_t(k >> 1);
+                        if (use > 0 && !wait_on(&s_free[par], (use - 1) & 1)) break;
+                        if (!wait_on(&full[k % (2 * STAGES)], uint32_t(k / (2 * STAGES)) & 1)) break;
                         tc_fence_after();
+                        const uint32_t kt = sbase + (k % STAGES) * C::STAGE;
+#pragma unroll
+                        for (int s = 0; s < UM_D / KQK; ++s) {
+                            // 32 bytes of the contraction per instruction: slice s*32/128, offset s*32%128
+                            const uint32_t off = (s * 32 / 128) * TILE + (s * 32) % 128;
+                            const uint32_t qoff = (s * 32 / 128) * (C::NMAX * 128) + (s * 32) % 128;
+                            tc_mma<KVT>(tmem + 32 * par, smem_desc(kt + off, 16, 1024),
+                                        smem_desc(qaddr + qoff, 16, 1024), idesc, s > 0);
+                        }
+                        tc_commit(&s_full[par]);
+                    }
+                    if (*s_abort) break;
+                    tc_commit(&q_free[qb]);  // this warp's last read of the unit's Qhat buffer
+                } else {
+                    for (int k = k_base; k < k_end; ++k) {
+                        // chunk k's Phat written by its softmax group
+                        const int par = k & 1;
+                        if (!wait_on(&p_full[par], uint32_t(k >> 1) & 1)) break;
+                        tc_fence_after();
+                        const int st = k % STAGES;
                         const uint32_t vt = sbase + st * C::STAGE + NSUB * TILE;
+                        const uint32_t pb = sbase + uint32_t(C::P_OFF) + par * C::PBUF;
                         // int8: O^T accumulates over the group's chunks until the softmax restarts it
                         const bool keep = KVT == 2 && p_restart[par] == 0;
 #pragma unroll
@@ -693,62 +697,13 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                             // 32-byte swizzle): KQK token rows of 32 B, atoms of 8 rows 256 B apart.
                             const uint32_t voff = s * (KQK / 8) * 1024;
                             const uint32_t poff = s * KQK * 32;
-                            tc_mma<KVT>(o_tm, smem_desc(vt + voff, TILE, 1024),
-                                        smem_desc(pb + poff, C::PBUF, 256, SWZ_32B), idesc_pv, s > 0 || keep);
+                            tc_mma<KVT>(tmem + 64 + 32 * par, smem_desc(vt + voff, TILE, 1024),
+                                        smem_desc(pb + poff, C::PBUF, 256, SWZ_32B), idesc, s > 0 || keep);
                         }
                         tc_commit(&o_full[par]);
-                        tc_commit(&empty[st]);  // K and V of chunk kk are no longer read
-                        pv_k0 = pv_k1;
-                        pv_st0 = pv_st1;
-                        --pv_n;
-                        progress = true;
+                        tc_commit(&empty[st]);  // K and V of chunk k are no longer read
                     }
-                }
-                // ---- S^T = K Qhat^T for the next own chunk
-                if (have_unit && qk < k_end && pv_n < 2) {
-                    const int st = qk % STAGES;
-                    const uint32_t use = uint32_t(qk >> 1);
-                    const bool ready = (!need_q || mbar_test(&q_full[qb], (unit_no >> 1) & 1)) &&
-                                       mbar_test(&full[qk % (2 * STAGES)], uint32_t(qk / (2 * STAGES)) & 1) &&
-                                       (use == 0 || mbar_test(&s_free[par], (use - 1) & 1));
-                    if (ready) {
-                        need_q = false;
-                        tc_fence_after();
-                        const uint32_t kt = sbase + st * C::STAGE;
-                        const uint32_t qaddr = sbase + uint32_t(C::Q_OFF) + qb * C::QBUF;
-#pragma unroll
-                        for (int s = 0; s < UM_D / KQK; ++s) {
-                            // 32 bytes of the contraction per instruction: slice s*32/128, offset s*32%128
-                            const uint32_t off = (s * 32 / 128) * TILE + (s * 32) % 128;
-                            const uint32_t qoff = (s * 32 / 128) * (C::NMAX * 128) + (s * 32) % 128;
-                            tc_mma<KVT>(s_tm, smem_desc(kt + off, 16, 1024), smem_desc(qaddr + qoff, 16, 1024),
-                                        idesc_qk, s > 0);
-                        }
-                        tc_commit(&s_full[par]);
-                        if (pv_n == 0) {
-                            pv_k0 = qk;
-                            pv_st0 = st;
-                        } else {
-                            pv_k1 = qk;
-                            pv_st1 = st;
-                        }
-                        ++pv_n;
-                        qk += 2;
-                        if (qk >= k_end) {
-                            tc_commit(&q_free[qb]);  // this warp's last read of the unit's Qhat buffer
-                            have_unit = false;
-                        }
-                        progress = true;
-                    }
-                }
-                if (units_done && !have_unit && pv_n == 0) break;
-                // bounded idling: give up (and report) after KVB_WAIT_LIMIT_NS without progress
-                if (progress) {
-                    spins = 0;
-                } else if (++spins == 1024u) {
-                    t_idle = globaltimer_ns();
-                } else if (spins > 1024u && (spins & 1023u) == 0 && globaltimer_ns() - t_idle > KVB_WAIT_LIMIT_NS) {
-                    give_up();
+                    if (*s_abort) break;
                 }
             }
         }
