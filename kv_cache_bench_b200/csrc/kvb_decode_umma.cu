@@ -357,24 +357,23 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     for (int i = tid; i < int((2 * C::QBUF + 2 * C::PBUF) / 16); i += UM_THREADS)
         sts128_zero(sbase + uint32_t(C::Q_OFF) + 16 * i);
     fence_proxy_async_smem();
-    if (tid == 0) {
-        for (int s = 0; s < 2 * STAGES; ++s) mbar_init(&full[s], 1);
-        for (int s = 0; s < STAGES; ++s) mbar_init(&empty[s], 1);
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&q_full[i], 1);
-            mbar_init(&q_free[i], 1 + 2 * UM_SOFT / 32);
-            mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], UM_SOFT / 32);
-            mbar_init(&p_full[i], UM_SOFT / 32);
-            mbar_init(&o_full[i], 1);
-            mbar_init(&pt_free[i], 2 * UM_SOFT / 32);
+    if (warp == 0) {
+        // one barrier per lane: full and empty (one arrival), then q_full, q_free, s_full, s_free,
+        // p_full, o_full, pt_free (two each; arrival counts packed four bits apiece), then the unit
+        // ring's r_full (one) and r_empty (three: the two MMA issuers and the Qhat warp)
+        constexpr uint32_t kCounts = 1u | (1u + 2 * UM_SOFT / 32) << 4 | 1u << 8 | (UM_SOFT / 32) << 12 |
+                                     (UM_SOFT / 32) << 16 | 1u << 20 | (2u * UM_SOFT / 32) << 24;
+        for (int i = lane; i < C::NBARS; i += 32) {
+            const int j = i - 3 * STAGES;
+            uint32_t cnt = 1;
+            if (j >= 0 && j < 14) cnt = (kCounts >> (4 * (j >> 1))) & 15u;
+            else if (j >= 14 + UM_RQ) cnt = 3;
+            mbar_init(&bars[i], cnt);
         }
-        for (int i = 0; i < UM_RQ; ++i) {
-            mbar_init(&r_full[i], 1);
-            mbar_init(&r_empty[i], 3);
+        if (lane == 0) {
+            *s_abort = 0;
+            s_xcnt[0] = s_xcnt[1] = 0;
         }
-        *s_abort = 0;
-        s_xcnt[0] = s_xcnt[1] = 0;
         fence_mbarrier_init();
     }
     if (warp == UM_TMEM_WARP) {
