@@ -217,9 +217,9 @@ struct UCfg {
     static constexpr size_t VSMAX_OFF = BAD_OFF + STAGES * sizeof(int);
     static constexpr size_t BAR_OFF = kvb_align_up(VSMAX_OFF + (KVT == 2 ? 2 : 0) * sizeof(float), 64);
     // full per (stage, chunk parity); empty per stage; q_full, q_free, s_full, s_free, p_full,
-    // o_full, pt_free x2; r_full, r_empty x UM_RQ
+    // pt_free x2; r_full, r_empty x UM_RQ (the O^T products complete on the stage's empty barrier)
     // unit ring: full and empty per entry
-    static constexpr int NBARS = 3 * STAGES + 2 * 7 + 2 * UM_RQ;
+    static constexpr int NBARS = 3 * STAGES + 2 * 6 + 2 * UM_RQ;
     static constexpr size_t RED_OFF = kvb_align_up(BAR_OFF + NBARS * sizeof(uint64_t), 16);
     static constexpr size_t WIN_OFF = RED_OFF + 2 * UM_GRED * sizeof(float);
     // page table: block ids [UM_PT]; int8: scales [2 buffers][UM_PT] for K and for V
@@ -286,9 +286,11 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     uint64_t* s_full = q_full + 4;         // [2] S^T ready (MMA -> softmax), one per chunk parity
     uint64_t* s_free = q_full + 6;         // [2] S^T read (softmax -> MMA)
     uint64_t* p_full = q_full + 8;         // [2] Phat^T written, previous O^T folded (softmax -> MMA)
-    uint64_t* o_full = q_full + 10;        // [2] O^T ready (MMA -> softmax)
-    uint64_t* pt_free = q_full + 12;       // [2] int8 scale buffer read (softmax -> producer)
-    uint64_t* r_full = q_full + 14;        // [UM_RQ] unit ring entry written (producer -> consumers)
+    // A chunk's O^T product completes on its stage's empty barrier, which the softmax group of the
+    // chunk waits on as well (stage k % STAGES, phase k / STAGES: only that group's later chunks
+    // move it on).
+    uint64_t* pt_free = q_full + 10;       // [2] int8 scale buffer read (softmax -> producer)
+    uint64_t* r_full = q_full + 12;        // [UM_RQ] unit ring entry written (producer -> consumers)
     uint64_t* r_empty = r_full + UM_RQ;    // [UM_RQ] unit ring entry read (MMA issuers, Qhat warp)
     auto ring_at = [&](int e) -> Unit& { return *reinterpret_cast<Unit*>(smem + C::RING_OFF + 64 * e); };
     volatile int* p_restart = reinterpret_cast<volatile int*>(smem + C::RESTART_OFF);
@@ -359,15 +361,15 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     fence_proxy_async_smem();
     if (warp == 0) {
         // one barrier per lane: full and empty (one arrival), then q_full, q_free, s_full, s_free,
-        // p_full, o_full, pt_free (two each; arrival counts packed four bits apiece), then the unit
+        // p_full, pt_free (two each; arrival counts packed four bits apiece), then the unit
         // ring's r_full (one) and r_empty (three: the two MMA issuers and the Qhat warp)
         constexpr uint32_t kCounts = 1u | (1u + 2 * UM_SOFT / 32) << 4 | 1u << 8 | (UM_SOFT / 32) << 12 |
-                                     (UM_SOFT / 32) << 16 | 1u << 20 | (2u * UM_SOFT / 32) << 24;
+                                     (UM_SOFT / 32) << 16 | (2u * UM_SOFT / 32) << 20;
         for (int i = lane; i < C::NBARS; i += 32) {
             const int j = i - 3 * STAGES;
             uint32_t cnt = 1;
-            if (j >= 0 && j < 14) cnt = (kCounts >> (4 * (j >> 1))) & 15u;
-            else if (j >= 14 + UM_RQ) cnt = 3;
+            if (j >= 0 && j < 12) cnt = (kCounts >> (4 * (j >> 1))) & 15u;
+            else if (j >= 12 + UM_RQ) cnt = 3;
             mbar_init(&bars[i], cnt);
         }
         if (lane == 0) {
@@ -699,8 +701,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                             tc_mma<KVT>(tmem + 64 + 32 * par, smem_desc(vt + voff, TILE, 1024),
                                         smem_desc(pb + poff, C::PBUF, 256, SWZ_32B), idesc, s > 0 || keep);
                         }
-                        tc_commit(&o_full[par]);
-                        tc_commit(&empty[st]);  // K and V of chunk k are no longer read
+                        tc_commit(&empty[st]);  // O^T_k done: K and V of chunk k are no longer read
                     }
                     if (*s_abort) break;
                 }
@@ -905,7 +906,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
             };
             auto fold_prev = [&](int kp, bool loaded) {
                 if (!loaded) {
-                    if (!*s_abort && !mbar_wait_bounded(&o_full[gi], uint32_t(kp >> 1) & 1, s_abort)) give_up();
+                    if (!*s_abort && !mbar_wait_bounded(&empty[kp % STAGES], uint32_t(kp / STAGES) & 1, s_abort))
+                        give_up();
                     tc_fence_after();
                     load_o();
                     tc_wait_ld();
@@ -966,7 +968,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 // the previous chunk's O^T too, when its PV product is already done (one load wait);
                 // not for int8 with 8 heads, whose S^T and O^T together would not fit the registers
                 constexpr bool kEarlyO = KVT == 1;  // int8 folds O^T only when its max moves
-                const bool early_o = kEarlyO && have_prev && mbar_test(&o_full[gi], uint32_t(k_own >> 1) & 1);
+                const bool early_o =
+                    kEarlyO && have_prev && mbar_test(&empty[k_own % STAGES], uint32_t(k_own / STAGES) & 1);
                 if (early_o) load_o();
                 float ks = 1.f, vs = 0.f;
                 if constexpr (KVT == 2) {
@@ -1032,7 +1035,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     // product then restarts it.
                     int restart = 1;
                     if (have_prev) {
-                        if (!*s_abort && !mbar_wait_bounded(&o_full[gi], uint32_t(k_own >> 1) & 1, s_abort)) give_up();
+                        if (!*s_abort && !mbar_wait_bounded(&empty[k_own % STAGES], uint32_t(k_own / STAGES) & 1, s_abort))
+                            give_up();
                         bool moved = false;  // group-uniform
 #pragma unroll
                         for (int g = 0; g < QGP; ++g) moved |= m_prev[g] != m[g];
@@ -1098,7 +1102,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 if constexpr (KVT == 1) {
                     fold_prev(k_own, false);
                 } else {
-                    if (!*s_abort && !mbar_wait_bounded(&o_full[gi], uint32_t(k_own >> 1) & 1, s_abort)) give_up();
+                    if (!*s_abort && !mbar_wait_bounded(&empty[k_own % STAGES], uint32_t(k_own / STAGES) & 1, s_abort))
+                        give_up();
                     fold_acc(vscale_prev);
                 }
             }
