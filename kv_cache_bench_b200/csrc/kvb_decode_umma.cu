@@ -251,7 +251,11 @@ static_assert(UCfg<2>::SCRATCH_FLOATS >= UM_THREADS, "prefix scan scratch");
 static_assert(UM_THREADS >= KVB_PREFIX_MAX, "one thread per sequence in the unit prefix");
 static_assert(sizeof(Unit) <= 64, "unit slot");
 
-template <int KVT, int QGP>  // QGP: query heads per group, padded to 1, 2, 4 or 8
+// QGP: query heads per group, padded to 1, 2, 4 or 8. MULTI: the launch may have more units than CTAs
+// (dynamic hand-out from the workspace's work counter); without it every CTA takes at most its one
+// unit blockIdx.x, and the code of the hand-out (about 10 KB of a 90 KB kernel) is left out, which
+// keeps more of the kernel in the SM's instruction cache.
+template <int KVT, int QGP, bool MULTI>
 __global__ void __launch_bounds__(UM_THREADS, 1)
     decode_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                        const DecodeParams p) {
@@ -464,7 +468,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         // SM that runs slow takes fewer). Every unit is published to the MMA issuers and the Qhat
         // warp through the unit ring, in order; -1 ends it.
         unsigned* wc = work_counters(p);
-        const bool dyn = total > (long long)gridDim.x;
+        const bool dyn = MULTI && total > (long long)gridDim.x;
         unsigned nxt = 0;
         bool asked = false;
         // The producer's first workspace access: the counter count, then (with more units than CTAs)
@@ -1204,21 +1208,30 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     if (warp == UM_TMEM_WARP) tc_dealloc(tmem, UM_TMEM_COLS);
 }
 
-template <int KVT, int QGP>
-cudaError_t launch_one(const DecodeParams& p, const CUtensorMap& tk, const CUtensorMap& tv, const LaunchInfo& li) {
+template <int KVT, int QGP, bool MULTI>
+cudaError_t launch_grid(const DecodeParams& p, const CUtensorMap& tk, const CUtensorMap& tv, const LaunchInfo& li,
+                        long long grid) {
     using C = UCfg<KVT>;
     static KvbPerDevice<int> configured;  // the shared-memory attribute, set on each device
     int done = 0;
     cudaError_t e = configured.get(&done, [](int* v) {
         *v = 1;
-        return cudaFuncSetAttribute(decode_umma_kernel<KVT, QGP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        return cudaFuncSetAttribute(decode_umma_kernel<KVT, QGP, MULTI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(C::SMEM));
     });
     if (e != cudaSuccess) return e;
+    return kvb_launch_pdl(decode_umma_kernel<KVT, QGP, MULTI>, (unsigned)grid, UM_THREADS, C::SMEM, li.stream, tk,
+                          tv, p);
+}
+
+template <int KVT, int QGP>
+cudaError_t launch_one(const DecodeParams& p, const CUtensorMap& tk, const CUtensorMap& tv, const LaunchInfo& li) {
+    // at most one unit per CTA when even the dense unit count (every sequence of max_len tokens) fits
     const long long upper = (long long)p.B * p.nhg * p.max_parts;
     const long long grid = std::min<long long>(upper, (long long)li.num_sms);
     if (grid <= 0) return cudaSuccess;
-    return kvb_launch_pdl(decode_umma_kernel<KVT, QGP>, (unsigned)grid, UM_THREADS, C::SMEM, li.stream, tk, tv, p);
+    return upper > grid ? launch_grid<KVT, QGP, true>(p, tk, tv, li, grid)
+                        : launch_grid<KVT, QGP, false>(p, tk, tv, li, grid);
 }
 
 template <int KVT>
