@@ -252,9 +252,11 @@ static_assert(UM_THREADS >= KVB_PREFIX_MAX, "one thread per sequence in the unit
 static_assert(sizeof(Unit) <= 64, "unit slot");
 
 // QGP: query heads per group, padded to 1, 2, 4 or 8. MULTI: the launch may have more units than CTAs
-// (dynamic hand-out from the workspace's work counter); without it every CTA takes at most its one
-// unit blockIdx.x, and the code of the hand-out (about 10 KB of a 90 KB kernel) is left out, which
-// keeps more of the kernel in the SM's instruction cache.
+// (dynamic hand-out from the workspace's work counter, units packed by a prefix over the sequences'
+// partition counts); without it every CTA takes at most its one unit, dense slot blockIdx.x
+// (sequence, head group, partition < max_parts; a slot past its sequence's partitions is empty), and
+// the code of the hand-out and the prefix (about 14 KB of a 90 KB kernel) is left out, which keeps
+// more of the kernel in the SM's instruction cache.
 template <int KVT, int QGP, bool MULTI>
 __global__ void __launch_bounds__(UM_THREADS, 1)
     decode_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
@@ -322,15 +324,15 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     // and the block table: have them on the way while the CTA sets up (the table cooperatively
     // across CTAs, when it is small).
     int my_len = 0;
-    if (tid < p.B && tid < KVB_PREFIX_MAX) {
+    if (MULTI && tid < p.B && tid < KVB_PREFIX_MAX) {
         if (early) my_len = __ldg(p.seq_lens + tid);
         else prefetch_l2(p.seq_lens + tid);
     }
     // The producer also guesses its first unit before the lengths arrive: unit blockIdx.x of the
-    // dense numbering (max_parts partitions for every sequence), which is the first unit whenever
-    // every sequence before it has max_parts partitions (a single sequence of max_len tokens, for
-    // one). It reads the guessed unit's block ids (up to 64 pages) at once, and uses them if the
-    // decoded first unit is the guessed one.
+    // dense numbering (max_parts partitions for every sequence), which is the first unit of a launch
+    // without MULTI (when it exists), and otherwise whenever every sequence before it has max_parts
+    // partitions (a single sequence of max_len tokens, for one). It reads the guessed unit's block
+    // ids (up to 64 pages) at once, and uses them if the decoded first unit is the guessed one.
     int g_b = -1, g_hg = 0, g_part = 0, g_npg = 0;
     int g_ids[2] = {0, 0};
     if (early && warp == UM_PRODUCER && (long long)blockIdx.x < (long long)p.B * p.div_seq.d) {
@@ -406,7 +408,9 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         pdl_trigger();
     }
     const int* prefix = nullptr;
-    if (p.B <= KVB_PREFIX_MAX) {
+    // Prefix mode packs the units of sequences with fewer partitions; a launch with at most one unit
+    // per CTA has a CTA for every dense slot (b, head group, partition < max_parts) and needs none.
+    if (MULTI && p.B <= KVB_PREFIX_MAX) {
         if (!early && tid < p.B) my_len = __ldg(p.seq_lens + tid);
         build_unit_prefix_wide(p, s_prefix, reinterpret_cast<int*>(scratch), tid, UM_THREADS, 1, s_lens, my_len);
         prefix = s_prefix;
