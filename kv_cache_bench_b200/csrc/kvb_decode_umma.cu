@@ -353,17 +353,31 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     }
     {
         const size_t tb = (size_t)p.B * p.max_blocks * sizeof(int);
-        if (tb <= (size_t(256) << 10))
-            for (size_t off = ((size_t)blockIdx.x * UM_THREADS + tid) * 128; off < tb;
-                 off += (size_t)gridDim.x * UM_THREADS * 128)
-                prefetch_l2(reinterpret_cast<const char*>(p.block_table) + off);
+        const size_t off0 = ((size_t)blockIdx.x * UM_THREADS + tid) * 128, step = (size_t)gridDim.x * UM_THREADS * 128;
+        auto table_to_l2 = [&](size_t off) { prefetch_l2(reinterpret_cast<const char*>(p.block_table) + off); };
+        // the loops here and below are kept rolled in the single-unit instance (less code; the
+        // many-unit instance keeps the compiler's choice, which measured faster there)
+        if (tb <= (size_t(256) << 10)) {
+            if constexpr (MULTI) {
+                for (size_t off = off0; off < tb; off += step) table_to_l2(off);
+            } else {
+#pragma unroll 1
+                for (size_t off = off0; off < tb; off += step) table_to_l2(off);
+            }
+        }
     }
 
     // Barriers and tensor memory. The ring is not cleared: rows a chunk does not load are either
     // masked (K: the token's score is not used) or multiplied by an exactly zero probability (int8
     // V) or cleared by the softmax before the PV product (fp16 V, where 0 * NaN would not be 0).
-    for (int i = tid; i < int((2 * C::QBUF + 2 * C::PBUF) / 16); i += UM_THREADS)
-        sts128_zero(sbase + uint32_t(C::Q_OFF) + 16 * i);
+    if constexpr (MULTI) {
+        for (int i = tid; i < int((2 * C::QBUF + 2 * C::PBUF) / 16); i += UM_THREADS)
+            sts128_zero(sbase + uint32_t(C::Q_OFF) + 16 * i);
+    } else {
+#pragma unroll 1
+        for (int i = tid; i < int((2 * C::QBUF + 2 * C::PBUF) / 16); i += UM_THREADS)
+            sts128_zero(sbase + uint32_t(C::Q_OFF) + 16 * i);
+    }
     fence_proxy_async_smem();
     if (warp == 0) {
         // one barrier per lane: full and empty (one arrival), then q_full, q_free, s_full, s_free,
@@ -429,7 +443,12 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
         const int pg0 = uu.t0 >> lp, pg1 = (uu.t1 - 1) >> lp;
         const int npg = min(pg1 - pg0 + 1, UM_PT);  // the host keeps partitions within UM_PT pages
         __syncwarp();
-        for (int i = lane; i < npg; i += 32) pt_blk[i] = table_entry(__ldg(bt + pg0 + i));
+        if constexpr (MULTI) {
+            for (int i = lane; i < npg; i += 32) pt_blk[i] = table_entry(__ldg(bt + pg0 + i));
+        } else {
+#pragma unroll 1
+            for (int i = lane; i < npg; i += 32) pt_blk[i] = table_entry(__ldg(bt + pg0 + i));
+        }
         __syncwarp();
     };
     bool ids_early = false;  // producer: the first unit's block ids are already in the page table
@@ -458,10 +477,9 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     };
     if (!defer) note_counter_count(p);
 
-    auto give_up = [&]() {
-        *s_abort = 1;
-        raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
-    };
+    // A wait that ran out sets the abort flag (every role's loops end on it); the error bit is
+    // raised once, at the kernel's end (one store here instead of an atomic at each of the waits).
+    auto give_up = [&]() { *s_abort = 1; };
 
     if (warp >= 8) reg_dealloc<UM_REGS_CTRL>();  // the split happens in each role's own code
     if (warp == UM_PRODUCER) {
@@ -590,12 +608,18 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                         float* ks_b = pt_ks + sb * UM_PT;
                         float* vs_b = pt_vs + sb * UM_PT;
                         float vunit = 0.f;
-                        for (int i = lane; i < npg; i += 32) {
+                        auto scale_of = [&](int i) {
                             const int b2 = pt_blk[i];
                             const float vsi = b2 >= 0 ? __ldg(p.v_scale + (size_t)b2 * p.Hkv + u.kvh) : 0.f;
                             ks_b[i] = b2 >= 0 ? __ldg(p.k_scale + (size_t)b2 * p.Hkv + u.kvh) : 0.f;
                             vs_b[i] = vsi;
                             vunit = fmaxf(vunit, vsi);
+                        };
+                        if constexpr (MULTI) {
+                            for (int i = lane; i < npg; i += 32) scale_of(i);
+                        } else {
+#pragma unroll 1
+                            for (int i = lane; i < npg; i += 32) scale_of(i);
                         }
                         vunit = warp_max(vunit);
                         if (lane == 0) unit_vsmax[sb] = vunit;
@@ -1196,7 +1220,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     }
                 }
                 // count the partition in; the last partition's CTA merges them all
-                finish_partition<UM_D, 12>(p, u, gt, UM_SOFT, gbar, &s_xcnt[2 + gi]);
+                finish_partition<UM_D, 12, (QGP >= 2 ? 1 : 32)>(p, u, gt, UM_SOFT, gbar, &s_xcnt[2 + gi]);
             }
             // this warp is done with the unit's slot (its factors, both shares)
             tc_fence_before();
@@ -1210,6 +1234,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     if (warp == UM_TMEM_WARP) tc_dealloc(tmem, UM_TMEM_COLS);
+    if (tid == 0 && *s_abort) raise_error(p.error_flag, KVB_DEVERR_TIMEOUT);
 }
 
 template <int KVT, int QGP, bool MULTI>

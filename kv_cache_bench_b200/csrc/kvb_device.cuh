@@ -510,28 +510,30 @@ __device__ __forceinline__ bool resolve_arrival(const DecodeParams& p, const Uni
     return last;
 }
 
-template <int D, int BATCH = 8>
+template <int D, int BATCH = 8, int MAXSPLIT = 32>
 __device__ __forceinline__ void merge_partitions(const DecodeParams& p, const Unit& u, int tid, int nthreads);
 
-template <int D, int BATCH = 8>
+// MAXSPLIT bounds the lanes that share a (head, 4-dim slice) pair: a caller whose heads always fill
+// half of its threads passes 1, and the lane combine is compiled out.
+template <int D, int BATCH = 8, int MAXSPLIT = 32>
 __device__ __forceinline__ void finish_partition(const DecodeParams& p, const Unit& u, int tid, int nthreads,
                                                  uint32_t bar_id, int* s_flag) {
     if (u.nparts <= 1) return;
     named_barrier(bar_id, nthreads);  // every thread's partial stores come before the arrival below
     if (tid == 0) *s_flag = resolve_arrival(p, u, arrive_partition(p, u));
     named_barrier(bar_id, nthreads);
-    if (*s_flag) merge_partitions<D, BATCH>(p, u, tid, nthreads);
+    if (*s_flag) merge_partitions<D, BATCH, MAXSPLIT>(p, u, tid, nthreads);
 }
 
 // The merge of all partitions of u into `out` (the CTA of the last partition, every other
 // partition's stores visible through the acquiring arrival).
-template <int D, int BATCH>
+template <int D, int BATCH, int MAXSPLIT>
 __device__ __forceinline__ void merge_partitions(const DecodeParams& p, const Unit& u, int tid, int nthreads) {
     constexpr int D4 = D / 4;
     const int np = u.nparts, nh = u.nh;
     const int pairs = nh * D4;
     int split = 1;
-    while (split < 32 && split * 2 * pairs <= nthreads) split *= 2;
+    while (split < MAXSPLIT && split * 2 * pairs <= nthreads) split *= 2;
     const int s = tid % split;
     for (int base = 0; base < pairs * split; base += nthreads) {  // the same trip count in every lane
         const int idx = base + tid;
