@@ -107,8 +107,8 @@ typedef struct kvb_paged_args {
  *   latency of one step. With fewer (sequence, head group) pairs than a third of the SMs, the tcgen05
  *   kernel then splits the context into fewer, longer partitions, so that a step's grid covers about
  *   a third of the SMs and three consecutive steps stream at once, each overlapping the others'
- *   first and last microseconds (config 3 int8 on B200: 16.3 -> 12.0 us per step over 1000 steps).
- *   A step that runs alone takes longer (config 3 int8: 39 against 26 us, each timed alone). */
+ *   first and last microseconds (config 3 int8 on B200: 14.2 -> 10.3 us per step over 1000 steps).
+ *   A step that runs alone takes longer, since its grid covers a third of the SMs. */
 #define KVB_FLAG_STEP_STREAM 4
 
 /* src/metal_attn.hpp:71-80 (NaiveArgs): contiguous cache [B][Hkv][max_len][D], fp32 or fp16. */
