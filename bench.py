@@ -787,13 +787,15 @@ def main():
         latency = measure_latency(ctx, m, part, kernel, args.latency_reps)
 
     # end to end through the public API with host buffers
-    e2e = e2e_pool = e2e_launch = None
+    e2e = e2e_pool = e2e_launch = e2e_copy = None
     if not args.no_e2e:
         e2e_launch, e2e_pool = measure_e2e(torch, dist, s, dec, part, kernel, m["stream"], args, world, ctx.barrier,
                                            job_bytes, w, m["gather"])
         e2e = e2e_launch
         if m["gather"].mode is None:
-            e2e = measure_e2e_graph(torch, dist, s, dec, part, kernel, args, world, ctx.barrier, job_bytes)
+            e2e_copy = measure_e2e_graph(torch, dist, s, dec, part, kernel, args, world, ctx.barrier, job_bytes)
+            e2e = measure_e2e_mapped(torch, dist, s, dec, part, kernel, args, world, ctx.barrier, job_bytes,
+                                     not args.no_step_stream)
 
     # parity of the step's own output (the checker, outside every timed region)
     parity = None
@@ -869,6 +871,8 @@ def main():
             line["latency"] = latency
         if e2e:
             line["e2e"] = e2e
+        if e2e_copy:
+            line["e2e_copy_engine"] = e2e_copy
         if e2e_launch and e2e_launch is not e2e:
             line["e2e_host_launch"] = e2e_launch
         if e2e_pool:
@@ -987,6 +991,75 @@ def measure_e2e_graph(torch, dist, s, dec, part, kernel, args, world, barrier, j
             "api": "kvb_paged_decode_async (C ABI) in CUDA graphs of %d steps: per step one packed pinned "
                    "host->device input copy, the launch, one device->pinned host output copy; copies on two "
                    "side streams, %d rotating buffers" % (per_graph, nb)}
+
+
+def measure_e2e_mapped(torch, dist, s, dec, part, kernel, args, world, barrier, job_bytes, step_stream):
+    """End to end with the step's inputs and output in pinned host memory, used in place: q, the
+    sequence lengths and the block table live in page-locked host buffers, and the output goes
+    into one. kvb_paged_decode_async is given those host pointers (the device reaches page-locked
+    memory at the same address), so every step's kernel reads its inputs from host memory across the
+    host link and writes its result there, inside the timed region; no copy-engine copy sits between
+    two steps, and consecutive steps overlap as they do on device buffers (flags as the device
+    timing: TABLES_READY | INPUTS_READY, and STEP_STREAM unless turned off). This is how the
+    reference's own path reaches its inputs: its buffers are shared storage that the GPU reads where
+    the host wrote them. The KV pool and its scales are device-resident state, rotated over the same
+    copies as the device timing. Replicas and one rank only."""
+    import kv_cache_bench_b200 as kvb
+
+    hq = s.q.cpu().pin_memory()
+    hl = s.seq_lens.cpu().pin_memory()
+    ht = s.table.cpu().pin_memory()
+    hout = torch.zeros(s.out.shape, dtype=s.out.dtype).pin_memory()
+    B, H, D = s.q.shape
+    num_blocks, Hkv, page, _ = s.pools[0][0].shape
+    kvt = {torch.int8: kvb.KvType.i8, torch.float16: kvb.KvType.f16,
+           torch.float32: kvb.KvType.f32}[s.pools[0][0].dtype]
+    cargs = [kvb.device_args(kvb.Shape(B, H, Hkv, D), kvt, page, s.table.shape[1], int(s.max_len),
+                             q=hq.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), block_table=ht.data_ptr(),
+                             seq_lens=hl.data_ptr(), out=hout.data_ptr(), num_blocks=num_blocks, part_tokens=part,
+                             k_scale=ks.data_ptr() if ks is not None else 0,
+                             v_scale=vs.data_ptr() if vs is not None else 0, kernel=kernel,
+                             tables_ready=True, inputs_ready=True, step_stream=step_stream)
+             for (k, v, ks, vs) in s.pools]
+    need = max(kvb.paged_workspace_bytes(c) for c in cargs)
+    if need > dec.workspace.numel():
+        dec.workspace = torch.zeros(need, dtype=torch.uint8, device=s.q.device)
+    ws, wsn = dec.workspace.data_ptr(), dec.workspace.numel()
+    stream = torch.cuda.Stream(s.q.device)
+    copies = len(cargs)
+
+    def step(i):
+        kvb.paged_decode_async(cargs[i % copies], ws, wsn, stream.cuda_stream)
+
+    per_graph = copies * max(1, math.ceil(64 / copies))
+    runner = make_runner(torch, stream, step, per_graph)
+    n = max(args.steps, 1)
+    runner.prepare(per_graph, n)
+    runner.run(per_graph)
+    barrier()
+    e0, e1 = timed_run(torch, stream, runner, n)
+    barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / n], dtype=torch.float64, device=s.q.device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    flag = dec.error_flag(stream)
+    runner.release()
+    # the same launch on device buffers (every pool copy holds the same pages)
+    k, v, ks, vs = s.pools[0]
+    dout = torch.empty_like(s.out)
+    dev_args = dec.args(s.q, k, v, s.table, s.seq_lens, s.max_len, out=dout, k_scale=ks, v_scale=vs, part_tokens=part,
+                        kernel=kernel, tables_ready=True, inputs_ready=True, step_stream=step_stream)
+    kvb.paged_decode_async(dev_args, ws, wsn, stream.cuda_stream)
+    stream.synchronize()
+    ok = torch.equal(hout, dout.cpu())
+    in_bytes = hq.numel() * 4 + hl.numel() * 4 + ht.numel() * 4
+    return {"value": round(job_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 6),
+            "h2d_bytes_per_step": int(in_bytes), "d2h_bytes_per_step": int(hout.numel() * 4), "steps": n,
+            "readback_matches_device": bool(ok), "error_flag": flag,
+            "api": "kvb_paged_decode_async (C ABI) in CUDA graphs of %d steps, q, sequence lengths and block "
+                   "table read by the kernel from pinned host memory and the output written into pinned host "
+                   "memory every step (no staging copies)%s" % (per_graph, ", step stream" if step_stream else "")}
 
 
 def measure_e2e(torch, dist, s, dec, part, kernel, stream, args, world, barrier, job_bytes, w, gather):

@@ -229,3 +229,36 @@ def test_cuda_core_kernel_with_inputs_ready_is_bit_identical(kv_type, page, lens
     for o in outs:
         assert torch.equal(o, base)
     assert dec.error_flag() == 0
+
+
+@pytest.mark.parametrize("kv_type,lens,kernel,flags", [
+    (oracle.I8, [32768], kvb.Kernel.auto, "stream"), (oracle.F16, [9000, 0, 700], kvb.Kernel.auto, "inputs"),
+    (oracle.I8, [5000, 129], kvb.Kernel.auto, ""), (oracle.F32, [3000, 65], kvb.Kernel.simt, "inputs")])
+def test_inputs_and_output_in_pinned_host_memory(kv_type, lens, kernel, flags):
+    """q, the lengths and the block table read by the kernels from page-locked host memory, the output
+    written into page-locked host memory (the device reaches it at the host address): back-to-back
+    steps give the result of the same launch on device buffers, bit for bit."""
+    case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=lens, kv_type=kv_type, page=128,
+                            seed=23)
+    d = _dev(case)
+    dec = PagedDecoder()
+    kw = dict(inputs_ready=flags in ("inputs", "stream"), step_stream=flags == "stream")
+    base = _call(dec, d, case.max_len, kernel=kernel, **kw).clone()
+    torch.cuda.synchronize()
+    assert oracle.max_abs_diff(base.cpu().numpy(), case.reference()) <= TOL
+    hq, hl, ht = (d[n].cpu().pin_memory() for n in ("q", "lens", "table"))
+    hout = torch.full(tuple(base.shape), float("nan")).pin_memory()
+    B, H, D = hq.shape
+    num_blocks, Hkv, page, _ = d["k"].shape
+    kvt = {oracle.F32: kvb.KvType.f32, oracle.F16: kvb.KvType.f16, oracle.I8: kvb.KvType.i8}[kv_type]
+    c = kvb.device_args(kvb.Shape(B, H, Hkv, D), kvt, page, ht.shape[1], case.max_len, q=hq.data_ptr(),
+                        k=d["k"].data_ptr(), v=d["v"].data_ptr(), block_table=ht.data_ptr(), seq_lens=hl.data_ptr(),
+                        out=hout.data_ptr(), num_blocks=num_blocks,
+                        k_scale=d["ks"].data_ptr() if "ks" in d else 0, v_scale=d["vs"].data_ptr() if "vs" in d else 0,
+                        kernel=kernel, **kw)
+    stream = torch.cuda.current_stream()
+    for _ in range(6):
+        kvb.paged_decode_async(c, dec.workspace.data_ptr(), dec.workspace.numel(), stream.cuda_stream)
+    stream.synchronize()
+    assert torch.equal(hout, base.cpu())
+    assert dec.error_flag() == 0
