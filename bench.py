@@ -12,16 +12,18 @@ the device by the library's page write path, int8 by the reference-identical qua
   2  f16, context 4096, page 32, 256-page pool, split-K partition 512
   3  int8 (default; --dtype f16 for the fp16 variant), context 32768, page 128, 512-page pool  [default]
   4  f16, 64 sequences, lengths log-uniform in [512, 32768], page 16, pool 1.1 x live pages;
-     sharded by sequence (LPT bin packing) across ranks, outputs all-gathered with NCCL
+     sharded by sequence (LPT bin packing) across ranks
   5  f16 or int8, 256 sequences, 64/8 heads, lengths uniform in [8192, 131072], page 64;
-     sharded by KV head across ranks, outputs all-gathered with NCCL
+     sharded by KV head across ranks
 Configs 1-3 are single-sequence steps; with --gpus N every rank runs its own replica (weak
 scaling). Inputs of configs 1-3 fit in L2 (126 MB), so each timed step reads one of R pool copies in
 rotation (R * live bytes > 4 x L2); configs 4-5 are far larger than L2.
 
 ``sharded`` (on by default for the single-sequence headline): configs 4 (f16, by sequence) and 5
-(int8 and f16, by KV head) measured at the same N in the same run, each step the decode kernel plus
-the NCCL all-gather and the reorder into global order, captured together in CUDA graphs.
+(int8 and f16, by KV head) measured at the same N in the same run. Each step is the decode kernel,
+which writes every finished output row into every rank's global output buffer in global order over
+peer memory (CUDA IPC mappings, NVLink), and a one-warp step barrier, captured together in CUDA
+graphs; --gather nccl replaces the in-kernel gather by an NCCL all-gather and a reorder.
 
 Timing: W warm-up steps, then exactly K steps between a barrier + synchronize on each side, timed
 with CUDA events on the launching stream; max over ranks. Steps are CUDA-graph replays; every graph
@@ -88,6 +90,9 @@ def parse_args(argv=None):
                     help="sharded configs measured after the headline: 'auto' (4:f16,5:i8,5:f16 when the headline "
                          "is a single-sequence config), 'none', or a list like 4:f16,5:i8")
     ap.add_argument("--sharded-s", type=float, default=1.5, help="timed seconds per sharded config, at most")
+    ap.add_argument("--gather", choices=["kernel", "nccl"], default="kernel",
+                    help="sharded steps: outputs written into every rank's buffer by the decode kernel over peer "
+                         "memory, or an NCCL all-gather and a reorder")
     ap.add_argument("--ramp-s", type=float, default=1.0, help="untimed load before warm-up (clock ramp)")
     ap.add_argument("--seqs", type=int, default=None,
                     help="keep only the first N sequences of the config (a smaller case for profilers)")
@@ -567,17 +572,31 @@ def decoder_for(ctx, s, part, kernel, step_stream):
 
 
 class Gather:
-    """The per-rank outputs of a sharded step put together in global order on every rank: one NCCL
+    """The per-rank outputs of a sharded step put together in global order on every rank. Default
+    ("kernel"): the decode kernel writes each finished row into every rank's global output buffer
+    over peer memory and a step barrier follows (kv_cache_bench_b200.peer); "nccl": one NCCL
     all-gather, then a reorder (a row gather for sequence shards, a head interleave for KV-head
     shards). Nothing for replicas and for one rank."""
 
-    def __init__(self, ctx, s, w):
+    def __init__(self, ctx, s, w, how="kernel"):
         from kv_cache_bench_b200 import shard as sh
         torch = ctx.torch
         self.ctx, self.s, self.w = ctx, s, w
         self.mode = None if (ctx.world == 1 or w["shard"] == "replica") else w["shard"]
+        self.fused = self.mode is not None and how == "kernel"
+        self.peer = None
         self.final = s.out
-        if self.mode == "sequence":
+        G = w["H"] // w["Hkv"]
+        self.h0 = s.kv_heads[0] * G if self.mode == "kv_head" else 0
+        if self.fused:
+            from kv_cache_bench_b200.peer import PeerGather
+            rows = None
+            if self.mode == "sequence":
+                rows = torch.tensor(s.seqs, dtype=torch.int32, device=ctx.device)
+            self.peer = PeerGather(torch, ctx.dist, ctx.rank, ctx.world, len(w["lens"]), w["H"], w["D"], ctx.device,
+                                   out_head0=self.h0, out_rows=rows)
+            self.final = self.peer.views[0]
+        elif self.mode == "sequence":
             pad = max(len(o) for o in s.owned)
             self.local = torch.zeros((pad, s.H, w["D"]), dtype=torch.float32, device=ctx.device)
             self.gathered = torch.empty((ctx.world * pad, s.H, w["D"]), dtype=torch.float32, device=ctx.device)
@@ -586,6 +605,25 @@ class Gather:
         elif self.mode == "kv_head":
             self.gathered = torch.empty((ctx.world,) + tuple(s.out.shape), dtype=torch.float32, device=ctx.device)
             self.final = torch.empty((len(w["lens"]), w["H"], w["D"]), dtype=torch.float32, device=ctx.device)
+
+    def describe(self):
+        if self.mode is None:
+            return "decode kernel"
+        if self.fused:
+            return ("decode kernel writing every output row into every rank's global buffer over peer memory "
+                    "+ step barrier kernel, one CUDA graph")
+        return "decode kernel + NCCL all-gather + reorder, one CUDA graph"
+
+    def launch(self, cargs, ws, wsn, stream, i):
+        """Step i on `stream` (a raw cudaStream_t): the decode and the gather. Returns the step's
+        global output."""
+        import kv_cache_bench_b200 as kvb
+        if self.fused:
+            self.final = self.peer.launch(cargs, ws, wsn, stream, i)
+            return self.final
+        if self.s.lens:
+            kvb.paged_decode_async(cargs, ws, wsn, stream)
+        return self()
 
     def __call__(self):
         torch, dist = self.ctx.torch, self.ctx.dist
@@ -602,9 +640,13 @@ class Gather:
         """Row of the gathered output that holds local sequence i's heads of this rank."""
         b = self.s.seqs[i]
         if self.mode == "kv_head":
-            h0 = self.s.kv_heads[0] * (self.w["H"] // self.w["Hkv"])
-            return self.final[b, h0:h0 + self.s.H]
+            return self.final[b, self.h0:self.h0 + self.s.H]
         return self.final[b]
+
+    def close(self):
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
 
 def measure(ctx, w, args, *, part, kernel, copies, with_clocks=None, max_seconds=None):
@@ -615,16 +657,14 @@ def measure(ctx, w, args, *, part, kernel, copies, with_clocks=None, max_seconds
     torch = ctx.torch
     s = DeviceStep(torch, w, device=ctx.device, rank=ctx.rank, world=ctx.world, copies=copies)
     dec, cargs = decoder_for(ctx, s, part, kernel, not args.no_step_stream)
-    gather = Gather(ctx, s, w)
+    gather = Gather(ctx, s, w, args.gather)
     stream = torch.cuda.Stream(ctx.device)
     ws_ptr, ws_n = dec.workspace.data_ptr(), dec.workspace.numel()
 
     def step(i):
-        if s.lens:
-            kvb.paged_decode_async(cargs[i % copies], ws_ptr, ws_n, stream.cuda_stream)
-        gather()
+        gather.launch(cargs[i % copies], ws_ptr, ws_n, stream.cuda_stream, i)
 
-    if gather.mode:  # the communicator is set up before any capture
+    if gather.mode and not gather.fused:  # the communicator is set up before any capture
         with torch.cuda.stream(stream):
             gather()
         ctx.barrier()
@@ -673,6 +713,15 @@ def measure(ctx, w, args, *, part, kernel, copies, with_clocks=None, max_seconds
         steady = ctx.reduce(f0.elapsed_time(f1)) / STEADY_STEPS
     flag = dec.error_flag(stream) if s.lens else 0
     runner.release()
+    if gather.fused:
+        # outside the timing: the local output of a plain launch (the parity check reads it) and one
+        # gathered step into the first buffer, complete on every rank
+        with torch.cuda.stream(stream):
+            if s.lens:
+                kvb.paged_decode_async(cargs[0], ws_ptr, ws_n, stream.cuda_stream)
+            gather.launch(cargs[0], ws_ptr, ws_n, stream.cuda_stream, 0)
+        ctx.barrier()
+        flag = max(flag, dec.error_flag(stream) if s.lens else 0)
     ms_step = ms_total / max(steps, 1)
     job_bytes = ctx.reduce(s.bytes, "sum")
     return dict(s=s, dec=dec, gather=gather, stream=stream, ms_step=ms_step, steps=steps, job_bytes=job_bytes,
@@ -815,6 +864,7 @@ def main():
             cb = {"value": None, "error": str(ex)[:200]}
     per_gpu = s.bytes / (ms_step * 1e-3) / 1e9
     part_used, flag = m["part"], m["flag"]
+    m["gather"].close()
     del m, s, dec
     torch.cuda.empty_cache()
 
@@ -829,10 +879,11 @@ def main():
                  "value": round(ms_["job_bytes"] / (ms_["ms_step"] * 1e-3) / 1e9, 2), "unit": "GB/s",
                  "frac_of_n_peak": round(ms_["job_bytes"] / (ms_["ms_step"] * 1e-3) / 1e9 / (world * peak), 4),
                  "part_tokens": ms_["part"], "error_flag": ms_["flag"],
-                 "step": "decode kernel + NCCL all-gather + reorder, one CUDA graph" if world > 1 else "decode kernel"}
+                 "step": ms_["gather"].describe()}
         if not args.no_parity:
             entry["parity"] = sharded_parity(ctx, ms_, threads)
         sharded[f"config{cfg}_{ws['kv']}"] = entry
+        ms_["gather"].close()
         del ms_
         torch.cuda.empty_cache()
 
@@ -1093,7 +1144,7 @@ def measure_e2e(torch, dist, s, dec, part, kernel, stream, args, world, barrier,
     q = stage[:q_b].view(torch.float32).view(s.q.shape)
     lens = stage[off_l:off_l + l_b].view(torch.int32)
     table = stage[off_t:off_t + t_b].view(torch.int32).view(s.table.shape)
-    result = gather()
+    result = gather.final if gather.fused else gather()
     torch.cuda.synchronize()
     hout = torch.empty(result.shape, dtype=result.dtype, pin_memory=True)
     # the inputs arrive by host copy each step (no kernel writes them)
@@ -1115,8 +1166,7 @@ def measure_e2e(torch, dist, s, dec, part, kernel, stream, args, world, barrier,
                 k, v, _, _ = s.pools[i % len(s.pools)]
                 k.copy_(pool_upload[0], non_blocking=True)
                 v.copy_(pool_upload[1], non_blocking=True)
-            kvb.paged_decode_async(cargs[i % len(cargs)], ws, wsn, raw)
-            hout.copy_(gather(), non_blocking=True)
+            hout.copy_(gather.launch(cargs[i % len(cargs)], ws, wsn, raw, i), non_blocking=True)
 
     def timed(count, pool_upload=None):
         for i in range(3):

@@ -256,6 +256,62 @@ int kvb_paged_static_error_flag(void* stream, int* flag);
  * the counters, so the workspace can be used again. */
 int kvb_paged_error_flag(void* workspace, void* stream, int* flag);
 
+/* ---- sharded steps: the output gathered by the decode kernel itself ----------------------- */
+/* No counterpart in the reference, which runs on one GPU. One process per GPU, ranks 0..n-1 on
+ * GPUs with peer access (NVLink / NVSwitch). Each rank decodes its share of the step (some
+ * sequences, or some KV heads of every sequence), and the kernel writes every finished output row
+ * straight into every rank's global output buffer, in global order, over peer memory: there is no
+ * separate all-gather and no reorder, and the transfers overlap the rest of the decode. A small
+ * barrier kernel then tells each rank that every peer's rows have landed. */
+
+#define KVB_MAX_PEERS 8
+
+/* Device memory that other processes can map (CUDA IPC): cudaMalloc'd, zero-filled, with its
+ * handle. Exchange the 64 handle bytes between ranks (any host channel), map peers' memory with
+ * kvb_ipc_open. */
+typedef struct { unsigned char bytes[64]; } kvb_ipc_handle;
+int kvb_ipc_alloc(size_t bytes, void** ptr, kvb_ipc_handle* handle);
+int kvb_ipc_free(void* ptr);
+/* Maps another process's kvb_ipc_alloc memory on the current device (peer access enabled). */
+int kvb_ipc_open(const kvb_ipc_handle* handle, void** ptr);
+int kvb_ipc_close(void* ptr);
+
+/* Where a sharded step's outputs go. Global output of every rank: [rows][out_heads][head_dim]
+ * fp32. Local sequence b, local query head h (0 <= h < num_heads of this rank's args) is global row
+ * out_rows[b] (or b when out_rows is NULL), global head out_head0 + h; each element is written to
+ * peer_out[0..n_peers), peer_out[self] being this rank's own buffer. Rows outside [0, rows) are
+ * refused on the device (error bit 2, nothing written). */
+typedef struct kvb_peer_out {
+    int n_peers;                        /* 1..KVB_MAX_PEERS */
+    int self;                           /* index of this rank's own buffer in peer_out */
+    int rows;                           /* global rows (sequences) of every peer buffer */
+    int out_heads;                      /* query heads per global row */
+    int out_head0;                      /* global head of this rank's head 0 */
+    const int* out_rows;                /* device [batch] or NULL */
+    float* peer_out[KVB_MAX_PEERS];     /* device pointers (this rank's own, or kvb_ipc_open'ed) */
+} kvb_peer_out;
+
+/* kvb_paged_decode_async with the outputs written through `peers` instead of args->out (which may
+ * be NULL). Stream-ordered. The peers' buffers must not be read until kvb_peer_barrier_async has
+ * passed on this step. */
+int kvb_paged_decode_gather_async(const kvb_paged_args* args, const kvb_peer_out* peers, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
+/* The step barrier after kvb_paged_decode_gather_async on every rank. signal[j] is rank j's signal
+ * array (KVB_MAX_PEERS unsigned words, kvb_ipc memory: this rank's own and the others' mapped);
+ * epoch is one word of this rank's device memory, zero at the start and never shared. One CTA: it
+ * waits for the decode before it on `stream`, counts the epoch up, stores it into word `rank` of
+ * every rank's signal array (system-scope release), then waits until every rank's word in its own
+ * array reached it (acquire). A wait that runs past timeout_us (0: one second) gives up, sets bit 4
+ * of the workspace's error word (kvb_paged_error_flag) and returns, so the context stays usable. */
+typedef struct kvb_peer_barrier_args {
+    int n_peers, rank;
+    unsigned int timeout_us;
+    unsigned int* epoch;
+    unsigned int* signal[KVB_MAX_PEERS];
+} kvb_peer_barrier_args;
+int kvb_peer_barrier_async(const kvb_peer_barrier_args* args, void* workspace, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

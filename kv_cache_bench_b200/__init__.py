@@ -32,7 +32,8 @@ __all__ = [
     "NaiveArgs", "metal_available", "device_name", "run_paged", "run_paged_steps", "run_naive",
     "begin_pipelined", "end_pipelined", "run_read_bandwidth", "flush_gpu_caches", "Kernel",
     "paged_workspace_bytes", "paged_part_tokens", "paged_decode_async", "paged_error_flag",
-    "paged_decode_static", "paged_static_error_flag", "library_path", "lib",
+    "paged_decode_static", "paged_static_error_flag", "library_path", "lib", "MAX_PEERS", "ipc_alloc", "ipc_free",
+    "ipc_open", "ipc_close", "peer_out", "paged_decode_gather_async", "peer_barrier_args", "peer_barrier_async",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -415,3 +416,94 @@ def paged_error_flag(workspace: int, stream: int = 0) -> int:
     f = ctypes.c_int()
     _check(_c_error_flag(workspace or None, stream or None, ctypes.byref(f)), "paged_error_flag")
     return f.value
+
+
+# ---- sharded steps gathered in the kernel (include/kvb_cuda.h, "sharded steps") ---------------------
+
+MAX_PEERS = 8
+
+
+class _CIpcHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
+
+
+class _CPeerOut(ctypes.Structure):
+    _fields_ = [("n_peers", ctypes.c_int), ("self", ctypes.c_int), ("rows", ctypes.c_int),
+                ("out_heads", ctypes.c_int), ("out_head0", ctypes.c_int), ("out_rows", ctypes.c_void_p),
+                ("peer_out", ctypes.c_void_p * MAX_PEERS)]
+
+
+class _CPeerBarrierArgs(ctypes.Structure):
+    _fields_ = [("n_peers", ctypes.c_int), ("rank", ctypes.c_int), ("timeout_us", ctypes.c_uint),
+                ("epoch", ctypes.c_void_p), ("signal", ctypes.c_void_p * MAX_PEERS)]
+
+
+_c_ipc_alloc = _sig("kvb_ipc_alloc", ctypes.c_int, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p),
+                    ctypes.POINTER(_CIpcHandle))
+_c_ipc_free = _sig("kvb_ipc_free", ctypes.c_int, ctypes.c_void_p)
+_c_ipc_open = _sig("kvb_ipc_open", ctypes.c_int, ctypes.POINTER(_CIpcHandle), ctypes.POINTER(ctypes.c_void_p))
+_c_ipc_close = _sig("kvb_ipc_close", ctypes.c_int, ctypes.c_void_p)
+_c_decode_gather = _sig("kvb_paged_decode_gather_async", ctypes.c_int, ctypes.POINTER(_CPagedArgs),
+                        ctypes.POINTER(_CPeerOut), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p)
+_c_peer_barrier = _sig("kvb_peer_barrier_async", ctypes.c_int, ctypes.POINTER(_CPeerBarrierArgs), ctypes.c_void_p,
+                       ctypes.c_void_p)
+
+
+def ipc_alloc(nbytes: int):
+    """kvb_ipc_alloc: zero-filled device memory another process can map. Returns (pointer, handle
+    bytes)."""
+    p, h = ctypes.c_void_p(), _CIpcHandle()
+    _check(_c_ipc_alloc(int(nbytes), ctypes.byref(p), ctypes.byref(h)), "ipc_alloc")
+    return p.value, bytes(h.bytes)
+
+
+def ipc_free(ptr: int) -> None:
+    _check(_c_ipc_free(ptr or None), "ipc_free")
+
+
+def ipc_open(handle: bytes) -> int:
+    """kvb_ipc_open: maps another process's ipc_alloc memory on the current device."""
+    h = _CIpcHandle()
+    if len(handle) != 64:
+        raise ValueError("an IPC handle has 64 bytes")
+    ctypes.memmove(h.bytes, handle, 64)
+    p = ctypes.c_void_p()
+    _check(_c_ipc_open(ctypes.byref(h), ctypes.byref(p)), "ipc_open")
+    return p.value
+
+
+def ipc_close(ptr: int) -> None:
+    _check(_c_ipc_close(ptr or None), "ipc_close")
+
+
+def peer_out(peers, self_index: int, rows: int, out_heads: int, out_head0: int = 0, out_rows: int = 0) -> _CPeerOut:
+    """kvb_peer_out: every rank's global output buffer (device pointers, this rank's own at
+    self_index), the global rows and heads, and the device array of global rows of the local
+    sequences (0: local index = global row)."""
+    if not 1 <= len(peers) <= MAX_PEERS:
+        raise ValueError(f"1..{MAX_PEERS} peers")
+    arr = (ctypes.c_void_p * MAX_PEERS)(*([int(x) for x in peers] + [None] * (MAX_PEERS - len(peers))))
+    return _CPeerOut(len(peers), int(self_index), int(rows), int(out_heads), int(out_head0), out_rows or None, arr)
+
+
+def paged_decode_gather_async(c: _CPagedArgs, peers: _CPeerOut, workspace: int, workspace_bytes: int,
+                              stream: int = 0) -> None:
+    """kvb_paged_decode_gather_async: a decode step whose outputs the kernel writes into every rank's
+    global output buffer."""
+    _check(_c_decode_gather(ctypes.byref(c), ctypes.byref(peers), workspace or None, int(workspace_bytes),
+                            stream or None), "paged_decode_gather_async")
+
+
+def peer_barrier_args(rank: int, signals, epoch: int, timeout_us: int = 0) -> _CPeerBarrierArgs:
+    """kvb_peer_barrier_args: every rank's signal array (device pointers, in rank order) and this
+    rank's epoch word."""
+    if not 1 <= len(signals) <= MAX_PEERS:
+        raise ValueError(f"1..{MAX_PEERS} peers")
+    arr = (ctypes.c_void_p * MAX_PEERS)(*([int(x) for x in signals] + [None] * (MAX_PEERS - len(signals))))
+    return _CPeerBarrierArgs(len(signals), int(rank), int(timeout_us), epoch or None, arr)
+
+
+def peer_barrier_async(b: _CPeerBarrierArgs, workspace: int, stream: int = 0) -> None:
+    """kvb_peer_barrier_async: the step barrier after paged_decode_gather_async on every rank; a wait
+    that runs out sets bit 4 of the workspace's error word."""
+    _check(_c_peer_barrier(ctypes.byref(b), workspace or None, stream or None), "peer_barrier_async")

@@ -203,8 +203,9 @@ int encode_pool_map(CUtensorMap* map, const void* pool, const kvb_paged_args* a,
     return KVB_OK;
 }
 
-// One decode step on `stream` with workspace `ws` (zeroed once, sized by kvb_paged_workspace_bytes).
-int launch_paged(const kvb_paged_args* a, void* ws, cudaStream_t stream) {
+// One decode step on `stream` with workspace `ws` (zeroed once, sized by kvb_paged_workspace_bytes);
+// with `peers`, the outputs go to every rank's global buffer instead of a->out.
+int launch_paged(const kvb_paged_args* a, void* ws, cudaStream_t stream, const kvb_peer_out* peers = nullptr) {
     DeviceFacts f;
     if (int rc = device_facts(&f)) return rc;
     const Geometry g = geometry(a, f.num_sms);
@@ -250,6 +251,13 @@ int launch_paged(const kvb_paged_args* a, void* ws, cudaStream_t stream) {
     p.launch = next_launch_id();
     p.tables_ready = (a->flags & KVB_FLAG_TABLES_READY) != 0;
     p.inputs_ready = (a->flags & KVB_FLAG_INPUTS_READY) != 0;
+    p.n_peers = peers ? peers->n_peers : 0;
+    p.peer_self = peers ? peers->self : 0;
+    p.peer_rows = peers ? peers->rows : 0;
+    p.out_heads = peers ? peers->out_heads : s.num_heads;
+    p.out_head0 = peers ? peers->out_head0 : 0;
+    p.out_rows = peers ? peers->out_rows : nullptr;
+    for (int j = 0; j < KVB_MAX_PEERS; ++j) p.peer_out[j] = peers && j < peers->n_peers ? peers->peer_out[j] : nullptr;
 
     if (g.kernel < 0)
         return fail(KVB_ERR_INVALID, "the requested tensor-core kernel does not support this shape, page size or dtype");
@@ -512,6 +520,85 @@ int kvb_paged_decode_async(const kvb_paged_args* a, void* workspace, size_t work
     if (!workspace || workspace_bytes < need)
         return fail(KVB_ERR_INVALID, "workspace too small: need " + std::to_string(need) + " bytes");
     return launch_paged(a, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int kvb_paged_decode_gather_async(const kvb_paged_args* a, const kvb_peer_out* peers, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+    if (!a || !peers) return fail(KVB_ERR_INVALID, "null arguments");
+    if (peers->n_peers < 1 || peers->n_peers > KVB_MAX_PEERS)
+        return fail(KVB_ERR_INVALID, "n_peers must be in [1, KVB_MAX_PEERS]");
+    if (peers->rows < 1 || peers->out_head0 < 0 || peers->out_heads < peers->out_head0 + a->shape.num_heads)
+        return fail(KVB_ERR_INVALID, "peer rows must be > 0 and out_head0 + num_heads <= out_heads");
+    if ((long long)peers->rows * peers->out_heads * a->shape.head_dim > (1LL << 40))
+        return fail(KVB_ERR_INVALID, "peer output too large");
+    if (peers->self < 0 || peers->self >= peers->n_peers) return fail(KVB_ERR_INVALID, "self must be in [0, n_peers)");
+    for (int j = 0; j < peers->n_peers; ++j)
+        if (!peers->peer_out[j] || !aligned16(peers->peer_out[j]))
+            return fail(KVB_ERR_INVALID, "every peer output must be non-null and 16-byte aligned");
+    kvb_paged_args local = *a;  // the local output is not written; the checks want one
+    if (!local.out) local.out = peers->peer_out[0];
+    if (int rc = check_static(&local)) return rc;
+    size_t need = 0;
+    if (int rc = kvb_paged_workspace_bytes(&local, &need)) return rc;
+    if (!workspace || workspace_bytes < need)
+        return fail(KVB_ERR_INVALID, "workspace too small: need " + std::to_string(need) + " bytes");
+    return launch_paged(&local, workspace, static_cast<cudaStream_t>(stream), peers);
+}
+
+int kvb_peer_barrier_async(const kvb_peer_barrier_args* a, void* workspace, void* stream) {
+    if (!a || !workspace) return fail(KVB_ERR_INVALID, "null arguments");
+    if (a->n_peers < 1 || a->n_peers > KVB_MAX_PEERS || a->rank < 0 || a->rank >= a->n_peers)
+        return fail(KVB_ERR_INVALID, "n_peers must be in [1, KVB_MAX_PEERS] and 0 <= rank < n_peers");
+    if (!a->epoch) return fail(KVB_ERR_INVALID, "null epoch");
+    for (int j = 0; j < a->n_peers; ++j)
+        if (!a->signal[j]) return fail(KVB_ERR_INVALID, "null signal array");
+    PeerBarrierParams p;
+    p.n_peers = a->n_peers;
+    p.rank = a->rank;
+    p.timeout_ns = 1000ull * (a->timeout_us ? a->timeout_us : 1000000u);
+    p.epoch = a->epoch;
+    for (int j = 0; j < KVB_MAX_PEERS; ++j) p.signal[j] = j < a->n_peers ? a->signal[j] : nullptr;
+    const WorkspaceLayout w = kvb_workspace_layout(0, 0, 0, 0, 0);
+    p.error_flag = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + w.flag_off);
+    const cudaError_t e = kvb_launch_peer_barrier(p, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(KVB_ERR_DEVICE, std::string("peer barrier launch: ") + cudaGetErrorString(e));
+    return KVB_OK;
+}
+
+int kvb_ipc_alloc(size_t bytes, void** ptr, kvb_ipc_handle* handle) {
+    if (!ptr || !handle || bytes == 0) return fail(KVB_ERR_INVALID, "null pointer or zero size");
+    *ptr = nullptr;
+    void* d = nullptr;
+    if (cudaMalloc(&d, bytes) != cudaSuccess) return fail(KVB_ERR_DEVICE, "cudaMalloc failed");
+    cudaIpcMemHandle_t h;
+    if (cudaMemset(d, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, d) != cudaSuccess) {
+        cudaFree(d);
+        return fail(KVB_ERR_DEVICE, "cudaIpcGetMemHandle failed");
+    }
+    static_assert(sizeof(h) == sizeof(handle->bytes), "IPC handle size");
+    std::memcpy(handle->bytes, &h, sizeof(h));
+    *ptr = d;
+    return KVB_OK;
+}
+
+int kvb_ipc_free(void* ptr) {
+    if (ptr && cudaFree(ptr) != cudaSuccess) return fail(KVB_ERR_DEVICE, "cudaFree failed");
+    return KVB_OK;
+}
+
+int kvb_ipc_open(const kvb_ipc_handle* handle, void** ptr) {
+    if (!handle || !ptr) return fail(KVB_ERR_INVALID, "null arguments");
+    *ptr = nullptr;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle->bytes, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return fail(KVB_ERR_DEVICE, std::string("cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+    return KVB_OK;
+}
+
+int kvb_ipc_close(void* ptr) {
+    if (ptr && cudaIpcCloseMemHandle(ptr) != cudaSuccess) return fail(KVB_ERR_DEVICE, "cudaIpcCloseMemHandle failed");
+    return KVB_OK;
 }
 
 // ---- page write path -------------------------------------------------------------------------------

@@ -260,7 +260,7 @@ static_assert(sizeof(Unit) <= 64, "unit slot");
 template <int KVT, int QGP, bool MULTI>
 __global__ void __launch_bounds__(UM_THREADS, 1)
     decode_umma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                       const DecodeParams p) {
+                       const __grid_constant__ DecodeParams p) {
     using C = UCfg<KVT>;
     constexpr int NSUB = C::NSUB, STAGES = C::STAGES;
     constexpr int qgp = QGP;
@@ -787,7 +787,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                     break;
                 }
                 wait_prev();
-                store_tokenless_unit<UM_D>(p, u, lane, 32);
+                store_tokenless_unit<UM_D, MULTI>(p, u, lane, 32);
             }
             const int qb = n & 1;
             if (n >= 2) {
@@ -1206,21 +1206,36 @@ __global__ void __launch_bounds__(UM_THREADS, 1)
                 if (gt == 0) s_xcnt[qb] = 0;  // both groups counted: the slot's next unit counts from zero
                 const float nanv = __int_as_float(0x7fc00000);
                 const int d = my_lane;
+                // a single-partition unit's heads are consecutive rows of the output: local
+                // out[b][h0 + g], or (peers) this rank's global buffer at the unit's global row
+                // (the peer path only in the many-unit instance, which every gathered launch uses)
+                float* obase = nullptr;
+                if (u.nparts == 1) {
+                    size_t i = 0;
+                    if (!MULTI || p.n_peers == 0) obase = p.out + ((size_t)u.b * p.H + u.h0) * UM_D;
+                    else if (peer_index(p, u.b, u.h0, UM_D, &i)) obase = p.peer_out[p.peer_self] + i;
+                }
 #pragma unroll
                 for (int g = 0; g < QGP; ++g) {
                     if (g >= u.nh) break;
                     const int h = u.h0 + g;
                     const float val = any_bad ? nanv : o[g] / L[g];
                     if (u.nparts == 1) {
-                        p.out[((size_t)u.b * p.H + h) * UM_D + d] = val;
+                        if (obase) obase[g * UM_D + d] = val;
                     } else {
                         const size_t slot = ((size_t)u.b * p.H + h) * p.max_parts + u.part;
                         p.part_o[slot * UM_D + d] = val;
                         if (d == 0) p.part_ml[slot] = make_float2(m[g], any_bad ? nanv : L[g]);
                     }
                 }
+                if (MULTI && p.n_peers > 0 && obase) {
+                    // the elements this thread stored, to the other ranks
+                    const size_t i = obase - p.peer_out[p.peer_self];
+#pragma unroll 1
+                    for (int g = 0; g < u.nh; ++g) copy_to_peers<float>(p, i + g * UM_D + d);
+                }
                 // count the partition in; the last partition's CTA merges them all
-                finish_partition<UM_D, 12, (QGP >= 2 ? 1 : 32)>(p, u, gt, UM_SOFT, gbar, &s_xcnt[2 + gi]);
+                finish_partition<UM_D, 12, (QGP >= 2 ? 1 : 32), MULTI>(p, u, gt, UM_SOFT, gbar, &s_xcnt[2 + gi]);
             }
             // this warp is done with the unit's slot (its factors, both shares)
             tc_fence_before();
@@ -1259,8 +1274,9 @@ cudaError_t launch_one(const DecodeParams& p, const CUtensorMap& tk, const CUten
     const long long upper = (long long)p.B * p.nhg * p.max_parts;
     const long long grid = std::min<long long>(upper, (long long)li.num_sms);
     if (grid <= 0) return cudaSuccess;
-    return upper > grid ? launch_grid<KVT, QGP, true>(p, tk, tv, li, grid)
-                        : launch_grid<KVT, QGP, false>(p, tk, tv, li, grid);
+    // the single-unit instance has no peer path: a gathered launch takes the many-unit one
+    return upper > grid || p.n_peers > 0 ? launch_grid<KVT, QGP, true>(p, tk, tv, li, grid)
+                                         : launch_grid<KVT, QGP, false>(p, tk, tv, li, grid);
 }
 
 template <int KVT>

@@ -244,6 +244,55 @@ __device__ __forceinline__ int div_small_quotient(int n, int d, int* rem) {
     return q;
 }
 
+// Output stores. Without peers: out[b][h][d]. With peers (a sharded step gathered in the kernel):
+// the element's global position, in this rank's own global buffer (peer_out[peer_self]) and, by
+// the same thread, in every other rank's over peer memory; a global row outside [0, peer_rows) is
+// refused (error bit KVB_DEVERR_BLOCK, nothing stored).
+__device__ __forceinline__ bool peer_index(const DecodeParams& p, int b, int h, int D, size_t* i) {
+    const int row = p.out_rows ? __ldg(p.out_rows + b) : b;
+    if (row < 0 || row >= p.peer_rows) {
+        raise_error(p.error_flag, KVB_DEVERR_BLOCK);
+        return false;
+    }
+    *i = ((size_t)row * p.out_heads + p.out_head0 + h) * D;
+    return true;
+}
+
+// The element at offset i of this rank's own global buffer, stored by this thread, copied to the
+// other ranks' buffers.
+template <typename T>
+__device__ __forceinline__ void copy_to_peers(const DecodeParams& p, size_t i) {
+    const T v = *reinterpret_cast<const T*>(p.peer_out[p.peer_self] + i);
+#pragma unroll 1
+    for (int j = 0; j < p.n_peers; ++j)
+        if (j != p.peer_self) *reinterpret_cast<T*>(p.peer_out[j] + i) = v;
+}
+
+// PEERS false compiles the peer path out (an instance that never serves a gathered launch).
+template <int D, bool PEERS = true>
+__device__ __forceinline__ void store_out(const DecodeParams& p, int b, int h, int d, float v) {
+    if (!PEERS || p.n_peers == 0) {
+        p.out[((size_t)b * p.H + h) * D + d] = v;
+        return;
+    }
+    size_t i;
+    if (!peer_index(p, b, h, D, &i)) return;
+    p.peer_out[p.peer_self][i + d] = v;
+    copy_to_peers<float>(p, i + d);
+}
+
+template <int D, bool PEERS = true>
+__device__ __forceinline__ void store_out4(const DecodeParams& p, int b, int h, int d4, float4 v) {
+    if (!PEERS || p.n_peers == 0) {
+        reinterpret_cast<float4*>(p.out + ((size_t)b * p.H + h) * D)[d4] = v;
+        return;
+    }
+    size_t i;
+    if (!peer_index(p, b, h, D, &i)) return;
+    reinterpret_cast<float4*>(p.peer_out[p.peer_self] + i)[d4] = v;
+    copy_to_peers<float4>(p, i + 4 * d4);
+}
+
 // One work unit is one split-K partition [t0, t1) of one sequence b for one group of query heads
 // that share a KV head. Units are numbered sequence-major, then head group, then partition.
 struct Unit {
@@ -443,7 +492,7 @@ __device__ __forceinline__ void merge_slots_and_store(const DecodeParams& p, con
         o *= o_scale;
         const int h = u.h0 + g0 + g;
         if (u.nparts == 1) {
-            p.out[((size_t)u.b * p.H + h) * D + d] = o / L;
+            store_out<D>(p, u.b, h, d, o / L);
         } else {
             const size_t slot = ((size_t)u.b * p.H + h) * p.max_parts + u.part;
             p.part_o[slot * D + d] = o / L;
@@ -510,24 +559,24 @@ __device__ __forceinline__ bool resolve_arrival(const DecodeParams& p, const Uni
     return last;
 }
 
-template <int D, int BATCH = 8, int MAXSPLIT = 32>
+template <int D, int BATCH = 8, int MAXSPLIT = 32, bool PEERS = true>
 __device__ __forceinline__ void merge_partitions(const DecodeParams& p, const Unit& u, int tid, int nthreads);
 
 // MAXSPLIT bounds the lanes that share a (head, 4-dim slice) pair: a caller whose heads always fill
 // half of its threads passes 1, and the lane combine is compiled out.
-template <int D, int BATCH = 8, int MAXSPLIT = 32>
+template <int D, int BATCH = 8, int MAXSPLIT = 32, bool PEERS = true>
 __device__ __forceinline__ void finish_partition(const DecodeParams& p, const Unit& u, int tid, int nthreads,
                                                  uint32_t bar_id, int* s_flag) {
     if (u.nparts <= 1) return;
     named_barrier(bar_id, nthreads);  // every thread's partial stores come before the arrival below
     if (tid == 0) *s_flag = resolve_arrival(p, u, arrive_partition(p, u));
     named_barrier(bar_id, nthreads);
-    if (*s_flag) merge_partitions<D, BATCH, MAXSPLIT>(p, u, tid, nthreads);
+    if (*s_flag) merge_partitions<D, BATCH, MAXSPLIT, PEERS>(p, u, tid, nthreads);
 }
 
 // The merge of all partitions of u into `out` (the CTA of the last partition, every other
 // partition's stores visible through the acquiring arrival).
-template <int D, int BATCH, int MAXSPLIT>
+template <int D, int BATCH, int MAXSPLIT, bool PEERS>
 __device__ __forceinline__ void merge_partitions(const DecodeParams& p, const Unit& u, int tid, int nthreads) {
     constexpr int D4 = D / 4;
     const int np = u.nparts, nh = u.nh;
@@ -588,20 +637,18 @@ __device__ __forceinline__ void merge_partitions(const DecodeParams& p, const Un
         }
         if (active && s == 0) {
             const float inv = 1.f / S;
-            reinterpret_cast<float4*>(p.out + ((size_t)u.b * p.H + h) * D)[d4] =
-                make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv);
+            store_out4<D, PEERS>(p, u.b, h, d4, make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv));
         }
     }
 }
 
 // Units with no tokens: an empty sequence attends to nothing and gives exactly 0; a sequence whose
 // length was refused gives NaN and raises the error flag.
-template <int D>
+template <int D, bool PEERS = true>
 __device__ __forceinline__ void store_tokenless_unit(const DecodeParams& p, const Unit& u, int tid, int nthreads) {
     if (u.bad && tid == 0) raise_error(p.error_flag, KVB_DEVERR_LENGTH);
     const float val = u.bad ? __int_as_float(0x7fc00000) : 0.0f;
-    for (int idx = tid; idx < u.nh * D; idx += nthreads)
-        p.out[((size_t)u.b * p.H + u.h0 + idx / D) * D + idx % D] = val;
+    for (int idx = tid; idx < u.nh * D; idx += nthreads) store_out<D, PEERS>(p, u.b, u.h0 + idx / D, idx % D, val);
 }
 
 }  // namespace kvb_dev

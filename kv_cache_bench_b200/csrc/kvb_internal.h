@@ -10,6 +10,8 @@
 
 #include <cuda_runtime.h>
 
+#include "kvb_cuda.h"
+
 // A value set up once per device: kernel attributes (cudaFuncSetAttribute), occupancy and symbol
 // addresses belong to a device's context, so a process that launches on several devices needs each
 // of them once per device. get() runs `init(T*)` the first time it is called with a device current
@@ -113,7 +115,24 @@ struct DecodeParams {
     int inputs_ready;  // KVB_FLAG_INPUTS_READY (with tables_ready): q, pools and scales may be read before it too
     // the launch's invariant divisors: part_tokens, gpk, max_parts, nhg * max_parts
     KvbDiv div_part, div_gpk, div_parts, div_seq;
+    // A sharded step gathered in the kernel (n_peers > 0): output element (b, h, d) goes to
+    // peer_out[0..n_peers) at ((out_rows ? out_rows[b] : b) * out_heads + out_head0 + h) * D + d,
+    // peer_out[peer_self] being this rank's own buffer, and out is not written. n_peers == 0:
+    // out[b][h][d].
+    int n_peers, peer_self, peer_rows, out_heads, out_head0;
+    const int* out_rows;
+    float* peer_out[KVB_MAX_PEERS];
 };
+
+// The step barrier of a sharded step gathered in the kernel (kvb_peer.cu).
+struct PeerBarrierParams {
+    int n_peers, rank;
+    unsigned long long timeout_ns;
+    unsigned* epoch;
+    unsigned* signal[KVB_MAX_PEERS];
+    unsigned* error_flag;
+};
+cudaError_t kvb_launch_peer_barrier(const PeerBarrierParams& p, cudaStream_t stream);
 
 // The page write path (kvb_pages.cu): a contiguous cache into the paged pool.
 struct PageWriteParams {

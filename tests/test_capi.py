@@ -119,7 +119,9 @@ def _c_layout(struct, fields):
 
 
 @pytest.mark.parametrize("struct,cls", [("kvb_shape", "_CShape"), ("kvb_paged_args", "_CPagedArgs"),
-                                        ("kvb_naive_args", "_CNaiveArgs"), ("kvb_page_write_args", "_CPageWriteArgs")])
+                                        ("kvb_naive_args", "_CNaiveArgs"), ("kvb_page_write_args", "_CPageWriteArgs"),
+                                        ("kvb_ipc_handle", "_CIpcHandle"), ("kvb_peer_out", "_CPeerOut"),
+                                        ("kvb_peer_barrier_args", "_CPeerBarrierArgs")])
 def test_python_structs_match_the_header_layout(struct, cls):
     # the ctypes mirrors must agree with the C header field for field: a field added on one side only
     # would shift every later one

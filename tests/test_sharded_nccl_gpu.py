@@ -1,9 +1,11 @@
-"""Sharded decode on two GPUs over NCCL, through bench.py's own measured path: each rank builds its
-shard of the step (kv_cache_bench_b200.workload.DeviceStep: sequences by LPT bin packing, or KV
-heads), replays CUDA graphs that hold the decode kernel, the NCCL all-gather and the reorder into
-global order, and rank 0 saves the gathered output. Every sequence of it is then compared with the
-fp64 oracle on the unsharded data (the values are keyed by sequence and head, so the shards are
-slices of the one-GPU step). Needs two GPUs; skipped on one."""
+"""Sharded decode on two GPUs, through bench.py's own measured path: each rank builds its shard of
+the step (kv_cache_bench_b200.workload.DeviceStep: sequences by LPT bin packing, or KV heads) and
+replays CUDA graphs that hold the step, with either gather: the decode kernel writing every output
+row into both ranks' global buffers over peer memory plus the step barrier (the default), or the
+NCCL all-gather and the reorder into global order. Rank 0 saves both gathered outputs. Every
+sequence is then compared with the fp64 oracle on the unsharded data (the values are keyed by
+sequence and head, so the shards are slices of the one-GPU step), and the two gathers must agree
+bit for bit. Needs two GPUs; skipped on one."""
 import datetime
 import os
 import socket
@@ -42,15 +44,18 @@ def _worker(rank, world, port, out_dir):
                             device_id=device)
     try:
         ctx = bench.Ctx(torch, dist, rank, world, device)
-        args = bench.parse_args(["--gpus", str(world), "--steps", "3", "--warmup", "3"])
-        for cfg, dtype, nseq in CASES:
-            m = bench.measure(ctx, _reduced(cfg, dtype, nseq), args, part=0, kernel=kvb.Kernel.auto, copies=1)
-            assert m["flag"] == 0
-            final = m["gather"].final.cpu().numpy()
-            if rank == 0:
-                np.save(os.path.join(out_dir, f"{cfg}_{dtype}.npy"), final)
-            del m
-            torch.cuda.empty_cache()
+        for how in ("nccl", "kernel"):
+            args = bench.parse_args(["--gpus", str(world), "--steps", "3", "--warmup", "3", "--gather", how])
+            for cfg, dtype, nseq in CASES:
+                m = bench.measure(ctx, _reduced(cfg, dtype, nseq), args, part=0, kernel=kvb.Kernel.auto, copies=1)
+                assert m["flag"] == 0
+                assert m["gather"].fused == (how == "kernel")
+                final = m["gather"].final.cpu().numpy()
+                if rank == 0:
+                    np.save(os.path.join(out_dir, f"{cfg}_{dtype}_{how}.npy"), final)
+                m["gather"].close()
+                del m
+                torch.cuda.empty_cache()
     finally:
         dist.barrier()
         dist.destroy_process_group()
@@ -68,7 +73,8 @@ def test_two_gpu_sharded_steps_match_the_unsharded_oracle(tmp_path):
     mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
     kvt = {"f16": oracle.F16, "i8": oracle.I8}
     for cfg, dtype, nseq in CASES:
-        final = np.load(tmp_path / f"{cfg}_{dtype}.npy")
+        final = np.load(tmp_path / f"{cfg}_{dtype}_kernel.npy")
+        assert np.array_equal(final, np.load(tmp_path / f"{cfg}_{dtype}_nccl.npy"), equal_nan=True)
         s = DeviceStep(torch, _reduced(cfg, dtype, nseq), device=torch.device("cuda", 0))  # the unsharded step
         assert final.shape == tuple(s.q.shape)
         for i in range(len(s.lens)):
