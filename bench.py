@@ -563,9 +563,14 @@ def decoder_for(ctx, s, part, kernel, step_stream):
     dec = PagedDecoder(ctx.device)
     # nothing in the step loop writes the lengths, the block table, q, the pools or the scales: the
     # kernel may read them while the previous step finishes; the steps are a back-to-back stream
-    cargs = [dec.args(s.q, k, v, s.table, s.seq_lens, s.max_len, out=s.out, k_scale=ks, v_scale=vs,
-                      part_tokens=part, kernel=kernel, tables_ready=True, inputs_ready=True, step_stream=step_stream)
-             for (k, v, ks, vs) in s.pools]
+    def make(p):
+        return [dec.args(s.q, k, v, s.table, s.seq_lens, s.max_len, out=s.out, k_scale=ks, v_scale=vs,
+                         part_tokens=p, kernel=kernel, tables_ready=True, inputs_ready=True, step_stream=step_stream)
+                for (k, v, ks, vs) in s.pools]
+    cargs = make(part)
+    if part == 0 and s.lens:
+        # the partition from this step's lengths, which the host knows (kvb_paged_part_tokens_for)
+        cargs = make(kvb.paged_part_tokens_for(cargs[0], s.lens))
     need = max(kvb.paged_workspace_bytes(c) for c in cargs) if s.lens else 256
     dec.workspace = ctx.torch.zeros(max(need, 256), dtype=ctx.torch.uint8, device=ctx.device)
     return dec, cargs

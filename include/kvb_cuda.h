@@ -186,6 +186,14 @@ int kvb_paged_part_tokens(const kvb_paged_args* args);
  * be zero-filled once before its first use (cudaMemset); every call leaves it ready for the next. */
 int kvb_paged_workspace_bytes(const kvb_paged_args* args, size_t* bytes);
 
+/* The split-K partition size for `args` given the sequence lengths on the host (host_lens[batch]),
+ * to pass as args->part_tokens (same return convention as kvb_paged_part_tokens). It is the
+ * automatic size, except on the tcgen05 kernel when that size gives more work units than CTAs but
+ * fewer than five per CTA: then partitions shrink toward about five units per CTA (at least 1024
+ * tokens), so that a ragged batch's last units end close together. No counterpart in the reference, whose partition follows
+ * max_len alone (src/metal_attn.hpp:47-51). Reads nothing on the device. */
+int kvb_paged_part_tokens_for(const kvb_paged_args* args, const int32_t* host_lens);
+
 /* src/metal_attn.hpp:86 run_paged() as one stream-ordered launch: all pointers are device
  * pointers, `stream` is a cudaStream_t (NULL = legacy default stream). Nothing is read on the
  * host, so lengths cannot be refused up front: a length outside [0, min(max_len,

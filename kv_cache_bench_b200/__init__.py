@@ -31,7 +31,7 @@ __all__ = [
     "Shape", "KvType", "name", "elem_size", "kSimdGroups", "auto_part_tokens", "Buffer", "PagedArgs",
     "NaiveArgs", "metal_available", "device_name", "run_paged", "run_paged_steps", "run_naive",
     "begin_pipelined", "end_pipelined", "run_read_bandwidth", "flush_gpu_caches", "Kernel",
-    "paged_workspace_bytes", "paged_part_tokens", "paged_decode_async", "paged_error_flag",
+    "paged_workspace_bytes", "paged_part_tokens", "paged_part_tokens_for", "paged_decode_async", "paged_error_flag",
     "paged_decode_static", "paged_static_error_flag", "library_path", "lib", "MAX_PEERS", "ipc_alloc", "ipc_free",
     "ipc_open", "ipc_close", "peer_out", "paged_decode_gather_async", "peer_barrier_args", "peer_barrier_async",
 ]
@@ -122,6 +122,8 @@ _c_flush = _sig("kvb_flush_caches", ctypes.c_int)
 _c_auto_part = _sig("kvb_auto_part_tokens", ctypes.c_int, _CShape, ctypes.c_int)
 _c_last_error = _sig("kvb_last_error", ctypes.c_char_p)
 _c_part_tokens = _sig("kvb_paged_part_tokens", ctypes.c_int, ctypes.POINTER(_CPagedArgs))
+_c_part_tokens_for = _sig("kvb_paged_part_tokens_for", ctypes.c_int, ctypes.POINTER(_CPagedArgs),
+                          ctypes.POINTER(ctypes.c_int32))
 _c_ws_bytes = _sig("kvb_paged_workspace_bytes", ctypes.c_int, ctypes.POINTER(_CPagedArgs),
                    ctypes.POINTER(ctypes.c_size_t))
 _c_decode_async = _sig("kvb_paged_decode_async", ctypes.c_int, ctypes.POINTER(_CPagedArgs), ctypes.c_void_p,
@@ -367,6 +369,15 @@ def paged_part_tokens(c: _CPagedArgs) -> int:
     r = _c_part_tokens(ctypes.byref(c))
     if r < 0:
         _check(-r, "paged_part_tokens")
+    return r
+
+
+def paged_part_tokens_for(c: _CPagedArgs, lens) -> int:
+    """kvb_paged_part_tokens_for: the partition size for these host-side sequence lengths."""
+    arr = (ctypes.c_int32 * max(1, len(lens)))(*[int(x) for x in lens])
+    r = _c_part_tokens_for(ctypes.byref(c), arr)
+    if r < 0:
+        _check(-r, "paged_part_tokens_for")
     return r
 
 

@@ -503,6 +503,33 @@ int kvb_paged_part_tokens(const kvb_paged_args* a) {
     return geometry(a, f.num_sms).part;
 }
 
+int kvb_paged_part_tokens_for(const kvb_paged_args* a, const int32_t* host_lens) {
+    if (int rc = check_static(a)) return -rc;
+    if (!host_lens && a->shape.batch > 0) return -fail(KVB_ERR_INVALID, "null host_lens");
+    DeviceFacts f;
+    if (int rc = device_facts(&f)) return -rc;
+    const Geometry g = geometry(a, f.num_sms);
+    if (a->part_tokens > 0 || g.kernel != KVB_KERNEL_UMMA) return g.part;
+    // Units of the automatic partition; a launch with no more units than CTAs keeps it.
+    const long long chunk = 128, slots = std::max(1, f.num_sms);
+    long long units = 0, tokens = 0;
+    for (int b = 0; b < a->shape.batch; ++b) {
+        const long long len = std::min<long long>(std::max(0, host_lens[b]), a->max_len);
+        units += (long long)g.nhg * std::max<long long>(1, (len + g.part - 1) / g.part);
+        tokens += len * g.nhg;
+    }
+    // One wave keeps it, and so do five or more units per CTA.
+    if (units <= slots || units >= 5 * slots) return g.part;
+    // A few units per CTA, handed out dynamically: partitions small enough for about five units per
+    // CTA, so that the last ones handed out end close together (a CTA with one 30-chunk unit too
+    // many ends 20-40 us late), and not below 1024 tokens, since every unit costs its CTA about
+    // 2 us of start and merge work. Config 4's first 8 sequences on one B200: 88.9 us per step with
+    // the automatic 3712 tokens, 72.5 us with 1024; its first 16: 139.6 us with 3840, 140.3 with 2048.
+    const long long want = (tokens + 5 * slots - 1) / (5 * slots);
+    const long long part = std::max<long long>(1024, (want + chunk - 1) / chunk * chunk);
+    return (int)std::min<long long>(part, g.part);
+}
+
 int kvb_paged_workspace_bytes(const kvb_paged_args* a, size_t* bytes) {
     if (!bytes) return fail(KVB_ERR_INVALID, "null bytes");
     if (int rc = check_static(a)) return rc;

@@ -262,3 +262,30 @@ def test_inputs_and_output_in_pinned_host_memory(kv_type, lens, kernel, flags):
     stream.synchronize()
     assert torch.equal(hout, base.cpu())
     assert dec.error_flag() == 0
+
+
+def test_partition_from_host_lengths():
+    """kvb_paged_part_tokens_for: a ragged batch with a few units per CTA gets smaller partitions
+    than the automatic size (at least 1024 tokens), one wave keeps the automatic size, and the
+    decode with the chosen size gives the oracle's result."""
+    lens = [9000, 30000, 700, 4100, 15000, 2000, 25000, 600]
+    case = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=lens, kv_type=oracle.F16, page=16,
+                            seed=31)
+    d = _dev(case)
+    dec = PagedDecoder()
+    auto = dec.part_tokens(d["q"], d["k"], d["v"], d["table"], d["lens"], case.max_len, inputs_ready=True)
+    out = torch.empty_like(d["q"])
+    c = dec.args(d["q"], d["k"], d["v"], d["table"], d["lens"], case.max_len, out=out, inputs_ready=True)
+    part = kvb.paged_part_tokens_for(c, lens)
+    assert 1024 <= part < auto and part % 128 == 0
+    got = _call(dec, d, case.max_len, part_tokens=part, inputs_ready=True)
+    torch.cuda.synchronize()
+    assert oracle.max_abs_diff(got.cpu().numpy(), case.reference()) <= TOL
+    assert dec.error_flag() == 0
+    one = oracle.make_case(num_heads=32, num_kv_heads=8, head_dim=128, lens=[32768], kv_type=oracle.I8, page=128,
+                           seed=31)
+    d1 = _dev(one)
+    o1 = torch.empty_like(d1["q"])
+    c1 = dec.args(d1["q"], d1["k"], d1["v"], d1["table"], d1["lens"], one.max_len, out=o1, k_scale=d1["ks"],
+                  v_scale=d1["vs"], inputs_ready=True)
+    assert kvb.paged_part_tokens_for(c1, [32768]) == kvb.paged_part_tokens(c1) == 1920
