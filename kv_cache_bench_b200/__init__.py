@@ -374,6 +374,8 @@ def paged_part_tokens(c: _CPagedArgs) -> int:
 
 def paged_part_tokens_for(c: _CPagedArgs, lens) -> int:
     """kvb_paged_part_tokens_for: the partition size for these host-side sequence lengths."""
+    if len(lens) < c.shape.batch:
+        raise ValueError(f"paged_part_tokens_for: {len(lens)} lengths for a batch of {c.shape.batch}")
     arr = (ctypes.c_int32 * max(1, len(lens)))(*[int(x) for x in lens])
     r = _c_part_tokens_for(ctypes.byref(c), arr)
     if r < 0:

@@ -130,3 +130,18 @@ def test_python_structs_match_the_header_layout(struct, cls):
     got = _c_layout(struct, names)
     assert got[0] == ctypes.sizeof(c), (struct, got[0], ctypes.sizeof(c))
     assert got[1:] == [getattr(c, n).offset for n in names], struct
+
+
+def test_partition_helper_and_gather_refuse_before_any_device_work():
+    # arguments are checked before the device is touched: these refusals need no GPU
+    c = kvb.device_args(kvb.Shape(2, 32, 8, 128), kvb.KvType.f16, 16, 64, 1024, q=16, k=16, v=16, block_table=16,
+                        seq_lens=16, out=16, num_blocks=4)
+    with pytest.raises(ValueError):
+        kvb.paged_part_tokens_for(c, [])  # no lengths for a batch of two
+    with pytest.raises(ValueError):
+        kvb.peer_out([], 0, 1, 1)
+    bad = kvb.peer_out([16], 1, 2, 32)  # self outside the peer list
+    with pytest.raises(ValueError):
+        kvb.paged_decode_gather_async(c, bad, 16, 1 << 20, 0)
+    with pytest.raises(ValueError):
+        kvb.peer_barrier_async(kvb.peer_barrier_args(0, [16], 0), 16, 0)  # no epoch word
