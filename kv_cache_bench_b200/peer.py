@@ -65,9 +65,15 @@ class PeerGather:
         rows_ptr = out_rows.data_ptr() if out_rows is not None else 0
         self.args = [kvb.peer_out(self.buffers[b], rank, rows, heads, out_head0, rows_ptr) for b in range(nbuf)]
         self.barrier = kvb.peer_barrier_args(rank, self.signals, self.epoch.data_ptr(), timeout_us)
-        self.views = [torch.as_tensor(_DeviceArray(mine[b], (rows, heads, head_dim)), device=device)
-                      for b in range(nbuf)]
+        self._mine, self._shape, self._device, self._views = mine, (rows, heads, head_dim), device, None
         dist.barrier()
+
+    @property
+    def views(self):
+        """This rank's global output buffers as torch tensors (no copy, not owned)."""
+        if self._views is None:
+            self._views = [self.torch.as_tensor(_DeviceArray(p, self._shape), device=self._device) for p in self._mine]
+        return self._views
 
     def _open(self, handle: bytes) -> int:
         p = kvb.ipc_open(handle)
@@ -92,7 +98,7 @@ class PeerGather:
             kvb.ipc_close(p)
         self._opened = []
         self.dist.barrier()
-        self.views = []
+        self._views, self._mine = None, []
         for p in self._own:
             kvb.ipc_free(p)
         self._own = []
