@@ -598,7 +598,10 @@ int kvb_ipc_alloc(size_t bytes, void** ptr, kvb_ipc_handle* handle) {
     void* d = nullptr;
     if (cudaMalloc(&d, bytes) != cudaSuccess) return fail(KVB_ERR_DEVICE, "cudaMalloc failed");
     cudaIpcMemHandle_t h;
-    if (cudaMemset(d, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, d) != cudaSuccess) {
+    // zeroed before the handle leaves: a peer may store into the memory as soon as it has mapped it,
+    // and a memset still in flight would wipe that store
+    if (cudaMemset(d, 0, bytes) != cudaSuccess || cudaStreamSynchronize(0) != cudaSuccess ||
+        cudaIpcGetMemHandle(&h, d) != cudaSuccess) {
         cudaFree(d);
         return fail(KVB_ERR_DEVICE, "cudaIpcGetMemHandle failed");
     }

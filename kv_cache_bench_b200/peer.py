@@ -66,6 +66,7 @@ class PeerGather:
         self.args = [kvb.peer_out(self.buffers[b], rank, rows, heads, out_head0, rows_ptr) for b in range(nbuf)]
         self.barrier = kvb.peer_barrier_args(rank, self.signals, self.epoch.data_ptr(), timeout_us)
         self._mine, self._shape, self._device, self._views = mine, (rows, heads, head_dim), device, None
+        torch.cuda.synchronize()  # the epoch word is zero before any barrier kernel reads it
         dist.barrier()
 
     @property
