@@ -727,10 +727,28 @@ def measure(ctx, w, args, *, part, kernel, copies, with_clocks=None, max_seconds
             gather.launch(cargs[0], ws_ptr, ws_n, stream.cuda_stream, 0)
         ctx.barrier()
         flag = max(flag, dec.error_flag(stream) if s.lens else 0)
+    decode_ms = None
+    if gather.mode is not None:
+        # each rank's decode alone (its share of the step, no gather), timed the same way; every rank
+        # takes the same barriers and reductions, with or without sequences of its own
+        def plain(i):
+            kvb.paged_decode_async(cargs[i % copies], ws_ptr, ws_n, stream.cuda_stream)
+        n2 = max(5, min(steps, 200))
+        alone = make_runner(torch, stream, plain, per_graph) if s.lens else None
+        if alone:
+            alone.prepare(n2)
+        ctx.barrier()
+        if alone:
+            k0, k1 = timed_run(torch, stream, alone, n2)
+        ctx.barrier()
+        mine = k0.elapsed_time(k1) / n2 if alone else 0.0
+        if alone:
+            alone.release()
+        decode_ms = (ctx.reduce(mine), -ctx.reduce(-mine))
     ms_step = ms_total / max(steps, 1)
     job_bytes = ctx.reduce(s.bytes, "sum")
     return dict(s=s, dec=dec, gather=gather, stream=stream, ms_step=ms_step, steps=steps, job_bytes=job_bytes,
-                steady_ms_step=steady,
+                steady_ms_step=steady, decode_ms=decode_ms,
                 flag=int(ctx.reduce(flag)), part=kvb.paged_part_tokens(cargs[0]) if s.lens else part,
                 copies=copies)
 
@@ -885,6 +903,10 @@ def main():
                  "frac_of_n_peak": round(ms_["job_bytes"] / (ms_["ms_step"] * 1e-3) / 1e9 / (world * peak), 4),
                  "part_tokens": ms_["part"], "error_flag": ms_["flag"],
                  "step": ms_["gather"].describe()}
+        if ms_["decode_ms"]:
+            entry["decode_us_per_rank"] = {"max": round(ms_["decode_ms"][0] * 1e3, 3),
+                                           "min": round(ms_["decode_ms"][1] * 1e3, 3),
+                                           "note": "each rank's decode alone, without the gather, back to back"}
         if not args.no_parity:
             entry["parity"] = sharded_parity(ctx, ms_, threads)
         sharded[f"config{cfg}_{ws['kv']}"] = entry
