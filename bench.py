@@ -1143,8 +1143,8 @@ def measure_e2e_mapped(torch, dist, s, dec, part, kernel, args, world, barrier, 
 def measure_e2e(torch, dist, s, dec, part, kernel, stream, args, world, barrier, job_bytes, w, gather):
     """The same metric through the public C ABI with host buffers: per step, one host->device copy
     of the step's inputs (q, sequence lengths, block table, packed in one pinned staging buffer),
-    kvb_paged_decode_async reading them where they landed, the output all-gather when sharded, and
-    the device->host copy of the (global) output. The KV pool is device-resident state (written when a
+    kvb_paged_decode_async reading them where they landed (the in-kernel gather and the step barrier,
+    or the NCCL all-gather, when sharded), and the device->host copy of the (global) output. The KV pool is device-resident state (written when a
     page is written), rotated over the same copies as the device timing.
 
     Unsharded steps that move more than 1 MiB of inputs and outputs are pipelined as a serving loop
@@ -1153,7 +1153,7 @@ def measure_e2e(torch, dist, s, dec, part, kernel, stream, args, world, barrier,
     last reader). Every step still copies its inputs in and its output out inside the timed region.
     Smaller steps (configs 1-3) run on one stream: there the cross-stream event handoffs cost more
     than the copies they would hide (config 3: 49 us pipelined against 39 us). Sharded runs keep one
-    stream too (the all-gather sits between kernel and readback)."""
+    stream too (the gather sits between kernel and readback)."""
     import kv_cache_bench_b200 as kvb
 
     def align(n):
