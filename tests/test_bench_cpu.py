@@ -122,3 +122,19 @@ def test_parity_picks_shortest_and_longest():
     assert bench.parity_picks([]) == []
     assert bench.parity_picks([7]) == [0]
     assert bench.parity_picks([5, 9, 1, 9]) == [1, 2]
+
+
+def test_gather_defaults_to_the_kernel_and_is_idle_on_one_rank():
+    import types
+    import torch
+    assert bench.parse_args([]).gather == "kernel"
+    assert bench.parse_args(["--gather", "nccl"]).gather == "nccl"
+    with pytest.raises(SystemExit):
+        bench.parse_args(["--gather", "allreduce"])
+    ctx = types.SimpleNamespace(torch=torch, dist=None, rank=0, world=1, device=torch.device("cpu"))
+    s = types.SimpleNamespace(out=torch.zeros(1, 4, 8), kv_heads=[0, 1], seqs=[0], lens=[5], H=4)
+    for cfg in (3, 4, 5):
+        g = bench.Gather(ctx, s, bench.workload(cfg, None))
+        assert g.mode is None and not g.fused and g.peer is None and g.final is s.out
+        assert g.describe() == "decode kernel" and g() is s.out
+        g.close()
