@@ -195,7 +195,9 @@ int kvb_paged_workspace_bytes(const kvb_paged_args* args, size_t* bytes);
 int kvb_paged_part_tokens_for(const kvb_paged_args* args, const int32_t* host_lens);
 
 /* src/metal_attn.hpp:86 run_paged() as one stream-ordered launch: all pointers are device
- * pointers, `stream` is a cudaStream_t (NULL = legacy default stream). Nothing is read on the
+ * pointers (q, seq_lens, block_table and out may also point at page-locked host memory, which the
+ * kernels then read and write across the host link: the step's inputs need no staging copy), `stream`
+ * is a cudaStream_t (NULL = legacy default stream). Nothing is read on the
  * host, so lengths cannot be refused up front: a length outside [0, min(max_len,
  * max_blocks * page_size)] or a live block id outside [0, num_blocks) makes the kernel write NaN
  * to that sequence's outputs and set a flag that kvb_paged_error_flag() reads; no access leaves
